@@ -1,0 +1,499 @@
+"""Benchmark: causal queries/s of the streaming Taylor-moment + block-coreset
+attention forward on B200, one process per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 3] [--impl ours|reference]
+
+For N > 1 launch under torchrun (one rank per GPU, NCCL); the B*H sequences
+of the configuration are split into N contiguous shards with no
+communication (every sequence is independent).  Rank 0 prints one JSON line.
+
+A step is one forward of the rank's shard.  ``value`` is timed with the
+inputs resident in HBM; ``e2e`` times the public entry point from pinned host
+buffers with the host->device copies of q, k, v and the device->host copy of
+the output inside the timed region.  Inputs (>= 1.5 GB for the default
+configuration) are larger than the 126 MB L2, so no flush is needed between
+steps.
+
+``--impl reference`` times the CPU restatement of the reference algorithm
+(oracle/oracle.py in float32 numpy; the reference itself is a Python/torch
+package that is not present on the GPU host) on bounded samples of the same
+workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "causal queries/sec (B·H·N/s)"
+UNIT = "queries/s"
+CLOCK_FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", type=int, default=3, choices=[1, 2, 3, 4, 5])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-heads", type=int, default=0, help="heads in the CPU sample (0 = auto)")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+def workload_name(c: dict, cfg_id: int) -> str:
+    return (f"config{cfg_id}: B={c['B']} H={c['H']} N={c['N']} d={c['d']} dv={c['dv']} degree={c['degree']} "
+            f"block_size={c['block_size']} compressor={c['compressor']} data={c['data']}")
+
+
+def pair_count(n: int, bs: int, m_blk: int) -> int:
+    """(query, rep-or-key) pairs the residual kernel evaluates for one sequence."""
+    i = np.arange(n, dtype=np.int64)
+    c = i // bs
+    return int((c * m_blk + (i - c * bs + 1)).sum())
+
+
+def algorithmic_work(c: dict) -> dict:
+    """Per-sequence algorithmic flops / bytes of each kernel."""
+    n, d, dv, bs = c["N"], c["d"], c["dv"], c["block_size"]
+    t = c["degree"]
+    F = sum(1 if l == 0 else math.comb(d + l - 1, l) for l in range(t + 1))
+    nc = (n - 1) // bs
+    m_blk = bs if c["compressor"] == "none" else (bs + 1) // 2
+    pairs = pair_count(n, bs, m_blk)
+    R = 0 if c["compressor"] == "none" else nc * m_blk
+    return {
+        "residual_flops": pairs * (2 * d + 2 * dv + 2),
+        "moment_flops": 2 * F * (dv + 1) * n + 2 * F * (dv + 1) * nc * bs,
+        "compress_bytes": (nc * bs * d * 4 + R * (d + dv) * 4 + R * (d + dv + 2) * 4
+                           + nc * (d + bs // 2) * 4) if R else 0,
+        "pairs": pairs,
+        "features": F,
+    }
+
+
+class ClockSampler:
+    """nvidia-smi samples of this GPU's clocks while the timed region runs."""
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{device_index}.csv")
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+        except Exception:
+            uuid = None
+        self.uuid = uuid
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            cmd = ["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+            if self.uuid:
+                cmd += ["-i", self.uuid]
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(cmd, stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self) -> dict:
+        try:
+            rows = [r.split(", ") for r in open(self.path).read().strip().splitlines() if r.count(",") >= 9]
+        except Exception:
+            rows = []
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        mx = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[j] for r in rows for j in range(4) if r[6 + j].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+_FMA_SRC = r"""
+extern "C" __global__ void fma_probe(float* out, int iters) {
+  float a0 = threadIdx.x * 1e-7f, a1 = a0 + 1e-6f, a2 = a0 + 2e-6f, a3 = a0 + 3e-6f;
+  float a4 = a0 + 4e-6f, a5 = a0 + 5e-6f, a6 = a0 + 6e-6f, a7 = a0 + 7e-6f;
+  for (int i = 0; i < iters; ++i) {
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      a0 = fmaf(a0, 0.9999f, 1e-7f); a1 = fmaf(a1, 0.9999f, 1e-7f);
+      a2 = fmaf(a2, 0.9999f, 1e-7f); a3 = fmaf(a3, 0.9999f, 1e-7f);
+      a4 = fmaf(a4, 0.9999f, 1e-7f); a5 = fmaf(a5, 0.9999f, 1e-7f);
+      a6 = fmaf(a6, 0.9999f, 1e-7f); a7 = fmaf(a7, 0.9999f, 1e-7f);
+    }
+  }
+  out[blockIdx.x * blockDim.x + threadIdx.x] = a0 + a1 + a2 + a3 + a4 + a5 + a6 + a7;
+}
+"""
+
+
+def fp32_fma_peak_tflops(dev: torch.device) -> float:
+    """FP32 FMA-pipe throughput of this GPU, measured with a small NVRTC-compiled
+    kernel (8 independent FMA chains per thread, all SMs full)."""
+    from cuda.bindings import driver, nvrtc
+
+    prog = nvrtc.nvrtcCreateProgram(_FMA_SRC.encode(), b"fma_probe.cu", 0, [], [])[1]
+    opts = [b"--gpu-architecture=sm_100a", b"-O3"]
+    if nvrtc.nvrtcCompileProgram(prog, len(opts), opts)[0] != nvrtc.nvrtcResult.NVRTC_SUCCESS:
+        return float("nan")
+    size = nvrtc.nvrtcGetCUBINSize(prog)[1]
+    cubin = b" " * size
+    nvrtc.nvrtcGetCUBIN(prog, cubin)
+    torch.cuda.synchronize(dev)
+    mod = driver.cuModuleLoadData(cubin)[1]
+    fn = driver.cuModuleGetFunction(mod, b"fma_probe")[1]
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    blocks, threads, iters = sms * 8, 256, 4096
+    out = torch.empty(blocks * threads, device=dev)
+    import ctypes
+    p_out = ctypes.c_void_p(out.data_ptr())
+    p_it = ctypes.c_int(iters)
+    args = (ctypes.c_void_p * 2)(ctypes.addressof(p_out), ctypes.addressof(p_it))
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    best = float("inf")
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        driver.cuLaunchKernel(fn, blocks, 1, 1, threads, 1, 1, 0, stream, ctypes.addressof(args), 0)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        best = min(best, e0.elapsed_time(e1) / 1e3)
+    driver.cuModuleUnload(mod)
+    flops = blocks * threads * iters * 16 * 8 * 2
+    return flops / best / 1e12
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+class Staged:
+    """The forward as its three C-ABI launches, with CUDA events between them
+    so every kernel's device time is measured on the launching stream."""
+
+    def __init__(self, sa_lib, c, q3, k3, v3, head_range, dev):
+        from streaming_attention_b200 import draws
+        self.lib = sa_lib
+        self.c = c
+        self.q3, self.k3, self.v3 = q3, k3, v3
+        bh, n, d = q3.shape
+        dv = v3.shape[-1]
+        self.bh, self.n, self.d, self.dv = bh, n, d, dv
+        self.scale = float(1.0 / math.sqrt(d) if c["scale"] is None else c["scale"])
+        self.comp = {"none": 0, "sorted_pair": 1, "random": 2}[c["compressor"]]
+        self.tables = draws.draw_tables(seed=0, batch=c["B"], heads=c["H"], n=n, d=d, block_size=c["block_size"],
+                                        compressor=c["compressor"], device=dev, head_range=head_range)
+        nc = self.tables.completed_blocks
+        m = self.tables.reps_per_block
+        R = nc * m if self.comp else 0
+        self.R = R
+        self.low = torch.empty(bh, n, dv + 1, device=dev)
+        self.out = torch.empty(bh, n, dv, device=dev)
+        self.rep_idx = torch.empty(bh, max(R, 1), device=dev, dtype=torch.int32)
+        self.rk = torch.empty(bh, max(R, 1), d, device=dev)
+        self.rv = torch.empty(bh, max(R, 1), dv, device=dev)
+        self.rw = torch.empty(bh, max(R, 1), device=dev)
+        self.launches = (1 if R else 0) + 2
+        self.times = {"compress": [], "moments": [], "residual": []}
+
+    def step(self, stream, record=False):
+        from streaming_attention_b200 import _lib
+        c, t = self.c, self.tables
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
+        if record:
+            ev[0].record()
+        if self.R:
+            _lib.check(self.lib.sa_compress_blocks(
+                self.k3.data_ptr(), self.v3.data_ptr(), self.bh, self.n, self.d, self.dv, c["block_size"],
+                self.comp, t.dirs.data_ptr() if t.dirs is not None else None,
+                t.coins.data_ptr() if t.coins is not None else None,
+                t.perms.data_ptr() if t.perms is not None else None, self.rep_idx.data_ptr(), self.rk.data_ptr(),
+                self.rv.data_ptr(), self.rw.data_ptr(), stream), "compress")
+        if record:
+            ev[1].record()
+        _lib.check(self.lib.sa_low_moments(self.q3.data_ptr(), self.k3.data_ptr(), self.v3.data_ptr(), self.bh,
+                                           self.n, self.d, self.dv, c["degree"], c["block_size"], self.scale,
+                                           self.low.data_ptr(), stream), "moments")
+        if record:
+            ev[2].record()
+        rk = self.rk if self.R else self.k3
+        rv = self.rv if self.R else self.v3
+        _lib.check(self.lib.sa_residual_combine(
+            self.q3.data_ptr(), self.k3.data_ptr(), self.v3.data_ptr(), rk.data_ptr(), rv.data_ptr(),
+            self.rw.data_ptr() if self.R else None, self.low.data_ptr(), self.bh, self.n, self.d, self.dv,
+            c["degree"], c["block_size"], self.comp, self.scale, 1e-12, self.out.data_ptr(), stream), "residual")
+        if record:
+            ev[3].record()
+        return ev
+
+    def collect(self, evs):
+        for ev in evs:
+            self.times["compress"].append(ev[0].elapsed_time(ev[1]))
+            self.times["moments"].append(ev[1].elapsed_time(ev[2]))
+            self.times["residual"].append(ev[2].elapsed_time(ev[3]))
+
+
+def run_ours(args, rank, world, dev):
+    import streaming_attention_b200 as sa
+    from streaming_attention_b200 import _lib, workloads
+
+    c = workloads.config(args.config)
+    bh_total = c["B"] * c["H"]
+    if bh_total % world:
+        raise SystemExit(f"B*H={bh_total} does not split over {world} GPUs")
+    per = bh_total // world
+    h0, h1 = rank * per, (rank + 1) * per
+    q, k, v = workloads.make_inputs(c, seed=0, device=dev, generator_device="cuda", heads=(h0, h1))
+    q3, k3, v3 = q.reshape(per, c["N"], c["d"]), k.reshape(per, c["N"], c["d"]), v.reshape(per, c["N"], c["dv"])
+    lib = _lib.load()
+    st = Staged(lib, c, q3, k3, v3, (h0, h1), dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        st.step(stream)
+    barrier()
+    evs = []
+    with ClockSampler(dev.index) as clk:
+        barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            evs.append(st.step(stream, record=True))
+        t1.record()
+        barrier()
+    st.collect(evs)
+    ms = t0.elapsed_time(t1)
+    ms_max = reduce_max(ms, world, dev)
+
+    # end to end through the public entry point, from pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+        hout = torch.empty(q.shape[:-1] + (c["dv"],), dtype=torch.float32).pin_memory()
+        kw = dict(degree=c["degree"], block_size=c["block_size"], scale=c["scale"], compressor=c["compressor"],
+                  seed=0)
+
+        grid = (c["B"], c["H"], c["N"])
+
+        def e2e_step():
+            dq, dk, dvv = (x.to(dev, non_blocking=True) for x in (hq, hk, hv))
+            if per == bh_total:
+                o = sa.fast_article_causal_attention(dq.view(*grid, c["d"]), dk.view(*grid, c["d"]),
+                                                     dvv.view(*grid, c["dv"]), **kw)
+            else:
+                o = sa.fast.fast_article_causal_attention_shard(dq, dk, dvv, head_range=(h0, h1), batch=c["B"],
+                                                                heads=c["H"], **kw)
+            hout.view(o.shape).copy_(o, non_blocking=True)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        barrier()
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        a1.record()
+        barrier()
+        e2e_ms = reduce_max(a0.elapsed_time(a1), world, dev)
+        e2e = {"value": bh_total * c["N"] * args.steps / (e2e_ms / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": int((hq.numel() + hk.numel() + hv.numel()) * 4 * world),
+               "d2h_bytes_per_step": int(hout.numel() * 4 * world), "ms_per_step": e2e_ms / args.steps}
+
+    out = None
+    if rank == 0:
+        work = algorithmic_work(c)
+        avg = {k_: statistics.mean(v_) for k_, v_ in st.times.items() if v_}
+        dominant = max(avg, key=avg.get)
+        peaks = measured_peaks()
+        try:
+            fma_peak = fp32_fma_peak_tflops(dev)
+        except Exception as exc:  # the probe is a measurement aid only
+            print(f"fp32 probe failed: {exc!r}", file=sys.stderr)
+            fma_peak = float("nan")
+        if dominant == "compress":
+            achieved = work["compress_bytes"] * per / (avg["compress"] / 1e3) / 1e9
+            roof = {"bound": "hbm", "achieved": achieved, "peak": peaks.get("hbm_gbs", 6650.0), "unit": "GB/s"}
+        else:
+            flops = work["residual_flops" if dominant == "residual" else "moment_flops"] * per
+            achieved = flops / (avg[dominant] / 1e3) / 1e12
+            roof = {"bound": "fp32", "achieved": achieved, "peak": fma_peak, "unit": "TFLOP/s"}
+        roof["frac"] = roof["achieved"] / roof["peak"] if roof["peak"] else None
+        roof["kernel"] = dominant
+        roof["traffic"] = None
+        roof["peak_source"] = ("measured FP32 FMA pipe (NVRTC probe in bench.py)" if roof["bound"] == "fp32"
+                               else "MEASURED_PEAKS.json hbm_gbs")
+        kernels = {}
+        for name, t_ in avg.items():
+            kernels[name] = {"ms": t_, "share": t_ / sum(avg.values())}
+        kernels["residual"]["tflops"] = work["residual_flops"] * per / (avg["residual"] / 1e3) / 1e12
+        kernels["moments"]["tflops"] = work["moment_flops"] * per / (avg["moments"] / 1e3) / 1e12
+        if "compress" in avg and avg["compress"] > 0:
+            kernels["compress"]["gbs"] = work["compress_bytes"] * per / (avg["compress"] / 1e3) / 1e9
+        value = bh_total * c["N"] * args.steps / (ms_max / 1e3)
+        out = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, CUDA generator)",
+            "config": {"workload": workload_name(c, args.config), "B": c["B"], "H": c["H"], "N": c["N"],
+                       "d": c["d"], "dv": c["dv"], "degree": c["degree"], "block_size": c["block_size"],
+                       "compressor": c["compressor"], "parallelism": f"heads sharded over {world} GPU(s)",
+                       "l2": "inputs larger than L2 (no flush needed)"},
+            "roofline": roof, "kernels": kernels,
+            "e2e": e2e, "gpu_launches": st.launches * args.steps,
+            "clocks": clk.summary(), "fp32_fma_peak_tflops": fma_peak,
+        }
+    return out, c
+
+
+def reduce_max(ms: float, world: int, dev) -> float:
+    if world == 1:
+        return ms
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU: the oracle port (the reference's algorithm in float32 numpy)
+# ---------------------------------------------------------------------------
+
+def cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        info = threadpool_info()
+        return max([i.get("num_threads", 1) for i in info] or [1])
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_sample(c: dict, heads: int, seed: int = 0):
+    """Run the oracle port (float32) on `heads` sequences of config c; returns seconds."""
+    from oracle import oracle as O
+    from streaming_attention_b200 import workloads
+
+    q, k, v = workloads.make_inputs(c, seed=seed, generator_device="cpu", heads=(0, heads))
+    q, k, v = q.numpy(), k.numpy(), v.numpy()
+    t0 = time.perf_counter()
+    for h in range(heads):
+        O.fast_attention_single(q[h], k[h], v[h], degree=c["degree"], block_size=c["block_size"], scale=c["scale"],
+                                compressor=c["compressor"], seed=h, dtype=np.float32)
+    return time.perf_counter() - t0
+
+
+def auto_sample_heads(c: dict, budget_s: float) -> int:
+    """Heads whose CPU time is about budget_s (at least one)."""
+    one = cpu_sample(c, 1)
+    return max(1, min(c["B"] * c["H"], int(budget_s / max(one, 1e-3))))
+
+
+def run_reference(args, rank, world):
+    from streaming_attention_b200 import workloads
+
+    if rank != 0:
+        return None
+    c = workloads.config(args.config)
+    heads = args.cpu_sample_heads or auto_sample_heads(c, 2.0)
+    for _ in range(args.warmup):
+        cpu_sample(c, heads)
+    times = [cpu_sample(c, heads) for _ in range(args.steps)]
+    per_step = statistics.mean(times)
+    value = heads * c["N"] / per_step
+    sample = f"{heads} of {c['B'] * c['H']} sequences (full N={c['N']}) per step"
+    return {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, CPU generator)",
+        "config": {"workload": workload_name(c, args.config)},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# ---------------------------------------------------------------------------
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+    try:
+        line, c = run_ours(args, rank, world, dev)
+        if rank == 0:
+            if world == 1 and not args.no_cpu_baseline:
+                heads = args.cpu_sample_heads or auto_sample_heads(c, 10.0)
+                secs = cpu_sample(c, heads)
+                line["cpu_baseline"] = {"value": heads * c["N"] / secs, "unit": UNIT, "cores": cpu_threads(),
+                                        "kind": "port",
+                                        "sample": f"{heads} of {c['B'] * c['H']} sequences (full N={c['N']}), "
+                                                  "oracle/oracle.py in float32"}
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

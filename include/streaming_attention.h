@@ -1,0 +1,125 @@
+/*
+ * streaming_attention.h -- C ABI of the B200 (sm_100a) streaming Taylor-moment
+ * + block-coreset causal attention library (libsa_b200.so).
+ *
+ * Every entry point takes raw pointers and sizes, enqueues its work on the
+ * given CUDA stream (a cudaStream_t passed as void*, NULL = legacy default
+ * stream) of the current device, and returns an int status (SA_OK == 0,
+ * negative on error).  Nothing throws across this boundary.  After an error,
+ * sa_last_error() returns a message for the calling thread.
+ *
+ * Tensor layouts (all contiguous, row-major, fp32 unless noted):
+ *   q, k  [bh, n, d]      v, out  [bh, n, dv]
+ *   bh = B*H sequences ("heads"); each is processed independently.
+ *
+ * Coreset draw tables (host-generated, copied to the device; see
+ * streaming_attention_b200/draws.py).  nc = completed blocks per head =
+ * (n - 1) / block_size, m = (block_size + 1) / 2 reps per completed block:
+ *   dirs  [bh, nc, d]              fp32, unit projection direction per block
+ *   coins [bh, nc, block_size/2]   fp32 uniform draws in [0,1) per pair
+ *   perms [bh, nc, m]              int32 block-local indices (random
+ *                                  compressor, and sorted_pair when
+ *                                  block_size <= 2)
+ *
+ * Reference interfaces replaced (PositiveLoss/streaming-attention):
+ *   sa_fast_attention      fast_article_causal_attention
+ *                          (fast_article_attention.py:634-719) and its
+ *                          per-sequence body (:522-631)
+ *   sa_compress_blocks     _build_completed_block_reps (:364-434) +
+ *                          _compress_one_completed_block (:312-361)
+ *   sa_low_moments         low_degree_taylor_causal_sums (:262-285) and the
+ *                          moment sketch (streaming_taylor_coreset_attention.py:229-296)
+ *   sa_residual_combine    _block_coreset_residual_tail (:467-514),
+ *                          _full_residual_tail (:437-464) and the final
+ *                          num / clamp(den, eps) (:596-598)
+ *   sa_feature_count       num_taylor_features (:137-148) /
+ *                          SymmetricTaylorFeatureMap.total_features
+ *                          (streaming_taylor_coreset_attention.py:180-182)
+ */
+#ifndef STREAMING_ATTENTION_H_
+#define STREAMING_ATTENTION_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define SA_OK 0
+#define SA_ERR_INVALID_ARG (-1)   /* bad shape / size / pointer; ValueError */
+#define SA_ERR_UNSUPPORTED (-2)   /* degree or dims beyond the kernels; NotImplementedError */
+#define SA_ERR_CUDA (-3)          /* CUDA launch or runtime error; RuntimeError */
+#define SA_ERR_TIMEOUT (-4)       /* a bounded device-side wait gave up */
+#define SA_ERR_WORKSPACE (-5)     /* workspace smaller than sa_*_workspace_size */
+
+/* compressor kinds (fast_article_attention.py:326, :332, :383) */
+#define SA_COMPRESSOR_NONE 0
+#define SA_COMPRESSOR_SORTED_PAIR 1
+#define SA_COMPRESSOR_RANDOM 2
+
+/* largest supported Taylor degree and feature count */
+#define SA_MAX_DEGREE 3
+#define SA_MAX_DIM 256
+#define SA_MAX_VALUE_DIM 256
+
+/* Library version, e.g. 100 for 0.1.0. */
+int sa_version(void);
+
+/* Message of the last error on this thread ("" if none). */
+const char* sa_last_error(void);
+
+/* Feature count sum_{l<=degree} C(dim+l-1, l). */
+int sa_feature_count(int dim, int degree, int64_t* count);
+
+/* Number of completed blocks that a later query reads: (n-1)/block_size
+ * (fast_article_attention.py:403-407).  *reps_per_block = (block_size+1)/2,
+ * or block_size for compressor none. */
+int sa_block_counts(int64_t n, int block_size, int compressor, int64_t* completed_blocks,
+                    int64_t* reps_per_block);
+
+/* C1: compress every completed block of every head.
+ * Outputs: rep_idx [bh, nc*m] int32 (global token index within the head, the
+ * bit-exact selection), rep_k [bh, nc*m, d], rep_v [bh, nc*m, dv],
+ * rep_w [bh, nc*m].  Any of rep_k / rep_v / rep_w may be NULL. */
+int sa_compress_blocks(const float* k, const float* v, int64_t bh, int64_t n, int d, int dv,
+                       int block_size, int compressor, const float* dirs, const float* coins,
+                       const int32_t* perms, int32_t* rep_idx, float* rep_k, float* rep_v,
+                       float* rep_w, void* stream);
+
+/* Low-degree Taylor term of every query, with the moment state taken over the
+ * completed blocks before the query's own block:
+ *   low[i, :dv] = sum_{j < bstart(i)} P_t(scale q_i.k_j) v_j,
+ *   low[i, dv]  = sum_{j < bstart(i)} P_t(scale q_i.k_j),
+ * where bstart(i) = (i / block_size) * block_size.  low is [bh, n, dv+1]. */
+int sa_low_moments(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d,
+                   int dv, int degree, int block_size, float scale, float* low, void* stream);
+
+/* Residual over the completed-block reps + exact current block, added to the
+ * low term, then out = num / max(den, eps).  For compressor none pass
+ * rep_k = k, rep_v = v, rep_w = NULL (all weights 1, block_size reps per block). */
+int sa_residual_combine(const float* q, const float* k, const float* v, const float* rep_k,
+                        const float* rep_v, const float* rep_w, const float* low, int64_t bh,
+                        int64_t n, int d, int dv, int degree, int block_size, int compressor,
+                        float scale, float eps, float* out, void* stream);
+
+/* Bytes of device workspace sa_fast_attention needs. */
+int sa_fast_attention_workspace_size(int64_t bh, int64_t n, int d, int dv, int degree,
+                                     int block_size, int compressor, size_t* bytes);
+
+/* The whole forward of fast_article_causal_attention for bh sequences.
+ * rep_idx (nullable) receives the coreset selection [bh, nc*m].  workspace is
+ * caller-owned device memory of at least sa_fast_attention_workspace_size
+ * bytes, 256-byte aligned. */
+int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d,
+                      int dv, int degree, int block_size, float scale, int compressor,
+                      const float* dirs, const float* coins, const int32_t* perms, float eps,
+                      float* out, int32_t* rep_idx, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* STREAMING_ATTENTION_H_ */

@@ -1,0 +1,21 @@
+"""B200-native (sm_100a) streaming Taylor-moment + block-coreset causal attention.
+
+Drop-in for the fast path of PositiveLoss/streaming-attention
+(``fast_article_attention.py``): the same entry points and arguments, computed
+by hand-written CUDA kernels in ``libsa_b200.so`` through a C ABI
+(``include/streaming_attention.h``).  There is no CPU fallback.
+"""
+
+from .fast import (  # noqa: F401
+    BlockReps,
+    FastArticleStats,
+    build_completed_block_reps,
+    classical_causal_attention,
+    exp_taylor,
+    fast_article_causal_attention,
+    fast_article_causal_attention_single,
+    num_taylor_features,
+    safe_relative_l2,
+)
+
+__version__ = "0.1.0"

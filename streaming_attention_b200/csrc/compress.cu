@@ -1,0 +1,158 @@
+// C1: per-block coreset compressor (sorted_pair and random).
+//
+// Follows _compress_one_completed_block (fast_article_attention.py:312-361)
+// and _build_completed_block_reps (:364-434): every completed block (one that
+// has a later query) is halved.  sorted_pair projects the block's keys on a
+// unit direction, sorts, pairs neighbours (0,1),(2,3),... and keeps one key of
+// each pair with probability proportional to its weight (u < wa/(wa+wb),
+// streaming_taylor_coreset_attention.py:452-457; with the unit weights of a
+// fresh block this is the u < 0.5 of fast_article_attention.py:348), giving it
+// the pair's summed weight; an odd last key is carried with its own weight.
+// random keeps perm[:m] with weight n/m (:326-330), also used for blocks of
+// <= 2 keys (:333-337).
+//
+// One CTA per (completed block, head).  Scores are float64 sums of exact
+// float32*float32 products taken sequentially over the feature axis, so the
+// order equals the one the CPU oracle computes; the sort is a shared-memory
+// bitonic sort over (score, index) keys, so equal scores keep index order.
+#include <float.h>
+#include <math.h>
+
+#include "sa_common.cuh"
+
+namespace sa {
+
+namespace {
+
+constexpr int kCompressThreads = 256;
+
+// Order-preserving map of a double to uint64 (NaN above +inf, -0 == +0).
+__device__ __forceinline__ unsigned long long orderable(double x) {
+  if (x != x) return 0xFFFFFFFFFFFFFFFEull;  // NaN: after every number
+  x = x + 0.0;                               // -0.0 -> +0.0
+  unsigned long long u = (unsigned long long)__double_as_longlong(x);
+  return (u & 0x8000000000000000ull) ? ~u : (u | 0x8000000000000000ull);
+}
+
+__global__ void __launch_bounds__(kCompressThreads)
+compress_blocks_kernel(const float* __restrict__ k, const float* __restrict__ v, int64_t n, int d, int dv,
+                       int bs, int nc, int m, int pow2, int use_perm, const float* __restrict__ dirs,
+                       const float* __restrict__ coins, const int32_t* __restrict__ perms,
+                       int32_t* __restrict__ rep_idx, float* __restrict__ rep_k, float* __restrict__ rep_v,
+                       float* __restrict__ rep_w) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned long long* skey = reinterpret_cast<unsigned long long*>(smem_raw);
+  int* sidx = reinterpret_cast<int*>(skey + pow2);
+  int* sel = sidx + pow2;
+  float* selw = reinterpret_cast<float*>(sel + m);
+  double* sdir = reinterpret_cast<double*>(
+      reinterpret_cast<unsigned char*>(smem_raw) + (((size_t)pow2 * 12 + (size_t)m * 8 + 15) & ~(size_t)15));
+
+  const int c = blockIdx.x;
+  const int64_t h = blockIdx.y;
+  const int64_t start = (int64_t)c * bs;
+  const int tid = threadIdx.x;
+  const int64_t blk = h * nc + c;
+
+  if (use_perm) {
+    const float w = (float)((double)bs / (double)m);
+    for (int p = tid; p < m; p += blockDim.x) {
+      sel[p] = perms[blk * m + p];
+      selw[p] = w;
+    }
+  } else {
+    for (int a = tid; a < d; a += blockDim.x) sdir[a] = (double)dirs[blk * d + a];
+    __syncthreads();
+    const float* kb = k + (h * n + start) * d;
+    for (int t = tid; t < pow2; t += blockDim.x) {
+      unsigned long long key = 0xFFFFFFFFFFFFFFFFull;  // padding sorts last
+      if (t < bs) {
+        const float* row = kb + (int64_t)t * d;
+        double acc = 0.0;
+        for (int a = 0; a < d; ++a) acc = fma((double)__ldg(row + a), sdir[a], acc);
+        key = orderable(acc);
+      }
+      skey[t] = key;
+      sidx[t] = t;
+    }
+    __syncthreads();
+    // bitonic sort, ascending by (key, index)
+    for (int size = 2; size <= pow2; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int t = tid; t < (pow2 >> 1); t += blockDim.x) {
+          const int lo = 2 * t - (t & (stride - 1));
+          const int hi = lo + stride;
+          const bool up = ((lo & size) == 0);
+          const unsigned long long klo = skey[lo], khi = skey[hi];
+          const int ilo = sidx[lo], ihi = sidx[hi];
+          const bool gt = (klo > khi) || (klo == khi && ilo > ihi);
+          if (gt == up) {
+            skey[lo] = khi;
+            skey[hi] = klo;
+            sidx[lo] = ihi;
+            sidx[hi] = ilo;
+          }
+        }
+        __syncthreads();
+      }
+    }
+    const int pairs = bs / 2;
+    const float* cb = coins + (int64_t)blk * pairs;
+    for (int p = tid; p < pairs; p += blockDim.x) {
+      const float wa = 1.0f, wb = 1.0f;  // a fresh block has unit weights
+      const float wsum = wa + wb;
+      const float prob_a = wa / fmaxf(wsum, 1e-30f);
+      const bool choose_a = cb[p] < prob_a;
+      sel[p] = choose_a ? sidx[2 * p] : sidx[2 * p + 1];
+      selw[p] = wsum;
+    }
+    if ((bs & 1) && tid == 0) {
+      sel[pairs] = sidx[bs - 1];
+      selw[pairs] = 1.0f;
+    }
+  }
+  __syncthreads();
+
+  // write the selection and gather the rep rows (one warp per rep)
+  const int64_t rbase = h * (int64_t)nc * m + (int64_t)c * m;
+  for (int p = tid; p < m; p += blockDim.x) {
+    if (rep_idx) rep_idx[rbase + p] = (int32_t)(start + sel[p]);
+    if (rep_w) rep_w[rbase + p] = selw[p];
+  }
+  const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  for (int p = warp; p < m; p += nwarps) {
+    const int64_t src = h * n + start + sel[p];
+    if (rep_k)
+      for (int a = lane; a < d; a += 32) rep_k[(rbase + p) * d + a] = __ldg(k + src * d + a);
+    if (rep_v)
+      for (int a = lane; a < dv; a += 32) rep_v[(rbase + p) * dv + a] = __ldg(v + src * dv + a);
+  }
+}
+
+}  // namespace
+
+int launch_compress(const float* k, const float* v, int64_t bh, int64_t n, int d, int dv, int bs, int compressor,
+                    const float* dirs, const float* coins, const int32_t* perms, int32_t* rep_idx, float* rep_k,
+                    float* rep_v, float* rep_w, cudaStream_t stream) {
+  const int64_t nc = n > 0 ? (n - 1) / bs : 0;
+  const int m = (bs + 1) / 2;
+  if (nc == 0 || bh == 0) return SA_OK;
+  if (nc > 2147483647LL || bh > 65535) return set_error(SA_ERR_UNSUPPORTED, "too many blocks or heads for one launch");
+  const bool use_perm = (compressor == SA_COMPRESSOR_RANDOM) || bs <= 2;
+  if (use_perm && !perms) return set_error(SA_ERR_INVALID_ARG, "perms table is required");
+  if (!use_perm && (!dirs || !coins)) return set_error(SA_ERR_INVALID_ARG, "dirs and coins tables are required");
+  int pow2 = 1;
+  while (pow2 < bs) pow2 <<= 1;
+  if (pow2 > 4096) return set_error(SA_ERR_UNSUPPORTED, "block_size > 4096 is not supported by the compressor");
+  const size_t smem = (((size_t)pow2 * 12 + (size_t)m * 8 + 15) & ~(size_t)15) + (size_t)d * 8;
+  if (smem > 48 * 1024) {
+    cudaFuncSetAttribute(compress_blocks_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  }
+  dim3 grid((unsigned)nc, (unsigned)bh);
+  compress_blocks_kernel<<<grid, kCompressThreads, smem, stream>>>(k, v, n, d, dv, bs, (int)nc, m, pow2,
+                                                                   use_perm ? 1 : 0, dirs, coins, perms, rep_idx,
+                                                                   rep_k, rep_v, rep_w);
+  return check_launch("compress_blocks_kernel");
+}
+
+}  // namespace sa

@@ -1,0 +1,103 @@
+// Shared helpers for the sm_100a kernels and the C ABI of libsa_b200.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/streaming_attention.h"
+
+namespace sa {
+
+// Records a message for sa_last_error() on this host thread and returns code.
+int set_error(int code, const char* fmt, ...);
+
+// Maps the last CUDA launch error (if any) to SA_ERR_CUDA.
+int check_launch(const char* what);
+
+__host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Feature count sum_{l<=t} C(d+l-1, l) for t <= 3.
+__host__ __device__ inline int64_t feature_count(int d, int t) {
+  int64_t f = 1;
+  if (t >= 1) f += d;
+  if (t >= 2) f += (int64_t)d * (d + 1) / 2;
+  if (t >= 3) f += (int64_t)d * (d + 1) * (d + 2) / 6;
+  return f;
+}
+
+// Monomial of feature f in combinations_with_replacement order
+// (streaming_taylor_coreset_attention.py:170; for degree 2 identical to the
+// triu order of fast_article_attention.py:173).  Index d stands for the
+// constant 1, so every feature is x[a]*x[b]*x[c] over a row with x[d] = 1.
+// coef is the key-side Taylor factor 1/prod(alpha_j!) (streaming...py:78-93).
+struct Monomial {
+  int a, b, c;
+  float coef;
+};
+
+__host__ __device__ inline Monomial monomial_of(int64_t f, int d) {
+  Monomial m{d, d, d, 1.0f};
+  if (f == 0) return m;
+  f -= 1;
+  if (f < d) {
+    m.a = (int)f;
+    return m;
+  }
+  f -= d;
+  const int64_t n2 = (int64_t)d * (d + 1) / 2;
+  if (f < n2) {
+    int a = 0;
+    while (f >= d - a) {
+      f -= d - a;
+      ++a;
+    }
+    m.a = a;
+    m.b = a + (int)f;
+    m.coef = (m.a == m.b) ? 0.5f : 1.0f;
+    return m;
+  }
+  f -= n2;
+  int a = 0;
+  while (true) {
+    const int64_t rem = d - a;
+    const int64_t cnt = rem * (rem + 1) / 2;
+    if (f < cnt) break;
+    f -= cnt;
+    ++a;
+  }
+  int b = a;
+  while (f >= d - b) {
+    f -= d - b;
+    ++b;
+  }
+  m.a = a;
+  m.b = b;
+  m.c = b + (int)f;
+  if (m.a == m.b && m.b == m.c)
+    m.coef = 1.0f / 6.0f;
+  else if (m.a == m.b || m.b == m.c)
+    m.coef = 0.5f;
+  return m;
+}
+
+// exp_{<=t}(x) accumulated as the reference does: term *= x / r; out += term
+// (fast_article_attention.py:95-104).
+// Division by 1 and 2 is written as the (exactly equal) multiplications.
+__device__ __forceinline__ float taylor_poly(float x, int degree) {
+  float out = 1.0f;
+  if (degree >= 1) {
+    float term = x;
+    out = out + term;
+    if (degree >= 2) {
+      term = term * x * 0.5f;
+      out = out + term;
+      for (int r = 3; r <= degree; ++r) {
+        term = __fdiv_rn(term * x, (float)r);
+        out = out + term;
+      }
+    }
+  }
+  return out;
+}
+
+}  // namespace sa

@@ -1,0 +1,350 @@
+"""Drop-in GPU entry points of the reference fast path.
+
+Mirrors ``fast_article_attention.py`` of PositiveLoss/streaming-attention:
+same names, keyword arguments, argument checks and messages, return types and
+``FastArticleStats`` fields.  All arithmetic runs in the sm_100a kernels of
+libsa_b200.so (compressor, block-granular moment scan, residual + combine);
+this module only validates, lays tensors out contiguously, builds the
+compressor's draw tables and calls the C ABI.  There is no CPU path: CPU
+tensors are rejected, and a missing library raises.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional, Tuple, Union
+
+import torch
+
+from . import _lib
+from .draws import DrawTables, completed_blocks, draw_tables
+
+Tensor = torch.Tensor
+
+__all__ = [
+    "FastArticleStats", "fast_article_causal_attention", "fast_article_causal_attention_single",
+    "num_taylor_features", "exp_taylor", "safe_relative_l2", "classical_causal_attention",
+    "build_completed_block_reps", "BlockReps",
+]
+
+
+@dataclass(frozen=True)
+class FastArticleStats:
+    """Field-for-field copy of fast_article_attention.py:293-301."""
+    degree: int
+    block_size: int
+    feature_count: int
+    coreset_items: int
+    approx_streaming_state_bytes: int
+    scratch_low_prefix_bytes: int
+    scratch_residual_matrix_bytes: int
+
+
+@dataclass(frozen=True)
+class BlockReps:
+    """Reps of the completed blocks (fast_article_attention.py:304-309) plus the
+    selected global token indices."""
+    keys: Tensor
+    values: Tensor
+    weights: Tensor
+    active_from: Tensor
+    indices: Tensor
+
+
+def _attention_scale(scale: Optional[float], dim: int) -> float:
+    """fast_article_attention.py:76-77."""
+    return float(1.0 / math.sqrt(dim) if scale is None else scale)
+
+
+def num_taylor_features(dim: int, degree: int) -> int:
+    """Feature count through ``degree`` (fast_article_attention.py:137-148),
+    extended to degree 3 (streaming_taylor_coreset_attention.py:155-164)."""
+    if degree < 0:
+        raise ValueError("degree must be non-negative")
+    if degree > _lib.MAX_DEGREE:
+        raise NotImplementedError(f"this implementation supports degree 0, 1, 2 or 3 (got {degree})")
+    total = 1
+    for l in range(1, degree + 1):
+        total += math.comb(dim + l - 1, l)
+    return total
+
+
+def exp_taylor(logits: Tensor, degree: int) -> Tensor:
+    """Elementwise sum_{r<=degree} logits**r / r! (fast_article_attention.py:95-104).
+    A small helper kept for API parity; it is not on the kernel path."""
+    if degree < 0:
+        raise ValueError("degree must be non-negative")
+    out = torch.ones_like(logits)
+    term = torch.ones_like(logits)
+    for r in range(1, degree + 1):
+        term = term * logits / float(r)
+        out = out + term
+    return out
+
+
+def safe_relative_l2(a: Tensor, b: Tensor, eps: float = 1e-12) -> float:
+    """fast_article_attention.py:107-108."""
+    return (torch.linalg.vector_norm(a - b) / torch.clamp(torch.linalg.vector_norm(b), min=eps)).item()
+
+
+@torch.no_grad()
+def classical_causal_attention(q: Tensor, k: Tensor, v: Tensor, *, scale: Optional[float] = None) -> Tensor:
+    """Exact causal softmax attention for [..., N, D] tensors (fast_article_attention.py:116-129,
+    streaming_taylor_coreset_attention.py:624-638).  A torch helper for comparisons, not the
+    product path."""
+    if q.shape[:-1] != k.shape[:-1] or v.shape[:-1] != k.shape[:-1]:
+        raise ValueError("q and k must match, and v must have the same sequence length")
+    s = _attention_scale(scale, q.shape[-1])
+    logits = torch.matmul(q, k.transpose(-1, -2)) * s
+    n = q.shape[-2]
+    mask = torch.ones(n, n, device=q.device, dtype=torch.bool).tril()
+    logits = logits.masked_fill(~mask, float("-inf"))
+    return torch.matmul(torch.softmax(logits, dim=-1), v)
+
+
+# ---------------------------------------------------------------------------
+# argument checks (mirror the reference's order and messages)
+# ---------------------------------------------------------------------------
+
+def _check_single(q: Tensor, k: Tensor, v: Tensor, query_chunk_size: int, block_size: int) -> None:
+    """fast_article_attention.py:552-561."""
+    if q.ndim != 2 or k.ndim != 2 or v.ndim != 2:
+        raise ValueError("q,k,v must have shapes [N,D], [N,D], [N,Dv]")
+    if q.shape != k.shape:
+        raise ValueError(f"q and k must have the same shape, got {tuple(q.shape)} and {tuple(k.shape)}")
+    if v.shape[0] != k.shape[0]:
+        raise ValueError("v must have the same sequence length as q/k")
+    if query_chunk_size <= 0:
+        raise ValueError("query_chunk_size must be positive")
+    if block_size <= 0:
+        raise ValueError("block_size must be positive")
+
+
+def _check_modes(n: int, block_size: int, degree: int, compressor: str, low_mode: str) -> None:
+    if low_mode not in ("auto", "stream", "prefix"):
+        raise ValueError("mode must be one of {'auto', 'stream', 'prefix'}")  # :285
+    if degree > _lib.MAX_DEGREE:
+        raise NotImplementedError(f"this implementation supports degree 0, 1, 2 or 3 (got {degree})")
+    if degree < 0 and n > 0:
+        raise ValueError("degree must be non-negative")  # exp_taylor, :97-98
+    # the reference rejects an unknown compressor only once a completed block
+    # reaches _compress_one_completed_block (:361)
+    if compressor not in _lib.COMPRESSORS and completed_blocks(n, block_size) > 0:
+        raise ValueError("compressor must be one of {'sorted_pair', 'random', 'none'}")
+
+
+def _check_device(*ts: Tensor) -> torch.device:
+    dev = ts[0].device
+    if dev.type != "cuda":
+        raise ValueError("the B200 kernels need CUDA tensors; move q, k, v to a CUDA device")
+    for t in ts:
+        if t.device != dev:
+            raise ValueError("q, k and v must be on the same device")
+        if t.dtype == torch.float64 or not t.dtype.is_floating_point:
+            raise ValueError(f"unsupported dtype {t.dtype}: the kernels compute in float32 "
+                             "(float32, float16 and bfloat16 inputs are accepted)")
+    return dev
+
+
+def _stats(n: int, dim: int, dv: int, degree: int, block_size: int, compressor: str, low_mode: str,
+           query_chunk_size: int, elem: int) -> FastArticleStats:
+    """fast_article_attention.py:580-631 for one sequence on a CUDA device."""
+    F = num_taylor_features(dim, degree)
+    if compressor == "none":
+        items = n
+        resid = min(query_chunk_size, n) * n * elem
+    else:
+        m = (block_size + 1) // 2
+        items = completed_blocks(n, block_size) * m
+        block_scratch = 0
+        for s0 in range(0, n, block_size):
+            b = min(s0 + block_size, n) - s0
+            block_scratch = max(block_scratch, b * b * elem)
+        resid = max(min(query_chunk_size, n) * max(items, 1) * elem, block_scratch)
+    approx = F * (1 + dv) * elem + items * (dim + dv + 1) * elem + min(block_size, n) * (dim + dv) * elem
+    resolved = "prefix" if low_mode == "auto" else low_mode
+    low_bytes = F * (1 + dv) * elem if resolved == "stream" else n * F * (1 + dv) * elem
+    return FastArticleStats(degree, block_size, F, items, int(approx), int(low_bytes), int(resid))
+
+
+# ---------------------------------------------------------------------------
+# the launch
+# ---------------------------------------------------------------------------
+
+def _ptr(t: Optional[Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _run(q3: Tensor, k3: Tensor, v3: Tensor, *, batch: int, heads: int, degree: int, block_size: int,
+         scale: float, compressor: str, seed: int, eps: float, want_rep_idx: bool = False,
+         head_range: Optional[Tuple[int, int]] = None, out: Optional[Tensor] = None):
+    """Forward of bh = q3.shape[0] sequences (contiguous float32 [bh, n, *]).
+
+    head_range selects which flattened (b, h) sequences of the full B*H grid the
+    rows of q3 are (their seeds are seed + b*H + h)."""
+    bh, n, d = q3.shape
+    dv = v3.shape[-1]
+    dev = q3.device
+    comp = _lib.COMPRESSORS.get(compressor, _lib.COMPRESSORS["sorted_pair"])
+    if out is None:
+        out = torch.empty(bh, n, dv, device=dev, dtype=torch.float32)
+    if bh == 0 or n == 0:
+        return out, None
+    hr = head_range if head_range is not None else (0, bh)
+    tables: DrawTables = draw_tables(seed=seed, batch=batch, heads=heads, n=n, d=d, block_size=block_size,
+                                     compressor=compressor if compressor in _lib.COMPRESSORS else "sorted_pair",
+                                     device=dev, head_range=hr)
+    nc = tables.completed_blocks
+    rep_idx = None
+    if want_rep_idx and compressor != "none" and nc > 0:
+        rep_idx = torch.empty(bh, nc * tables.reps_per_block, device=dev, dtype=torch.int32)
+    lib = _lib.load()
+    nbytes = _lib.ctypes.c_size_t(0)
+    _lib.check(lib.sa_fast_attention_workspace_size(bh, n, d, dv, degree, block_size, comp,
+                                                    _lib.ctypes.byref(nbytes)), "sa_fast_attention_workspace_size")
+    ws = torch.empty(max(int(nbytes.value), 256), device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        _lib.check(lib.sa_fast_attention(
+            q3.data_ptr(), k3.data_ptr(), v3.data_ptr(), bh, n, d, dv, degree, block_size, float(scale), comp,
+            _ptr(tables.dirs), _ptr(tables.coins), _ptr(tables.perms), float(eps), out.data_ptr(),
+            _ptr(rep_idx), ws.data_ptr(), ws.numel(), stream), "sa_fast_attention")
+    return out, rep_idx
+
+
+def _as_f32(t: Tensor) -> Tensor:
+    return t.to(torch.float32).contiguous()
+
+
+@torch.no_grad()
+def fast_article_causal_attention_single(
+    q: Tensor, k: Tensor, v: Tensor, *, degree: int = 2, block_size: int = 128, scale: Optional[float] = None,
+    compressor: str = "sorted_pair", seed: int = 0, query_chunk_size: int = 2048, low_mode: str = "auto",
+    denominator_eps: float = 1e-12, return_stats: bool = False,
+) -> Union[Tensor, Tuple[Tensor, FastArticleStats]]:
+    """Approximate causal attention for one [N,D] sequence
+    (fast_article_attention.py:522-631).  ``query_chunk_size`` and ``low_mode``
+    are validated as in the reference and only affect the reported stats."""
+    _check_single(q, k, v, query_chunk_size, block_size)
+    n, dim = q.shape
+    _check_modes(n, block_size, degree, compressor, low_mode)
+    _check_device(q, k, v)
+    s = _attention_scale(scale, dim)
+    out, _ = _run(_as_f32(q)[None], _as_f32(k)[None], _as_f32(v)[None], batch=1, heads=1, degree=degree,
+                  block_size=block_size, scale=s, compressor=compressor, seed=seed, eps=denominator_eps)
+    out = out[0].to(q.dtype)
+    if not return_stats:
+        return out
+    return out, _stats(n, dim, v.shape[-1], degree, block_size, compressor, low_mode, query_chunk_size,
+                       q.element_size())
+
+
+@torch.no_grad()
+def fast_article_causal_attention(
+    q: Tensor, k: Tensor, v: Tensor, *, degree: int = 2, block_size: int = 128, scale: Optional[float] = None,
+    compressor: str = "sorted_pair", seed: int = 0, query_chunk_size: int = 2048, low_mode: str = "auto",
+    denominator_eps: float = 1e-12, return_stats: bool = False,
+) -> Union[Tensor, Tuple[Tensor, FastArticleStats]]:
+    """Approximate causal attention for [N,D] or [B,H,N,D] tensors
+    (fast_article_attention.py:634-719).  Sequence (b, h) uses seed
+    ``seed + b*H + h`` (:693).  All B*H sequences run in one set of kernel
+    launches."""
+    if q.ndim == 2:
+        return fast_article_causal_attention_single(
+            q, k, v, degree=degree, block_size=block_size, scale=scale, compressor=compressor, seed=seed,
+            query_chunk_size=query_chunk_size, low_mode=low_mode, denominator_eps=denominator_eps,
+            return_stats=return_stats)
+    if q.ndim != 4:
+        raise ValueError("q/k/v must be [N,D] or [B,H,N,D]")
+    if q.shape != k.shape:
+        raise ValueError("q and k must have identical shape [B,H,N,D]")
+    if v.shape[:3] != q.shape[:3]:
+        raise ValueError("v must have shape [B,H,N,Dv]")
+    bsz, heads, n, dim = q.shape
+    dv = v.shape[-1]
+    if bsz * heads > 0:
+        if v.ndim != 4:
+            raise ValueError("q,k,v must have shapes [N,D], [N,D], [N,Dv]")
+        if query_chunk_size <= 0:
+            raise ValueError("query_chunk_size must be positive")
+        if block_size <= 0:
+            raise ValueError("block_size must be positive")
+        _check_modes(n, block_size, degree, compressor, low_mode)
+    _check_device(q, k, v)
+    bh = bsz * heads
+    s = _attention_scale(scale, dim)
+    out3, _ = _run(_as_f32(q).reshape(bh, n, dim), _as_f32(k).reshape(bh, n, dim), _as_f32(v).reshape(bh, n, dv),
+                   batch=bsz, heads=heads, degree=degree, block_size=block_size, scale=s, compressor=compressor,
+                   seed=seed, eps=denominator_eps)
+    out = out3.reshape(bsz, heads, n, dv).to(q.dtype)
+    if not return_stats:
+        return out
+    if bh == 0:
+        stats = FastArticleStats(degree, block_size, num_taylor_features(dim, degree), 0, 0, 0, 0)
+    else:
+        stats = _stats(n, dim, dv, degree, block_size, compressor, low_mode, query_chunk_size, q.element_size())
+    return out, stats
+
+
+@torch.no_grad()
+def fast_article_causal_attention_shard(
+    q: Tensor, k: Tensor, v: Tensor, *, head_range: Tuple[int, int], batch: int, heads: int, degree: int = 2,
+    block_size: int = 128, scale: Optional[float] = None, compressor: str = "sorted_pair", seed: int = 0,
+    denominator_eps: float = 1e-12,
+) -> Tensor:
+    """Forward of the flattened sequences ``head_range = [h0, h1)`` of a
+    [batch, heads] grid, for one rank of a head-sharded multi-GPU run.
+    q, k, v hold just those sequences ([h1-h0, ..., N, D] with any middle
+    shape); sequence f = b*heads + h uses seed ``seed + f`` exactly as in the
+    unsharded call, so the union of the shards equals the full result."""
+    h0, h1 = head_range
+    cnt = h1 - h0
+    n, dim = q.shape[-2], q.shape[-1]
+    dv = v.shape[-1]
+    if q.numel() != cnt * n * dim or k.shape != q.shape or v.numel() != cnt * n * dv:
+        raise ValueError("q/k/v must hold exactly the sequences of head_range")
+    if not (0 <= h0 <= h1 <= batch * heads):
+        raise ValueError("head_range outside the [batch, heads] grid")
+    if block_size <= 0:
+        raise ValueError("block_size must be positive")
+    _check_modes(n, block_size, degree, compressor, "auto")
+    _check_device(q, k, v)
+    s = _attention_scale(scale, dim)
+    out3, _ = _run(_as_f32(q).reshape(cnt, n, dim), _as_f32(k).reshape(cnt, n, dim), _as_f32(v).reshape(cnt, n, dv),
+                   batch=batch, heads=heads, degree=degree, block_size=block_size, scale=s, compressor=compressor,
+                   seed=seed, eps=denominator_eps, head_range=head_range)
+    return out3.reshape(q.shape[:-1] + (dv,)).to(q.dtype)
+
+
+@torch.no_grad()
+def build_completed_block_reps(k: Tensor, v: Tensor, *, block_size: int, compressor: str, seed: int) -> BlockReps:
+    """GPU restatement of _build_completed_block_reps (fast_article_attention.py:364-434)
+    for one [N,D] sequence: the reps, weights, active_from, and the selected token indices."""
+    if block_size <= 0:
+        raise ValueError("block_size must be positive")
+    dev = _check_device(k, v)
+    n, d = k.shape
+    dv = v.shape[-1]
+    if compressor == "none":
+        pos = torch.arange(n, device=dev)
+        return BlockReps(k, v, torch.ones(n, device=dev, dtype=k.dtype), pos, pos.to(torch.int32))
+    nc = completed_blocks(n, block_size)
+    if nc > 0 and compressor not in _lib.COMPRESSORS:
+        raise ValueError("compressor must be one of {'sorted_pair', 'random', 'none'}")
+    m = (block_size + 1) // 2
+    R = nc * m
+    k3, v3 = _as_f32(k)[None], _as_f32(v)[None]
+    idx = torch.empty(1, R, device=dev, dtype=torch.int32)
+    rk = torch.empty(1, R, d, device=dev)
+    rv = torch.empty(1, R, dv, device=dev)
+    rw = torch.empty(1, R, device=dev)
+    if R > 0:
+        t = draw_tables(seed=seed, batch=1, heads=1, n=n, d=d, block_size=block_size, compressor=compressor,
+                        device=dev)
+        with torch.cuda.device(dev):
+            _lib.call("sa_compress_blocks", k3.data_ptr(), v3.data_ptr(), 1, n, d, dv, block_size,
+                      _lib.COMPRESSORS[compressor], _ptr(t.dirs), _ptr(t.coins), _ptr(t.perms), idx.data_ptr(),
+                      rk.data_ptr(), rv.data_ptr(), rw.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+    active = ((torch.arange(R, device=dev) // m + 1) * block_size).to(torch.long)
+    return BlockReps(rk[0].to(k.dtype), rv[0].to(v.dtype), rw[0].to(k.dtype), active, idx[0])

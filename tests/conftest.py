@@ -1,0 +1,34 @@
+"""Shared pytest configuration.
+
+Tests marked ``gpu`` need a CUDA device and the built sm_100a library; the
+rest run on CPU only (oracle vs. golden fixtures, host logic, the C-ABI symbol
+table and the gloo multi-process paths).
+"""
+
+import json
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200) and the built CUDA library")
+
+
+def load_golden(name):
+    z = np.load(os.path.join(GOLDEN, name + ".npz"))
+    d = {key: z[key] for key in z.files}
+    d["meta"] = json.loads(bytes(d["meta"]).decode())
+    return d
+
+
+def golden_names():
+    return sorted(f[:-4] for f in os.listdir(GOLDEN)
+                  if f.endswith(".npz") and f not in ("misc.npz",) and not f.startswith("stream_"))

@@ -1,0 +1,92 @@
+"""Host-side logic on CPU: draw tables, stats formulas, argument checks."""
+
+import numpy as np
+import pytest
+import torch
+
+import streaming_attention_b200 as sa
+from conftest import golden_names, load_golden
+from oracle import oracle as O
+from streaming_attention_b200 import draws, fast
+
+
+@pytest.mark.parametrize("comp,bs", [("sorted_pair", 16), ("sorted_pair", 33), ("sorted_pair", 2),
+                                     ("random", 16), ("random", 1)])
+def test_draw_tables_replay_the_reference_stream(comp, bs):
+    B, H, n, d, seed = 2, 3, 150, 6, 5
+    t = draws.draw_tables(seed=seed, batch=B, heads=H, n=n, d=d, block_size=bs, compressor=comp,
+                          device=torch.device("cpu"), cache=False)
+    nc = (n - 1) // bs
+    assert t.completed_blocks == nc
+    for b in range(B):
+        for h in range(H):
+            ref = O.block_draws(seed + b * H + h, n, d, bs, comp)
+            assert len(ref) == nc
+            for c, dr in enumerate(ref):
+                if dr.perm is not None:
+                    np.testing.assert_array_equal(t.perms[b * H + h, c].numpy(), dr.perm)
+                else:
+                    np.testing.assert_array_equal(t.dirs[b * H + h, c].numpy(), dr.direction)
+                    np.testing.assert_array_equal(t.coins[b * H + h, c].numpy(), dr.u)
+
+
+def test_draw_tables_head_range_is_a_slice_of_the_full_grid():
+    kw = dict(seed=3, batch=2, heads=4, n=100, d=5, block_size=10, compressor="sorted_pair",
+              device=torch.device("cpu"), cache=False)
+    full = draws.draw_tables(**kw)
+    part = draws.draw_tables(head_range=(3, 6), **kw)
+    assert torch.equal(full.dirs[3:6], part.dirs)
+    assert torch.equal(full.coins[3:6], part.coins)
+
+
+@pytest.mark.parametrize("name", [n for n in golden_names() if load_golden(n)["meta"]["degree"] <= 2])
+def test_stats_formula_matches_reference(name):
+    g = load_golden(name)
+    m = g["meta"]
+    if not m["stats"]:
+        pytest.skip("no stats recorded")
+    n, d = g["q"].shape[2:]
+    dv = g["v"].shape[-1]
+    # the fixture ran the reference on CPU with low_mode="stream"
+    st = fast._stats(n, d, dv, m["degree"], m["bs"], m["compressor"], "stream", 2048, 4)
+    for key, val in m["stats"].items():
+        assert getattr(st, key) == val, key
+
+
+def test_num_taylor_features():
+    assert sa.num_taylor_features(64, 2) == 2145
+    assert sa.num_taylor_features(16, 3) == 969
+    with pytest.raises(NotImplementedError):
+        sa.num_taylor_features(8, 4)
+    with pytest.raises(ValueError):
+        sa.num_taylor_features(8, -1)
+
+
+def test_argument_errors_match_reference_messages():
+    q = torch.zeros(8, 4)
+    f = sa.fast_article_causal_attention
+    with pytest.raises(ValueError, match=r"q,k,v must have shapes"):
+        f(q, q[0], q)
+    with pytest.raises(ValueError, match="same shape"):
+        f(q, torch.zeros(8, 5), q)
+    with pytest.raises(ValueError, match="same sequence length"):
+        f(q, q, torch.zeros(7, 4))
+    with pytest.raises(ValueError, match="query_chunk_size must be positive"):
+        f(q, q, q, query_chunk_size=0)
+    with pytest.raises(ValueError, match="block_size must be positive"):
+        f(q, q, q, block_size=0)
+    with pytest.raises(ValueError, match="mode must be one of"):
+        f(q, q, q, low_mode="fast")
+    with pytest.raises(NotImplementedError):
+        f(q, q, q, degree=4)
+    with pytest.raises(ValueError, match="compressor must be one of"):
+        f(q, q, q, compressor="bogus", block_size=2)
+    with pytest.raises(ValueError, match=r"q/k/v must be \[N,D\] or \[B,H,N,D\]"):
+        f(q[None], q[None], q[None])
+    with pytest.raises(ValueError, match="identical shape"):
+        f(q[None, None], q[None, None, :4], q[None, None])
+    with pytest.raises(ValueError, match=r"v must have shape \[B,H,N,Dv\]"):
+        f(q[None, None], q[None, None], q[None, None, :7])
+    # CPU tensors: no CPU fallback
+    with pytest.raises(ValueError, match="CUDA"):
+        f(q, q, q)
