@@ -175,7 +175,7 @@ def fp32_fma_peak_tflops(dev: torch.device) -> float:
     from cuda.bindings import driver, nvrtc
 
     prog = nvrtc.nvrtcCreateProgram(_FMA_SRC.encode(), b"fma_probe.cu", 0, [], [])[1]
-    opts = [b"--gpu-architecture=sm_100a", b"-O3"]
+    opts = [b"--gpu-architecture=sm_100a"]
     if nvrtc.nvrtcCompileProgram(prog, len(opts), opts)[0] != nvrtc.nvrtcResult.NVRTC_SUCCESS:
         return float("nan")
     size = nvrtc.nvrtcGetCUBINSize(prog)[1]
