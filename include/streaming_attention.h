@@ -118,6 +118,26 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
                       float* out, int32_t* rep_idx, void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/* Bytes of the library's built-in device scratch (per GPU). */
+#define SA_STATIC_SCRATCH_BYTES (64u * 1024u * 1024u)
+
+/* sa_fast_attention for callers that cannot allocate device memory.  It has
+ * no counterpart in the reference; it exists for callers such as programs
+ * whose device memory belongs entirely to another allocator, serving loops
+ * that forbid cudaMalloc after start-up, or plain-C callers with no device
+ * allocator.  Same arguments and result as sa_fast_attention, minus the
+ * workspace: the scratch is a SA_STATIC_SCRATCH_BYTES array built into the
+ * library, held by every GPU that loads it until the process exits.  Problems
+ * whose sa_fast_attention_workspace_size exceeds it are rejected with
+ * SA_ERR_INVALID_ARG.  The first call on each device looks up the array's
+ * address (make it before any stream capture).  All calls share the array:
+ * calls that overlap on the GPU race, so order them.  Allocates nothing. */
+int sa_fast_attention_static_scratch(const float* q, const float* k, const float* v, int64_t bh,
+                                     int64_t n, int d, int dv, int degree, int block_size,
+                                     float scale, int compressor, const float* dirs,
+                                     const float* coins, const int32_t* perms, float eps,
+                                     float* out, int32_t* rep_idx, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

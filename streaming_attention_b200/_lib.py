@@ -41,6 +41,8 @@ SIGNATURES = {
     "sa_fast_attention_workspace_size": [_i64, _i64, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(_sz)],
     "sa_fast_attention": [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _vp, _vp, _f32, _vp,
                           _vp, _vp, _sz, _vp],
+    "sa_fast_attention_static_scratch": [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _vp,
+                                         _vp, _f32, _vp, _vp, _vp],
 }
 
 _lock = threading.Lock()
