@@ -55,7 +55,17 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-heads", type=int, default=0, help="heads in the CPU sample (0 = auto)")
+    ap.add_argument("--bh", type=int, default=0,
+                    help="profiling only: replace B*H by this many sequences (B=1) to make a small case")
     return ap.parse_args()
+
+
+def bench_config(args) -> dict:
+    from streaming_attention_b200 import workloads
+
+    if args.bh:
+        return workloads.config(args.config, B=1, H=args.bh)
+    return workloads.config(args.config)
 
 
 # ---------------------------------------------------------------------------
@@ -279,7 +289,7 @@ def run_ours(args, rank, world, dev):
     import streaming_attention_b200 as sa
     from streaming_attention_b200 import _lib, workloads
 
-    c = workloads.config(args.config)
+    c = bench_config(args)
     bh_total = c["B"] * c["H"]
     if bh_total % world:
         raise SystemExit(f"B*H={bh_total} does not split over {world} GPUs")
@@ -440,7 +450,7 @@ def run_reference(args, rank, world):
 
     if rank != 0:
         return None
-    c = workloads.config(args.config)
+    c = bench_config(args)
     heads = args.cpu_sample_heads or auto_sample_heads(c, 2.0)
     for _ in range(args.warmup):
         cpu_sample(c, heads)
