@@ -70,7 +70,7 @@ def build(force: bool = False, verbose: bool = False, jobs: int = 8) -> str:
             _drain(procs)
     _drain(procs)
     tmp = LIB + ".tmp"
-    cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp, *objs, "-lcuda"]
+    cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp, *objs]
     if verbose:
         print(" ".join(cmd), flush=True)
     out = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)

@@ -5,8 +5,10 @@
 // SA_ERR_INVALID_ARG with a message; every CUDA error is caught here and
 // returned as SA_ERR_CUDA.  No entry point allocates device memory: outputs
 // and scratch belong to the caller.
+#include <cuda.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "sa_common.cuh"
@@ -15,7 +17,13 @@ namespace sa {
 
 int launch_compress(const float* k, const float* v, int64_t bh, int64_t n, int d, int dv, int bs, int compressor,
                     const float* dirs, const float* coins, const int32_t* perms, int32_t* rep_idx, float* rep_k,
-                    float* rep_v, float* rep_w, cudaStream_t stream);
+                    float* rep_v, float* rep_w, SplitOut sp, cudaStream_t stream);
+int launch_split(const float* src, int64_t rows, int cols, int cols_pad, float* hi, float* lo, cudaStream_t stream);
+int residual_tc_dp(int d);
+int residual_tc_dvp(int dv);
+int launch_residual_tc(const CUtensorMap* maps, const float* q, const float* rep_w, int64_t r_pad, const float* low,
+                       float* out, int* status, int64_t bh, int64_t n, int d, int dv, int degree, int bs,
+                       int64_t m_blk, float scale, float eps, cudaStream_t stream);
 int launch_low_moments(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d, int dv,
                        int degree, int bs, float scale, float* low, cudaStream_t stream);
 int launch_residual(const float* q, const float* k, const float* v, const float* rk, const float* rv,
@@ -64,27 +72,93 @@ int check_compressor(int c) {
 constexpr size_t kAlign = 256;
 inline size_t align_up(size_t x) { return (x + kAlign - 1) & ~(kAlign - 1); }
 
+// Workspace layout.  Offset 0 always holds the launch status word (int, 0 = ok).
+// Tensor-core path (d <= 64, dv <= 128): tf32 hi / fp32 remainder copies of
+// k, v (padded to dp / dvp columns) and of the gathered reps; rep weights
+// padded per sequence to a multiple of 64.  SIMT path: raw reps.
 struct Workspace {
-  size_t low, rep_k, rep_v, rep_w, rep_idx, total;
+  bool tc = false;
+  int dp = 0, dvp = 0;
+  int64_t R = 0, r_pad = 0;
+  size_t status = 0, low = 0, khi = 0, klo = 0, vhi = 0, vlo = 0;
+  size_t rkhi = 0, rklo = 0, rvhi = 0, rvlo = 0, rep_k = 0, rep_v = 0, rep_w = 0, rep_idx = 0, total = 0;
 };
 
 Workspace plan(int64_t bh, int64_t n, int d, int dv, int bs, int compressor) {
   Workspace w{};
-  size_t off = 0;
-  w.low = off;
-  off = align_up(off + (size_t)bh * n * (dv + 1) * sizeof(float));
+  w.dp = residual_tc_dp(d);
+  w.dvp = residual_tc_dvp(dv);
+  // SA_FORCE_SIMT=1 selects the CUDA-core kernels for every shape (A/B comparisons)
+  const char* force = getenv("SA_FORCE_SIMT");
+  w.tc = w.dp > 0 && w.dvp > 0 && !(force && force[0] == '1');
   const int64_t nc = n > 0 ? (n - 1) / bs : 0;
-  const int64_t R = (compressor == SA_COMPRESSOR_NONE) ? 0 : nc * ((bs + 1) / 2);
-  w.rep_k = off;
-  off = align_up(off + (size_t)bh * R * d * sizeof(float));
-  w.rep_v = off;
-  off = align_up(off + (size_t)bh * R * dv * sizeof(float));
-  w.rep_w = off;
-  off = align_up(off + (size_t)bh * R * sizeof(float));
-  w.rep_idx = off;
-  off = align_up(off + (size_t)bh * R * sizeof(int32_t));
+  w.R = (compressor == SA_COMPRESSOR_NONE) ? 0 : nc * ((bs + 1) / 2);
+  w.r_pad = (w.R + 63) / 64 * 64;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align_up(off + bytes);
+    return at;
+  };
+  const size_t f = sizeof(float);
+  w.status = take(sizeof(int));
+  w.low = take((size_t)bh * n * (dv + 1) * f);
+  if (w.tc) {
+    w.khi = take((size_t)bh * n * w.dp * f);
+    w.klo = take((size_t)bh * n * w.dp * f);
+    w.vhi = take((size_t)bh * n * w.dvp * f);
+    w.vlo = take((size_t)bh * n * w.dvp * f);
+    w.rkhi = take((size_t)bh * w.R * w.dp * f);
+    w.rklo = take((size_t)bh * w.R * w.dp * f);
+    w.rvhi = take((size_t)bh * w.R * w.dvp * f);
+    w.rvlo = take((size_t)bh * w.R * w.dvp * f);
+    w.rep_w = take((size_t)bh * w.r_pad * f);
+  } else {
+    w.rep_k = take((size_t)bh * w.R * d * f);
+    w.rep_v = take((size_t)bh * w.R * dv * f);
+    w.rep_w = take((size_t)bh * w.R * f);
+  }
+  w.rep_idx = take((size_t)bh * w.R * sizeof(int32_t));
   w.total = off;
   return w;
+}
+
+// 3-D tensor map over a [outer, rows, inner] fp32 array; box {32, box_rows, 1},
+// 128-byte swizzle, zero fill out of bounds.
+// The driver's tensor-map encoder, looked up at run time so that the library
+// loads on machines without a driver (the CPU-side tests only load it).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+int encode_map_3d(CUtensorMap* map, const void* base, int inner, int64_t rows, int64_t outer, int box_rows,
+                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)(rows > 0 ? rows : 1), (cuuint64_t)(outer > 0 ? outer : 1)};
+  cuuint64_t strides[2] = {(cuuint64_t)inner * 4, (cuuint64_t)inner * 4 * (cuuint64_t)(rows > 0 ? rows : 1)};
+  cuuint32_t box[3] = {32, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return set_error(SA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(SA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return SA_OK;
 }
 
 }  // namespace
@@ -128,7 +202,7 @@ int sa_compress_blocks(const float* k, const float* v, int64_t bh, int64_t n, in
   if (compressor == SA_COMPRESSOR_NONE)
     return set_error(SA_ERR_INVALID_ARG, "compressor none keeps every key; nothing to compress");
   return launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, rep_idx, rep_k, rep_v,
-                         rep_w, (cudaStream_t)stream);
+                         rep_w, SplitOut{}, (cudaStream_t)stream);
 }
 
 int sa_low_moments(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d, int dv, int degree,
@@ -183,25 +257,84 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
     return set_error(SA_ERR_INVALID_ARG, "workspace must be %zu-byte aligned", kAlign);
   char* ws = static_cast<char*>(workspace);
   float* low = reinterpret_cast<float*>(ws + w.low);
+  int* status = reinterpret_cast<int*>(ws + w.status);
   cudaStream_t s = (cudaStream_t)stream;
   const int64_t nc = (n - 1) / block_size;
-  const float* rk = k;
-  const float* rv = v;
-  const float* rw = nullptr;
-  if (compressor != SA_COMPRESSOR_NONE && nc > 0) {
-    float* rep_k = reinterpret_cast<float*>(ws + w.rep_k);
-    float* rep_v = reinterpret_cast<float*>(ws + w.rep_v);
-    float* rep_w = reinterpret_cast<float*>(ws + w.rep_w);
-    int32_t* ridx = rep_idx ? rep_idx : reinterpret_cast<int32_t*>(ws + w.rep_idx);
-    rc = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, ridx, rep_k, rep_v, rep_w, s);
+  const bool compress = compressor != SA_COMPRESSOR_NONE && nc > 0;
+  int32_t* ridx = rep_idx ? rep_idx : reinterpret_cast<int32_t*>(ws + w.rep_idx);
+  cudaError_t ce = cudaMemsetAsync(status, 0, sizeof(int), s);
+  if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "status reset: %s", cudaGetErrorString(ce));
+
+  if (!w.tc) {
+    const float* rk = k;
+    const float* rv = v;
+    const float* rw = nullptr;
+    if (compress) {
+      float* rep_k = reinterpret_cast<float*>(ws + w.rep_k);
+      float* rep_v = reinterpret_cast<float*>(ws + w.rep_v);
+      float* rep_w = reinterpret_cast<float*>(ws + w.rep_w);
+      rc = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, ridx, rep_k, rep_v, rep_w,
+                           SplitOut{}, s);
+      if (rc) return rc;
+      rk = rep_k;
+      rv = rep_v;
+      rw = rep_w;
+    }
+    rc = launch_low_moments(q, k, v, bh, n, d, dv, degree, block_size, scale, low, s);
     if (rc) return rc;
-    rk = rep_k;
-    rv = rep_v;
-    rw = rep_w;
+    return launch_residual(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, block_size, compressor, scale, eps, out,
+                           s);
+  }
+
+  // tensor-core path
+  float* khi = reinterpret_cast<float*>(ws + w.khi);
+  float* klo = reinterpret_cast<float*>(ws + w.klo);
+  float* vhi = reinterpret_cast<float*>(ws + w.vhi);
+  float* vlo = reinterpret_cast<float*>(ws + w.vlo);
+  rc = launch_split(k, bh * n, d, w.dp, khi, klo, s);
+  if (rc) return rc;
+  rc = launch_split(v, bh * n, dv, w.dvp, vhi, vlo, s);
+  if (rc) return rc;
+  float* rep_w = nullptr;
+  const float* maps_src[4] = {khi, klo, vhi, vlo};
+  int64_t rep_rows = n;
+  if (compress) {
+    SplitOut sp;
+    sp.khi = reinterpret_cast<float*>(ws + w.rkhi);
+    sp.klo = reinterpret_cast<float*>(ws + w.rklo);
+    sp.vhi = reinterpret_cast<float*>(ws + w.rvhi);
+    sp.vlo = reinterpret_cast<float*>(ws + w.rvlo);
+    sp.dp = w.dp;
+    sp.dvp = w.dvp;
+    sp.w_stride = w.r_pad;
+    rep_w = reinterpret_cast<float*>(ws + w.rep_w);
+    ce = cudaMemsetAsync(rep_w, 0, (size_t)bh * w.r_pad * sizeof(float), s);
+    if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "rep weight reset: %s", cudaGetErrorString(ce));
+    rc = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, ridx, nullptr, nullptr,
+                         rep_w, sp, s);
+    if (rc) return rc;
+    maps_src[0] = sp.khi;
+    maps_src[1] = sp.klo;
+    maps_src[2] = sp.vhi;
+    maps_src[3] = sp.vlo;
+    rep_rows = w.R;
   }
   rc = launch_low_moments(q, k, v, bh, n, d, dv, degree, block_size, scale, low, s);
   if (rc) return rc;
-  return launch_residual(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, block_size, compressor, scale, eps, out, s);
+  CUtensorMap maps[8];
+  const int widths[4] = {w.dp, w.dp, w.dvp, w.dvp};
+  const float* cur_src[4] = {khi, klo, vhi, vlo};
+  for (int j = 0; j < 4; ++j) {
+    // K tiles: K-major, 128-byte swizzle; V tiles: MN-major, 128-byte swizzle with 32-byte atoms
+    const CUtensorMapSwizzle sw = j < 2 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    rc = encode_map_3d(&maps[j], maps_src[j], widths[j], rep_rows, bh, 64, sw);
+    if (rc) return rc;
+    rc = encode_map_3d(&maps[4 + j], cur_src[j], widths[j], n, bh, 64, sw);
+    if (rc) return rc;
+  }
+  const int64_t m_blk = compressor == SA_COMPRESSOR_NONE ? block_size : (block_size + 1) / 2;
+  return launch_residual_tc(maps, q, rep_w, w.r_pad, low, out, status, bh, n, d, dv, degree, block_size, m_blk,
+                            scale, eps, s);
 }
 
 }  // extern "C"

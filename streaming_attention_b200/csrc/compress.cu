@@ -39,7 +39,7 @@ compress_blocks_kernel(const float* __restrict__ k, const float* __restrict__ v,
                        int bs, int nc, int m, int pow2, int use_perm, const float* __restrict__ dirs,
                        const float* __restrict__ coins, const int32_t* __restrict__ perms,
                        int32_t* __restrict__ rep_idx, float* __restrict__ rep_k, float* __restrict__ rep_v,
-                       float* __restrict__ rep_w) {
+                       float* __restrict__ rep_w, const SplitOut sp) {
   extern __shared__ unsigned char smem_raw[];
   unsigned long long* skey = reinterpret_cast<unsigned long long*>(smem_raw);
   int* sidx = reinterpret_cast<int*>(skey + pow2);
@@ -115,9 +115,10 @@ compress_blocks_kernel(const float* __restrict__ k, const float* __restrict__ v,
 
   // write the selection and gather the rep rows (one warp per rep)
   const int64_t rbase = h * (int64_t)nc * m + (int64_t)c * m;
+  const int64_t wbase = h * sp.w_stride + (int64_t)c * m;
   for (int p = tid; p < m; p += blockDim.x) {
     if (rep_idx) rep_idx[rbase + p] = (int32_t)(start + sel[p]);
-    if (rep_w) rep_w[rbase + p] = selw[p];
+    if (rep_w) rep_w[wbase + p] = selw[p];
   }
   const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   for (int p = warp; p < m; p += nwarps) {
@@ -126,6 +127,36 @@ compress_blocks_kernel(const float* __restrict__ k, const float* __restrict__ v,
       for (int a = lane; a < d; a += 32) rep_k[(rbase + p) * d + a] = __ldg(k + src * d + a);
     if (rep_v)
       for (int a = lane; a < dv; a += 32) rep_v[(rbase + p) * dv + a] = __ldg(v + src * dv + a);
+    if (sp.khi) {
+      for (int a = lane; a < sp.dp; a += 32) {
+        const float x = a < d ? __ldg(k + src * d + a) : 0.0f;
+        const float hi = __uint_as_float(tc_split_hi(x));
+        sp.khi[(rbase + p) * sp.dp + a] = hi;
+        sp.klo[(rbase + p) * sp.dp + a] = x - hi;
+      }
+      for (int a = lane; a < sp.dvp; a += 32) {
+        const float x = a < dv ? __ldg(v + src * dv + a) : 0.0f;
+        const float hi = __uint_as_float(tc_split_hi(x));
+        sp.vhi[(rbase + p) * sp.dvp + a] = hi;
+        sp.vlo[(rbase + p) * sp.dvp + a] = x - hi;
+      }
+    }
+  }
+}
+
+// Split rows of a [rows, cols] fp32 matrix into tf32 hi and fp32 remainder
+// arrays of width cols_pad (zero padded), the operand format of the
+// tensor-core residual.
+__global__ void split_rows_kernel(const float* __restrict__ src, int64_t rows, int cols, int cols_pad,
+                                  float* __restrict__ hi, float* __restrict__ lo) {
+  const int64_t total = rows * cols_pad;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = e / cols_pad;
+    const int c = (int)(e - r * cols_pad);
+    const float x = c < cols ? __ldg(src + r * cols + c) : 0.0f;
+    const float h = __uint_as_float(tc_split_hi(x));
+    hi[e] = h;
+    lo[e] = x - h;
   }
 }
 
@@ -133,10 +164,11 @@ compress_blocks_kernel(const float* __restrict__ k, const float* __restrict__ v,
 
 int launch_compress(const float* k, const float* v, int64_t bh, int64_t n, int d, int dv, int bs, int compressor,
                     const float* dirs, const float* coins, const int32_t* perms, int32_t* rep_idx, float* rep_k,
-                    float* rep_v, float* rep_w, cudaStream_t stream) {
+                    float* rep_v, float* rep_w, SplitOut sp, cudaStream_t stream) {
   const int64_t nc = n > 0 ? (n - 1) / bs : 0;
   const int m = (bs + 1) / 2;
   if (nc == 0 || bh == 0) return SA_OK;
+  if (sp.w_stride == 0) sp.w_stride = nc * m;
   if (nc > 2147483647LL || bh > 65535) return set_error(SA_ERR_UNSUPPORTED, "too many blocks or heads for one launch");
   const bool use_perm = (compressor == SA_COMPRESSOR_RANDOM) || bs <= 2;
   if (use_perm && !perms) return set_error(SA_ERR_INVALID_ARG, "perms table is required");
@@ -151,8 +183,17 @@ int launch_compress(const float* k, const float* v, int64_t bh, int64_t n, int d
   dim3 grid((unsigned)nc, (unsigned)bh);
   compress_blocks_kernel<<<grid, kCompressThreads, smem, stream>>>(k, v, n, d, dv, bs, (int)nc, m, pow2,
                                                                    use_perm ? 1 : 0, dirs, coins, perms, rep_idx,
-                                                                   rep_k, rep_v, rep_w);
+                                                                   rep_k, rep_v, rep_w, sp);
   return check_launch("compress_blocks_kernel");
+}
+
+int launch_split(const float* src, int64_t rows, int cols, int cols_pad, float* hi, float* lo, cudaStream_t stream) {
+  if (rows == 0) return SA_OK;
+  const int64_t total = rows * cols_pad;
+  const int threads = 256;
+  const int64_t blocks = min((total + threads - 1) / threads, (int64_t)148 * 16);
+  split_rows_kernel<<<(unsigned)blocks, threads, 0, stream>>>(src, rows, cols, cols_pad, hi, lo);
+  return check_launch("split_rows_kernel");
 }
 
 }  // namespace sa

@@ -1,0 +1,410 @@
+// Residual (tail) + combine on the 5th-generation tensor cores (tcgen05, TMEM, TMA).
+//
+// Same mathematics as residual.cu (fast_article_attention.py:437-514 and the
+// combine at :596-598): for query i in block c,
+//   num_i = low_i + sum_{reps of blocks < c} w_r (exp(x) - P_t(x)) v_r
+//                 + sum_{j in block c, j <= i} exp(x) v_j ,   x = scale q_i.k
+// and den_i the same with v -> 1; out_i = num_i / max(den_i, eps).
+//
+// One CTA per (128-query tile, sequence).  Key material streams in tiles of
+// 64 rows: first the coreset reps of the blocks before the tile, then the keys
+// of the current block(s).  Roles:
+//   warp 0      TMA producer: K_hi, K_lo, V_hi, V_lo (+ rep weights) per stage
+//   warp 1      TMEM owner; lane 0 issues every tcgen05.mma and commit
+//   warps 2..5  one query row per thread (TMEM lane): write the scaled query
+//               into TMEM, turn each S tile into P = f(S), then the epilogue
+// Precision: 3xTF32.  Every fp32 operand x is carried as hi = rna_tf32(x) and
+// lo = x - hi, and each product uses hi*hi + hi*lo + lo*hi, which keeps the
+// result within a few fp32 ulps (a single TF32 product loses ~11 bits).
+// Q (hi/lo) lives in TMEM as the A operand of S = Q K^T; P (hi/lo) is written
+// back to TMEM in place of S and is the A operand of O += P V.  K tiles are
+// K-major (128-byte swizzle); V tiles are MN-major (128-byte swizzle with
+// 32-byte atoms, the MN-major tf32 layout), both written by TMA.
+#include <math.h>
+
+#include "sa_common.cuh"
+#include "tc_util.cuh"
+
+namespace sa {
+
+namespace {
+
+using namespace tc;
+
+constexpr int kRowsQ = 128;    // queries per CTA = UMMA M
+constexpr int kTile = 64;      // keys per tile = N of S = K of PV
+constexpr int kThreads = 192;
+
+// status codes written to the launch's status word
+constexpr int kErrWaitQ = 101, kErrWaitFull = 102, kErrWaitSfree = 103, kErrWaitP = 104, kErrWaitS = 105,
+              kErrWaitEmpty = 106, kErrWaitO = 107, kErrDrain = 108;
+
+struct ResTCParams {
+  const float* q;        // [bh, n, d] raw queries
+  const float* rep_w;    // [bh, r_pad] rep weights (nullptr: every weight is 1)
+  const float* low;      // [bh, n, dv+1]
+  float* out;            // [bh, n, dv]
+  int* status;           // launch status word (0 = ok)
+  int64_t n;
+  int64_t m_blk;         // reps per completed block
+  int64_t r_pad;         // per-sequence stride of rep_w
+  int d, dv, bs;
+  float scale, eps;
+};
+
+template <int DP, int DVP>
+struct Layout {
+  static constexpr uint32_t kKT = DP * kTile * 4;   // one K tile (hi or lo)
+  static constexpr uint32_t kVT = DVP * kTile * 4;  // one V tile
+  static constexpr uint32_t kStage = 2 * kKT + 2 * kVT;
+  static constexpr int kStages = (200u * 1024u / kStage) >= 4 ? 4 : (int)(200u * 1024u / kStage);
+  static_assert(kStages >= 2, "at least double buffering");
+  static constexpr uint32_t kW = kStages * kTile * 4;
+  // TMEM columns
+  static constexpr uint32_t kQhi = 0, kQlo = DP;
+  static constexpr uint32_t kS0 = 2 * DP;           // buffer b: S/P_hi at kS0 + 128 b, P_lo at kS0 + 128 b + 64
+  static constexpr uint32_t kO = 2 * DP + 256;
+  static_assert(kO + DVP <= 512, "TMEM columns");
+  static constexpr uint32_t kSmemBytes = kStages * kStage + kW + (2 * kStages + 10) * 8 + 64 + 1024;
+};
+
+template <int DEG>
+__device__ __forceinline__ float taylor_t(float x) {
+  // the reference's term recurrence (fast_article_attention.py:95-104)
+  float out = 1.0f;
+  if (DEG >= 1) {
+    float term = x;
+    out = out + term;
+    if (DEG >= 2) {
+      term = term * x * 0.5f;
+      out = out + term;
+      if (DEG >= 3) {
+        term = __fdiv_rn(term * x, 3.0f);
+        out = out + term;
+      }
+    }
+  }
+  return out;
+}
+
+template <int DP, int DVP, int DEG>
+__global__ void __launch_bounds__(kThreads, 1)
+residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_constant__ CUtensorMap tm_rkl,
+                   const __grid_constant__ CUtensorMap tm_rvh, const __grid_constant__ CUtensorMap tm_rvl,
+                   const __grid_constant__ CUtensorMap tm_kh, const __grid_constant__ CUtensorMap tm_kl,
+                   const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl,
+                   const ResTCParams p) {
+  using L = Layout<DP, DVP>;
+  constexpr int kStages = L::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* wbuf = reinterpret_cast<float*>(smem + kStages * L::kStage);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * L::kStage + L::kW);
+  uint64_t* full = bars;                 // [kStages]
+  uint64_t* empty = bars + kStages;      // [kStages]
+  uint64_t* sfull = bars + 2 * kStages;  // [2]
+  uint64_t* pfull = sfull + 2;           // [2]
+  uint64_t* sfree = pfull + 2;           // [2]
+  uint64_t* qready = sfree + 2;
+  uint64_t* ofull = qready + 1;
+  uint64_t* drain = ofull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* abort_word = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t h = blockIdx.y;
+  // heavy query tiles (late in the sequence) first
+  const int64_t n_qt = (p.n + kRowsQ - 1) / kRowsQ;
+  const int64_t qt = n_qt - 1 - blockIdx.x;
+  const int64_t q0 = qt * kRowsQ;
+  const int64_t q_last = min(q0 + kRowsQ, p.n) - 1;
+  const int64_t c_first = q0 / p.bs, c_last = q_last / p.bs;
+  const int64_t r_end = c_last * p.m_blk;
+  const int n_rep = (int)((r_end + kTile - 1) / kTile);
+  const int64_t kb0 = c_first * p.bs;
+  const int n_cur = (int)((q_last + 1 - kb0 + kTile - 1) / kTile);
+  const int T = n_rep + n_cur;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sfull[b], 1);
+      mbar_init(&pfull[b], 128);
+      mbar_init(&sfree[b], 1);
+    }
+    mbar_init(qready, 128);
+    mbar_init(ofull, 1);
+    mbar_init(drain, 1);
+    *abort_word = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const Abort ab{abort_word, p.status};
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_rkh);
+      tma_prefetch_desc(&tm_kh);
+      int issued = 0;
+      for (int t = 0; t < T; ++t) {
+        const int s = t % kStages;
+        if (t >= kStages && !mbar_wait(&empty[s], ((t / kStages) - 1) & 1, ab, kErrWaitEmpty)) break;
+        const bool rep = t < n_rep;
+        const int row0 = rep ? t * kTile : (int)(kb0 + (int64_t)(t - n_rep) * kTile);
+        const bool with_w = rep && p.rep_w != nullptr;
+        mbar_arrive_expect_tx(&full[s], L::kStage + (with_w ? kTile * 4 : 0));
+        uint8_t* st = smem + s * L::kStage;
+        const CUtensorMap* mkh = rep ? &tm_rkh : &tm_kh;
+        const CUtensorMap* mkl = rep ? &tm_rkl : &tm_kl;
+        const CUtensorMap* mvh = rep ? &tm_rvh : &tm_vh;
+        const CUtensorMap* mvl = rep ? &tm_rvl : &tm_vl;
+#pragma unroll
+        for (int a = 0; a < DP / 32; ++a) {
+          tma_load_3d(st + a * (kTile * 128), mkh, &full[s], a * 32, row0, (int)h);
+          tma_load_3d(st + L::kKT + a * (kTile * 128), mkl, &full[s], a * 32, row0, (int)h);
+        }
+#pragma unroll
+        for (int a = 0; a < DVP / 32; ++a) {
+          tma_load_3d(st + 2 * L::kKT + a * (kTile * 128), mvh, &full[s], a * 32, row0, (int)h);
+          tma_load_3d(st + 2 * L::kKT + L::kVT + a * (kTile * 128), mvl, &full[s], a * 32, row0, (int)h);
+        }
+        if (with_w) bulk_load(wbuf + s * kTile, p.rep_w + h * p.r_pad + row0, kTile * 4, &full[s]);
+        ++issued;
+      }
+      // never leave with copies in flight: the last use of each stage must have landed
+      for (int t = max(0, issued - kStages); t < issued; ++t) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full[t % kStages], (t / kStages) & 1)) {
+          if (globaltimer_ns() - t0 > 1000000000ull) {
+            atomicCAS(p.status, 0, kErrDrain);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_tf32(128, kTile, false, false);
+      constexpr uint32_t idesc_pv = idesc_tf32(128, DVP, false, true);
+      bool ok = mbar_wait(qready, 0, ab, kErrWaitQ);
+      if (ok) tc_fence_after();
+      auto issue_pv = [&](int tp) -> bool {
+        const int sp = tp % kStages, bp = tp & 1;
+        if (!mbar_wait(&pfull[bp], (tp >> 1) & 1, ab, kErrWaitP)) return false;
+        tc_fence_after();
+        const uint32_t vh = smem_u32(smem + sp * L::kStage + 2 * L::kKT);
+        const uint32_t vl = vh + L::kVT;
+        const uint32_t ph = tmem + L::kS0 + 128 * bp;
+        const uint32_t pl = ph + 64;
+#pragma unroll
+        for (int kk = 0; kk < kTile / 8; ++kk) {
+          const uint64_t bh_ = sdesc_sw128_atom32(vh + kk * 1024, kTile * 128, 512);
+          const uint64_t bl_ = sdesc_sw128_atom32(vl + kk * 1024, kTile * 128, 512);
+          mma_tf32_ts(tmem + L::kO, ph + kk * 8, bh_, idesc_pv, (tp > 0 || kk > 0) ? 1u : 0u);
+          mma_tf32_ts(tmem + L::kO, ph + kk * 8, bl_, idesc_pv, 1u);
+          mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
+        }
+        mma_commit(&empty[sp]);
+        mma_commit(&sfree[bp]);
+        return true;
+      };
+      for (int t = 0; ok && t < T; ++t) {
+        const int s = t % kStages, b = t & 1;
+        if (!mbar_wait(&full[s], (t / kStages) & 1, ab, kErrWaitFull)) { ok = false; break; }
+        if (t >= 2 && !mbar_wait(&sfree[b], ((t >> 1) - 1) & 1, ab, kErrWaitSfree)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t kh = smem_u32(smem + s * L::kStage);
+        const uint32_t kl = kh + L::kKT;
+        const uint32_t dS = tmem + L::kS0 + 128 * b;
+#pragma unroll
+        for (int kk = 0; kk < DP / 8; ++kk) {
+          const uint32_t off = (kk >> 2) * (kTile * 128) + (kk & 3) * 32;
+          const uint64_t bh_ = sdesc_sw128(kh + off, 16, 1024);
+          const uint64_t bl_ = sdesc_sw128(kl + off, 16, 1024);
+          mma_tf32_ts(dS, tmem + L::kQhi + kk * 8, bh_, idesc_qk, kk > 0 ? 1u : 0u);
+          mma_tf32_ts(dS, tmem + L::kQhi + kk * 8, bl_, idesc_qk, 1u);
+          mma_tf32_ts(dS, tmem + L::kQlo + kk * 8, bh_, idesc_qk, 1u);
+        }
+        mma_commit(&sfull[b]);
+        if (t >= 1 && !issue_pv(t - 1)) { ok = false; break; }
+      }
+      if (ok && T > 0) ok = issue_pv(T - 1);
+      if (ok) mma_commit(ofull);
+      // drain: nothing of ours may still write TMEM when it is freed
+      mma_commit(drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0)) {
+        if (globaltimer_ns() - t0 > 2000000000ull) {
+          atomicCAS(p.status, 0, kErrDrain);
+          break;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ query rows
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int64_t i = q0 + row;
+    const bool valid = i < p.n;
+    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    // scaled query, split hi/lo, into TMEM
+    {
+      const float* qr = p.q + (h * p.n + (valid ? i : 0)) * p.d;
+#pragma unroll
+      for (int cchunk = 0; cchunk < DP / 32; ++cchunk) {
+        uint32_t hi[32], lo[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int a = cchunk * 32 + j;
+          const float x = (valid && a < p.d) ? __ldg(qr + a) * p.scale : 0.0f;
+          hi[j] = to_tf32(x);
+          lo[j] = __float_as_uint(x - __uint_as_float(hi[j]));
+        }
+        tmem_st32(lane_addr + L::kQhi + cchunk * 32, hi);
+        tmem_st32(lane_addr + L::kQlo + cchunk * 32, lo);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(qready);
+    }
+    const int64_t ci = valid ? i / p.bs : 0;
+    const int64_t lim = valid ? ci * p.m_blk : 0;    // reps r < lim are active for this query
+    const int64_t bst = valid ? ci * p.bs : p.n;      // first key of this query's block
+    float den = 0.0f;
+    bool ok = true;
+    for (int t = 0; t < T; ++t) {
+      const int s = t % kStages, b = t & 1;
+      if (!mbar_wait(&sfull[b], (t >> 1) & 1, ab, kErrWaitS)) { ok = false; break; }
+      const bool rep = t < n_rep;
+      const bool with_w = rep && p.rep_w != nullptr;
+      if (with_w && !mbar_wait(&full[s], (t / kStages) & 1, ab, kErrWaitFull)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t tS = lane_addr + L::kS0 + 128 * b;
+      const int64_t row0 = rep ? (int64_t)t * kTile : kb0 + (int64_t)(t - n_rep) * kTile;
+#pragma unroll
+      for (int cchunk = 0; cchunk < kTile / 32; ++cchunk) {
+        float sv[32];
+        tmem_ld32(tS + cchunk * 32, sv);
+        tmem_wait_ld();
+        uint32_t hi[32], lo[32];
+        const int64_t col0 = row0 + cchunk * 32;
+        if (rep) {
+          const float* w = with_w ? wbuf + s * kTile + cchunk * 32 : nullptr;
+          const bool all_on = col0 + 32 <= lim;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float x = sv[j];
+            float e = __expf(x) - taylor_t<DEG>(x);
+            if (w) e *= w[j];
+            if (!all_on && col0 + j >= lim) e = 0.0f;
+            den += e;
+            hi[j] = to_tf32(e);
+            lo[j] = __float_as_uint(e - __uint_as_float(hi[j]));
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int64_t key = col0 + j;
+            float e = __expf(sv[j]);
+            if (key > i || key < bst) e = 0.0f;
+            den += e;
+            hi[j] = to_tf32(e);
+            lo[j] = __float_as_uint(e - __uint_as_float(hi[j]));
+          }
+        }
+        tmem_st32(tS + cchunk * 32, hi);
+        tmem_st32(tS + 64 + cchunk * 32, lo);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&pfull[b]);
+    }
+    if (ok && mbar_wait(ofull, 0, ab, kErrWaitO)) {
+      tc_fence_after();
+      const float* lrow = p.low + (h * p.n + (valid ? i : 0)) * (int64_t)(p.dv + 1);
+      const float dtot = valid ? __ldg(lrow + p.dv) + den : 1.0f;
+      const float dmax = fmaxf(dtot, p.eps);
+      float* orow = p.out + (h * p.n + (valid ? i : 0)) * (int64_t)p.dv;
+#pragma unroll
+      for (int cchunk = 0; cchunk < DVP / 32; ++cchunk) {
+        float ov[32];
+        tmem_ld32(lane_addr + L::kO + cchunk * 32, ov);
+        tmem_wait_ld();
+        if (valid) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int col = cchunk * 32 + j;
+            if (col < p.dv) orow[col] = __fdiv_rn(ov[j] + __ldg(lrow + col), dmax);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int DP, int DVP, int DEG>
+int launch_tc(const CUtensorMap* maps, const ResTCParams& prm, int64_t bh, cudaStream_t stream) {
+  using L = Layout<DP, DVP>;
+  auto kern = residual_tc_kernel<DP, DVP, DEG>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kSmemBytes);
+  if (e != cudaSuccess) return set_error(SA_ERR_CUDA, "residual_tc smem attribute: %s", cudaGetErrorString(e));
+  dim3 grid((unsigned)((prm.n + kRowsQ - 1) / kRowsQ), (unsigned)bh);
+  kern<<<grid, kThreads, L::kSmemBytes, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], maps[6],
+                                                  maps[7], prm);
+  return check_launch("residual_tc_kernel");
+}
+
+template <int DP, int DVP>
+int launch_deg(int degree, const CUtensorMap* maps, const ResTCParams& prm, int64_t bh, cudaStream_t s) {
+  switch (degree) {
+    case 0: return launch_tc<DP, DVP, 0>(maps, prm, bh, s);
+    case 1: return launch_tc<DP, DVP, 1>(maps, prm, bh, s);
+    case 2: return launch_tc<DP, DVP, 2>(maps, prm, bh, s);
+    default: return launch_tc<DP, DVP, 3>(maps, prm, bh, s);
+  }
+}
+
+}  // namespace
+
+// Padded widths the tensor-core residual uses (0 if the shape is not supported).
+int residual_tc_dp(int d) { return d <= 32 ? 32 : (d <= 64 ? 64 : 0); }
+int residual_tc_dvp(int dv) { return dv <= 32 ? 32 : (dv <= 64 ? 64 : (dv <= 128 ? 128 : 0)); }
+
+// maps: rep_k_hi, rep_k_lo, rep_v_hi, rep_v_lo, k_hi, k_lo, v_hi, v_lo (3-D, box {32, 64, 1}).
+int launch_residual_tc(const CUtensorMap* maps, const float* q, const float* rep_w, int64_t r_pad, const float* low,
+                       float* out, int* status, int64_t bh, int64_t n, int d, int dv, int degree, int bs,
+                       int64_t m_blk, float scale, float eps, cudaStream_t stream) {
+  if (bh == 0 || n == 0) return SA_OK;
+  if (bh > 65535 || (n + kRowsQ - 1) / kRowsQ > 2147483647LL)
+    return set_error(SA_ERR_UNSUPPORTED, "grid too large for the tensor-core residual");
+  ResTCParams prm{q, rep_w, low, out, status, n, m_blk, r_pad, d, dv, bs, scale, eps};
+  const int dp = residual_tc_dp(d), dvp = residual_tc_dvp(dv);
+  if (dp == 32 && dvp == 32) return launch_deg<32, 32>(degree, maps, prm, bh, stream);
+  if (dp == 32 && dvp == 64) return launch_deg<32, 64>(degree, maps, prm, bh, stream);
+  if (dp == 32 && dvp == 128) return launch_deg<32, 128>(degree, maps, prm, bh, stream);
+  if (dp == 64 && dvp == 32) return launch_deg<64, 32>(degree, maps, prm, bh, stream);
+  if (dp == 64 && dvp == 64) return launch_deg<64, 64>(degree, maps, prm, bh, stream);
+  if (dp == 64 && dvp == 128) return launch_deg<64, 128>(degree, maps, prm, bh, stream);
+  return set_error(SA_ERR_UNSUPPORTED, "tensor-core residual: d=%d dv=%d not supported", d, dv);
+}
+
+}  // namespace sa

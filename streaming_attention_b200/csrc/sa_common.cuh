@@ -80,6 +80,24 @@ __host__ __device__ inline Monomial monomial_of(int64_t f, int d) {
   return m;
 }
 
+// Optional tf32 hi / fp32 remainder copies of the gathered reps, the operand
+// format of the tensor-core residual (zero padded to dp / dvp columns).
+struct SplitOut {
+  float* khi = nullptr;
+  float* klo = nullptr;
+  float* vhi = nullptr;
+  float* vlo = nullptr;
+  int dp = 0, dvp = 0;
+  int64_t w_stride = 0;  // per-sequence stride of rep_w
+};
+
+// tf32 (round to nearest, ties away from zero) of x, in a 32-bit container.
+__device__ __forceinline__ uint32_t tc_split_hi(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
 // exp_{<=t}(x) accumulated as the reference does: term *= x / r; out += term
 // (fast_article_attention.py:95-104).
 // Division by 1 and 2 is written as the (exactly equal) multiplications.

@@ -12,6 +12,7 @@ tensors are rejected, and a missing library raises.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import Optional, Tuple, Union
 
@@ -210,7 +211,21 @@ def _run(q3: Tensor, k3: Tensor, v3: Tensor, *, batch: int, heads: int, degree: 
             q3.data_ptr(), k3.data_ptr(), v3.data_ptr(), bh, n, d, dv, degree, block_size, float(scale), comp,
             _ptr(tables.dirs), _ptr(tables.coins), _ptr(tables.perms), float(eps), out.data_ptr(),
             _ptr(rep_idx), ws.data_ptr(), ws.numel(), stream), "sa_fast_attention")
+        if _CHECK_STATUS:
+            check_device_status(ws)
     return out, rep_idx
+
+
+_CHECK_STATUS = os.environ.get("SA_CHECK_STATUS", "0") == "1"
+
+
+def check_device_status(workspace: Tensor) -> None:
+    """Read the launch status word (the first 4 bytes of the workspace): the
+    tensor-core kernels bound every wait and record a nonzero code there when
+    one gives up.  Synchronises the stream."""
+    code = int(workspace[:4].view(torch.int32).item())
+    if code != 0:
+        raise _lib.SAError(f"device status {code}: a bounded device-side wait gave up")
 
 
 def _as_f32(t: Tensor) -> Tensor:

@@ -13,6 +13,8 @@ import numpy as np
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+# every forward in the tests reads back the device status word of its launch
+os.environ.setdefault("SA_CHECK_STATUS", "1")
 GOLDEN = os.path.join(ROOT, "tests", "golden")
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
