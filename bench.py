@@ -245,8 +245,28 @@ class Staged:
         self.rk = torch.empty(bh, max(R, 1), d, device=dev)
         self.rv = torch.empty(bh, max(R, 1), dv, device=dev)
         self.rw = torch.empty(bh, max(R, 1), device=dev)
-        self.launches = (1 if R else 0) + 2
+        import ctypes
+        nbytes = ctypes.c_size_t(0)
+        sa_lib.sa_residual_combine_workspace_size(bh, n, d, dv, c["block_size"], self.comp, ctypes.byref(nbytes))
+        self.res_ws = torch.empty(max(int(nbytes.value), 256), device=dev, dtype=torch.uint8)
         self.times = {"compress": [], "moments": [], "residual": []}
+        # the fused entry point (the timed `value`)
+        fb = ctypes.c_size_t(0)
+        sa_lib.sa_fast_attention_workspace_size(bh, n, d, dv, c["degree"], c["block_size"], self.comp,
+                                                ctypes.byref(fb))
+        self.ws = torch.empty(max(int(fb.value), 256), device=dev, dtype=torch.uint8)
+        tc = int(nbytes.value) > 0
+        # kernels per fused forward: (split k, split v,) compress, moments, residual
+        self.launches = (2 if tc else 0) + (1 if R else 0) + 2
+
+    def fused(self, stream):
+        from streaming_attention_b200 import _lib
+        c, t = self.c, self.tables
+        ptr = lambda x: None if x is None else x.data_ptr()  # noqa: E731
+        _lib.check(self.lib.sa_fast_attention(
+            self.q3.data_ptr(), self.k3.data_ptr(), self.v3.data_ptr(), self.bh, self.n, self.d, self.dv,
+            c["degree"], c["block_size"], self.scale, self.comp, ptr(t.dirs), ptr(t.coins), ptr(t.perms), 1e-12,
+            self.out.data_ptr(), None, self.ws.data_ptr(), self.ws.numel(), stream), "sa_fast_attention")
 
     def step(self, stream, record=False):
         from streaming_attention_b200 import _lib
@@ -273,7 +293,8 @@ class Staged:
         _lib.check(self.lib.sa_residual_combine(
             self.q3.data_ptr(), self.k3.data_ptr(), self.v3.data_ptr(), rk.data_ptr(), rv.data_ptr(),
             self.rw.data_ptr() if self.R else None, self.low.data_ptr(), self.bh, self.n, self.d, self.dv,
-            c["degree"], c["block_size"], self.comp, self.scale, 1e-12, self.out.data_ptr(), stream), "residual")
+            c["degree"], c["block_size"], self.comp, self.scale, 1e-12, self.out.data_ptr(), self.res_ws.data_ptr(),
+            self.res_ws.numel(), stream), "residual")
         if record:
             ev[3].record()
         return ev
@@ -306,22 +327,29 @@ def run_ours(args, rank, world, dev):
             torch.distributed.barrier()
         torch.cuda.synchronize(dev)
 
+    # the headline: the fused entry point, inputs resident in HBM
     for _ in range(args.warmup):
-        st.step(stream)
+        st.fused(stream)
     barrier()
-    evs = []
     with ClockSampler(dev.index) as clk:
         barrier()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
         for _ in range(args.steps):
-            evs.append(st.step(stream, record=True))
+            st.fused(stream)
         t1.record()
         barrier()
-    st.collect(evs)
     ms = t0.elapsed_time(t1)
     ms_max = reduce_max(ms, world, dev)
+    # per-kernel device times: the same kernels through the staged entry points,
+    # CUDA events between the launches on the launching stream
+    for _ in range(max(1, args.warmup)):
+        st.step(stream)
+    barrier()
+    evs = [st.step(stream, record=True) for _ in range(args.steps)]
+    barrier()
+    st.collect(evs)
 
     # end to end through the public entry point, from pinned host buffers
     e2e = None

@@ -97,12 +97,19 @@ int sa_low_moments(const float* q, const float* k, const float* v, int64_t bh, i
                    int dv, int degree, int block_size, float scale, float* low, void* stream);
 
 /* Residual over the completed-block reps + exact current block, added to the
- * low term, then out = num / max(den, eps).  For compressor none pass
- * rep_k = k, rep_v = v, rep_w = NULL (all weights 1, block_size reps per block). */
+ * low term, then out = num / max(den, eps).  rep_k/rep_v/rep_w are the
+ * outputs of sa_compress_blocks ([bh, nc*m, *]); for compressor none they are
+ * ignored (every earlier key is a rep of weight 1).  For d <= 64 and
+ * dv <= 128 the tensor-core kernel runs and needs a caller workspace of
+ * sa_residual_combine_workspace_size bytes (256-byte aligned); otherwise the
+ * workspace may be NULL. */
+int sa_residual_combine_workspace_size(int64_t bh, int64_t n, int d, int dv, int block_size,
+                                       int compressor, size_t* bytes);
 int sa_residual_combine(const float* q, const float* k, const float* v, const float* rep_k,
                         const float* rep_v, const float* rep_w, const float* low, int64_t bh,
                         int64_t n, int d, int dv, int degree, int block_size, int compressor,
-                        float scale, float eps, float* out, void* stream);
+                        float scale, float eps, float* out, void* workspace,
+                        size_t workspace_bytes, void* stream);
 
 /* Bytes of device workspace sa_fast_attention needs. */
 int sa_fast_attention_workspace_size(int64_t bh, int64_t n, int d, int dv, int degree,

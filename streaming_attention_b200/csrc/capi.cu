@@ -161,6 +161,28 @@ int encode_map_3d(CUtensorMap* map, const void* base, int inner, int64_t rows, i
   return SA_OK;
 }
 
+// Tensor maps over the split operands, then the tensor-core residual.
+// rep_src / cur_src: {k_hi, k_lo, v_hi, v_lo} of the reps (rep_rows rows per
+// sequence) and of all keys (n rows per sequence).
+int residual_tc_from_split(const Workspace& w, const float* const rep_src[4], int64_t rep_rows,
+                           const float* const cur_src[4], const float* rep_w, const float* q, const float* low,
+                           float* out, int* status, int64_t bh, int64_t n, int d, int dv, int degree, int block_size,
+                           int compressor, float scale, float eps, cudaStream_t s) {
+  CUtensorMap maps[8];
+  const int widths[4] = {w.dp, w.dp, w.dvp, w.dvp};
+  for (int j = 0; j < 4; ++j) {
+    // K tiles: K-major, 128-byte swizzle; V tiles: MN-major, 128-byte swizzle with 32-byte atoms
+    const CUtensorMapSwizzle sw = j < 2 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    int rc = encode_map_3d(&maps[j], rep_src[j], widths[j], rep_rows, bh, 64, sw);
+    if (rc) return rc;
+    rc = encode_map_3d(&maps[4 + j], cur_src[j], widths[j], n, bh, 64, sw);
+    if (rc) return rc;
+  }
+  const int64_t m_blk = compressor == SA_COMPRESSOR_NONE ? block_size : (block_size + 1) / 2;
+  return launch_residual_tc(maps, q, rep_w, w.r_pad, low, out, status, bh, n, d, dv, degree, block_size, m_blk,
+                            scale, eps, s);
+}
+
 }  // namespace
 }  // namespace sa
 
@@ -213,18 +235,74 @@ int sa_low_moments(const float* q, const float* k, const float* v, int64_t bh, i
   return launch_low_moments(q, k, v, bh, n, d, dv, degree, block_size, scale, low, (cudaStream_t)stream);
 }
 
+int sa_residual_combine_workspace_size(int64_t bh, int64_t n, int d, int dv, int block_size, int compressor,
+                                       size_t* bytes) {
+  if (!bytes) return set_error(SA_ERR_INVALID_ARG, "null output pointer");
+  int rc = check_common(nullptr, nullptr, nullptr, 0, n, d, dv, 0, block_size);
+  if (rc) return rc;
+  if (bh < 0) return set_error(SA_ERR_INVALID_ARG, "bh must be non-negative");
+  rc = check_compressor(compressor);
+  if (rc) return rc;
+  const Workspace w = plan(bh, n, d, dv, block_size, compressor);
+  *bytes = w.tc ? w.total : 0;
+  return SA_OK;
+}
+
 int sa_residual_combine(const float* q, const float* k, const float* v, const float* rep_k, const float* rep_v,
                         const float* rep_w, const float* low, int64_t bh, int64_t n, int d, int dv, int degree,
-                        int block_size, int compressor, float scale, float eps, float* out, void* stream) {
+                        int block_size, int compressor, float scale, float eps, float* out, void* workspace,
+                        size_t workspace_bytes, void* stream) {
   int rc = check_common(q, k, v, bh, n, d, dv, degree, block_size);
   if (rc) return rc;
   rc = check_compressor(compressor);
   if (rc) return rc;
-  if (bh > 0 && n > 0 && (!low || !out)) return set_error(SA_ERR_INVALID_ARG, "null low or out pointer");
-  const int64_t nc = n > 0 ? (n - 1) / block_size : 0;
-  if (bh > 0 && nc > 0 && (!rep_k || !rep_v)) return set_error(SA_ERR_INVALID_ARG, "null rep pointer");
-  return launch_residual(q, k, v, rep_k, rep_v, rep_w, low, bh, n, d, dv, degree, block_size, compressor, scale, eps,
-                         out, (cudaStream_t)stream);
+  if (bh == 0 || n == 0) return SA_OK;
+  if (!low || !out) return set_error(SA_ERR_INVALID_ARG, "null low or out pointer");
+  const int64_t nc = (n - 1) / block_size;
+  const bool have_reps = compressor != SA_COMPRESSOR_NONE && nc > 0;
+  if (have_reps && (!rep_k || !rep_v || !rep_w)) return set_error(SA_ERR_INVALID_ARG, "null rep pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  const Workspace w = plan(bh, n, d, dv, block_size, compressor);
+  if (!w.tc)
+    return launch_residual(q, k, v, rep_k, rep_v, rep_w, low, bh, n, d, dv, degree, block_size, compressor, scale,
+                           eps, out, s);
+  if (!workspace || workspace_bytes < w.total)
+    return set_error(SA_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu required", workspace_bytes,
+                     w.total);
+  if (((uintptr_t)workspace) % kAlign)
+    return set_error(SA_ERR_INVALID_ARG, "workspace must be %zu-byte aligned", kAlign);
+  char* ws = static_cast<char*>(workspace);
+  int* status = reinterpret_cast<int*>(ws + w.status);
+  cudaError_t ce = cudaMemsetAsync(status, 0, sizeof(int), s);
+  if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "status reset: %s", cudaGetErrorString(ce));
+  float* cur[4] = {reinterpret_cast<float*>(ws + w.khi), reinterpret_cast<float*>(ws + w.klo),
+                   reinterpret_cast<float*>(ws + w.vhi), reinterpret_cast<float*>(ws + w.vlo)};
+  rc = launch_split(k, bh * n, d, w.dp, cur[0], cur[1], s);
+  if (rc) return rc;
+  rc = launch_split(v, bh * n, dv, w.dvp, cur[2], cur[3], s);
+  if (rc) return rc;
+  const float* rep_src[4] = {cur[0], cur[1], cur[2], cur[3]};
+  const float* cur_src[4] = {cur[0], cur[1], cur[2], cur[3]};
+  float* wpad = nullptr;
+  int64_t rep_rows = n;
+  if (have_reps) {
+    float* r[4] = {reinterpret_cast<float*>(ws + w.rkhi), reinterpret_cast<float*>(ws + w.rklo),
+                   reinterpret_cast<float*>(ws + w.rvhi), reinterpret_cast<float*>(ws + w.rvlo)};
+    rc = launch_split(rep_k, bh * w.R, d, w.dp, r[0], r[1], s);
+    if (rc) return rc;
+    rc = launch_split(rep_v, bh * w.R, dv, w.dvp, r[2], r[3], s);
+    if (rc) return rc;
+    wpad = reinterpret_cast<float*>(ws + w.rep_w);
+    ce = cudaMemsetAsync(wpad, 0, (size_t)bh * w.r_pad * sizeof(float), s);
+    if (ce == cudaSuccess)
+      ce = cudaMemcpy2DAsync(wpad, (size_t)w.r_pad * sizeof(float), rep_w, (size_t)w.R * sizeof(float),
+                             (size_t)w.R * sizeof(float), (size_t)bh, cudaMemcpyDeviceToDevice, s);
+    if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "rep weight copy: %s", cudaGetErrorString(ce));
+    for (int j = 0; j < 4; ++j) rep_src[j] = r[j];
+    rep_rows = w.R;
+  }
+  return residual_tc_from_split(w, rep_src, rep_rows, cur_src, wpad, q, low, out, status, bh, n, d, dv, degree,
+                                block_size, compressor, scale, eps, s);
 }
 
 int sa_fast_attention_workspace_size(int64_t bh, int64_t n, int d, int dv, int degree, int block_size, int compressor,
@@ -321,20 +399,9 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
   }
   rc = launch_low_moments(q, k, v, bh, n, d, dv, degree, block_size, scale, low, s);
   if (rc) return rc;
-  CUtensorMap maps[8];
-  const int widths[4] = {w.dp, w.dp, w.dvp, w.dvp};
   const float* cur_src[4] = {khi, klo, vhi, vlo};
-  for (int j = 0; j < 4; ++j) {
-    // K tiles: K-major, 128-byte swizzle; V tiles: MN-major, 128-byte swizzle with 32-byte atoms
-    const CUtensorMapSwizzle sw = j < 2 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-    rc = encode_map_3d(&maps[j], maps_src[j], widths[j], rep_rows, bh, 64, sw);
-    if (rc) return rc;
-    rc = encode_map_3d(&maps[4 + j], cur_src[j], widths[j], n, bh, 64, sw);
-    if (rc) return rc;
-  }
-  const int64_t m_blk = compressor == SA_COMPRESSOR_NONE ? block_size : (block_size + 1) / 2;
-  return launch_residual_tc(maps, q, rep_w, w.r_pad, low, out, status, bh, n, d, dv, degree, block_size, m_blk,
-                            scale, eps, s);
+  return residual_tc_from_split(w, maps_src, rep_rows, cur_src, rep_w, q, low, out, status, bh, n, d, dv, degree,
+                                block_size, compressor, scale, eps, s);
 }
 
 }  // extern "C"
