@@ -249,6 +249,9 @@ class Staged:
         nbytes = ctypes.c_size_t(0)
         sa_lib.sa_residual_combine_workspace_size(bh, n, d, dv, c["block_size"], self.comp, ctypes.byref(nbytes))
         self.res_ws = torch.empty(max(int(nbytes.value), 256), device=dev, dtype=torch.uint8)
+        mb = ctypes.c_size_t(0)
+        sa_lib.sa_low_moments_workspace_size(bh, n, d, dv, c["degree"], c["block_size"], ctypes.byref(mb))
+        self.mom_ws = torch.empty(max(int(mb.value), 256), device=dev, dtype=torch.uint8)
         self.times = {"compress": [], "moments": [], "residual": []}
         # the fused entry point (the timed `value`)
         fb = ctypes.c_size_t(0)
@@ -285,7 +288,8 @@ class Staged:
             ev[1].record()
         _lib.check(self.lib.sa_low_moments(self.q3.data_ptr(), self.k3.data_ptr(), self.v3.data_ptr(), self.bh,
                                            self.n, self.d, self.dv, c["degree"], c["block_size"], self.scale,
-                                           self.low.data_ptr(), stream), "moments")
+                                           self.low.data_ptr(), self.mom_ws.data_ptr(), self.mom_ws.numel(),
+                                           stream), "moments")
         if record:
             ev[2].record()
         rk = self.rk if self.R else self.k3

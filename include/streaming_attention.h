@@ -92,9 +92,15 @@ int sa_compress_blocks(const float* k, const float* v, int64_t bh, int64_t n, in
  * completed blocks before the query's own block:
  *   low[i, :dv] = sum_{j < bstart(i)} P_t(scale q_i.k_j) v_j,
  *   low[i, dv]  = sum_{j < bstart(i)} P_t(scale q_i.k_j),
- * where bstart(i) = (i / block_size) * block_size.  low is [bh, n, dv+1]. */
+ * where bstart(i) = (i / block_size) * block_size.  low is [bh, n, dv+1].
+ * When the tensor-core kernel applies (dv <= 64) it needs a caller workspace
+ * of sa_low_moments_workspace_size bytes (256-byte aligned); otherwise the
+ * workspace may be NULL. */
+int sa_low_moments_workspace_size(int64_t bh, int64_t n, int d, int dv, int degree, int block_size,
+                                  size_t* bytes);
 int sa_low_moments(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d,
-                   int dv, int degree, int block_size, float scale, float* low, void* stream);
+                   int dv, int degree, int block_size, float scale, float* low, void* workspace,
+                   size_t workspace_bytes, void* stream);
 
 /* Residual over the completed-block reps + exact current block, added to the
  * low term, then out = num / max(den, eps).  rep_k/rep_v/rep_w are the

@@ -35,7 +35,8 @@ SIGNATURES = {
     "sa_feature_count": [_i32, _i32, ctypes.POINTER(_i64)],
     "sa_block_counts": [_i64, _i32, _i32, ctypes.POINTER(_i64), ctypes.POINTER(_i64)],
     "sa_compress_blocks": [_vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
-    "sa_low_moments": [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _f32, _vp, _vp],
+    "sa_low_moments_workspace_size": [_i64, _i64, _i32, _i32, _i32, _i32, ctypes.POINTER(_sz)],
+    "sa_low_moments": [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _sz, _vp],
     "sa_residual_combine_workspace_size": [_i64, _i64, _i32, _i32, _i32, _i32, ctypes.POINTER(_sz)],
     "sa_residual_combine": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _f32,
                             _f32, _vp, _vp, _sz, _vp],

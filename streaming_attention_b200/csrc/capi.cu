@@ -5,6 +5,13 @@
 // SA_ERR_INVALID_ARG with a message; every CUDA error is caught here and
 // returned as SA_ERR_CUDA.  No entry point allocates device memory: outputs
 // and scratch belong to the caller.
+//
+// Two kernel families:
+//  * tensor cores (tcgen05 / TMEM / TMA, 3xTF32) for d <= 64, dv <= 128
+//    (residual) and dv <= 64 (moments): the operands are first split into a
+//    tf32 "hi" and an fp32 remainder by split_rows_kernel / the compressor;
+//  * CUDA cores (fp32 FMA) for every other shape, and on request
+//    (SA_FORCE_SIMT=1, for A/B comparisons).
 #include <cuda.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -22,8 +29,12 @@ int launch_split(const float* src, int64_t rows, int cols, int cols_pad, float* 
 int residual_tc_dp(int d);
 int residual_tc_dvp(int dv);
 int launch_residual_tc(const CUtensorMap* maps, const float* q, const float* rep_w, int64_t r_pad, const float* low,
-                       float* out, int* status, int64_t bh, int64_t n, int d, int dv, int degree, int bs,
+                       int groups, float* out, int* status, int64_t bh, int64_t n, int d, int dv, int degree, int bs,
                        int64_t m_blk, float scale, float eps, cudaStream_t stream);
+int moments_tc_groups(int d, int dv, int degree);
+int launch_moments_tc(const CUtensorMap* maps, const float* q, const float* k, float* part, int* status, int64_t bh,
+                      int64_t n, int d, int dv, int degree, int bs, float scale, cudaStream_t stream);
+int launch_sum_groups(const float* part, int groups, int64_t stride, float* out, cudaStream_t stream);
 int launch_low_moments(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d, int dv,
                        int degree, int bs, float scale, float* low, cudaStream_t stream);
 int launch_residual(const float* q, const float* k, const float* v, const float* rk, const float* rv,
@@ -72,25 +83,36 @@ int check_compressor(int c) {
 constexpr size_t kAlign = 256;
 inline size_t align_up(size_t x) { return (x + kAlign - 1) & ~(kAlign - 1); }
 
+bool force_simt() {
+  const char* force = getenv("SA_FORCE_SIMT");
+  return force && force[0] == '1';
+}
+
 // Workspace layout.  Offset 0 always holds the launch status word (int, 0 = ok).
-// Tensor-core path (d <= 64, dv <= 128): tf32 hi / fp32 remainder copies of
-// k, v (padded to dp / dvp columns) and of the gathered reps; rep weights
-// padded per sequence to a multiple of 64.  SIMT path: raw reps.
+// tc:     tensor-core residual: tf32 hi / fp32 remainder copies of k, v
+//         (padded to dp / dvp columns) and of the gathered reps; rep weights
+//         padded per sequence to a multiple of 64.
+// groups: >0 when the tensor-core moment kernel runs: `low` then holds that
+//         many partial slices [groups, bh, n, dv+1] (summed by the residual).
 struct Workspace {
   bool tc = false;
+  int groups = 0;
   int dp = 0, dvp = 0;
   int64_t R = 0, r_pad = 0;
   size_t status = 0, low = 0, khi = 0, klo = 0, vhi = 0, vlo = 0;
   size_t rkhi = 0, rklo = 0, rvhi = 0, rvlo = 0, rep_k = 0, rep_v = 0, rep_w = 0, rep_idx = 0, total = 0;
 };
 
-Workspace plan(int64_t bh, int64_t n, int d, int dv, int bs, int compressor) {
+enum class Plan { kFull, kResidualOnly, kMomentsOnly };
+
+Workspace plan(int64_t bh, int64_t n, int d, int dv, int degree, int bs, int compressor, Plan what) {
   Workspace w{};
+  const bool simt = force_simt();
   w.dp = residual_tc_dp(d);
   w.dvp = residual_tc_dvp(dv);
-  // SA_FORCE_SIMT=1 selects the CUDA-core kernels for every shape (A/B comparisons)
-  const char* force = getenv("SA_FORCE_SIMT");
-  w.tc = w.dp > 0 && w.dvp > 0 && !(force && force[0] == '1');
+  w.tc = w.dp > 0 && w.dvp > 0 && !simt;
+  w.groups = (!simt && what != Plan::kResidualOnly) ? moments_tc_groups(d, dv, degree) : 0;
+  if (w.groups > 0 && w.dvp == 0) w.dvp = dv <= 32 ? 32 : 64;
   const int64_t nc = n > 0 ? (n - 1) / bs : 0;
   w.R = (compressor == SA_COMPRESSOR_NONE) ? 0 : nc * ((bs + 1) / 2);
   w.r_pad = (w.R + 63) / 64 * 64;
@@ -102,29 +124,34 @@ Workspace plan(int64_t bh, int64_t n, int d, int dv, int bs, int compressor) {
   };
   const size_t f = sizeof(float);
   w.status = take(sizeof(int));
-  w.low = take((size_t)bh * n * (dv + 1) * f);
-  if (w.tc) {
+  if (what != Plan::kResidualOnly) w.low = take((size_t)(w.groups > 0 ? w.groups : 1) * bh * n * (dv + 1) * f);
+  const bool need_v_split = w.groups > 0 || (w.tc && what != Plan::kMomentsOnly);
+  if (w.tc && what != Plan::kMomentsOnly) {
     w.khi = take((size_t)bh * n * w.dp * f);
     w.klo = take((size_t)bh * n * w.dp * f);
+  }
+  if (need_v_split) {
     w.vhi = take((size_t)bh * n * w.dvp * f);
     w.vlo = take((size_t)bh * n * w.dvp * f);
-    w.rkhi = take((size_t)bh * w.R * w.dp * f);
-    w.rklo = take((size_t)bh * w.R * w.dp * f);
-    w.rvhi = take((size_t)bh * w.R * w.dvp * f);
-    w.rvlo = take((size_t)bh * w.R * w.dvp * f);
-    w.rep_w = take((size_t)bh * w.r_pad * f);
-  } else {
-    w.rep_k = take((size_t)bh * w.R * d * f);
-    w.rep_v = take((size_t)bh * w.R * dv * f);
-    w.rep_w = take((size_t)bh * w.R * f);
   }
-  w.rep_idx = take((size_t)bh * w.R * sizeof(int32_t));
+  if (what != Plan::kMomentsOnly) {
+    if (w.tc) {
+      w.rkhi = take((size_t)bh * w.R * w.dp * f);
+      w.rklo = take((size_t)bh * w.R * w.dp * f);
+      w.rvhi = take((size_t)bh * w.R * w.dvp * f);
+      w.rvlo = take((size_t)bh * w.R * w.dvp * f);
+      w.rep_w = take((size_t)bh * w.r_pad * f);
+    } else if (what == Plan::kFull) {
+      w.rep_k = take((size_t)bh * w.R * d * f);
+      w.rep_v = take((size_t)bh * w.R * dv * f);
+      w.rep_w = take((size_t)bh * w.R * f);
+    }
+    if (what == Plan::kFull) w.rep_idx = take((size_t)bh * w.R * sizeof(int32_t));
+  }
   w.total = off;
   return w;
 }
 
-// 3-D tensor map over a [outer, rows, inner] fp32 array; box {32, box_rows, 1},
-// 128-byte swizzle, zero fill out of bounds.
 // The driver's tensor-map encoder, looked up at run time so that the library
 // loads on machines without a driver (the CPU-side tests only load it).
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -146,8 +173,10 @@ EncodeTiledFn encode_tiled_fn() {
   return fn;
 }
 
+// 3-D tensor map over a [outer, rows, inner] fp32 array; box {32, box_rows, 1},
+// zero fill out of bounds.
 int encode_map_3d(CUtensorMap* map, const void* base, int inner, int64_t rows, int64_t outer, int box_rows,
-                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+                  CUtensorMapSwizzle swizzle) {
   cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)(rows > 0 ? rows : 1), (cuuint64_t)(outer > 0 ? outer : 1)};
   cuuint64_t strides[2] = {(cuuint64_t)inner * 4, (cuuint64_t)inner * 4 * (cuuint64_t)(rows > 0 ? rows : 1)};
   cuuint32_t box[3] = {32, (cuuint32_t)box_rows, 1};
@@ -166,8 +195,8 @@ int encode_map_3d(CUtensorMap* map, const void* base, int inner, int64_t rows, i
 // sequence) and of all keys (n rows per sequence).
 int residual_tc_from_split(const Workspace& w, const float* const rep_src[4], int64_t rep_rows,
                            const float* const cur_src[4], const float* rep_w, const float* q, const float* low,
-                           float* out, int* status, int64_t bh, int64_t n, int d, int dv, int degree, int block_size,
-                           int compressor, float scale, float eps, cudaStream_t s) {
+                           int groups, float* out, int* status, int64_t bh, int64_t n, int d, int dv, int degree,
+                           int block_size, int compressor, float scale, float eps, cudaStream_t s) {
   CUtensorMap maps[8];
   const int widths[4] = {w.dp, w.dp, w.dvp, w.dvp};
   for (int j = 0; j < 4; ++j) {
@@ -179,8 +208,35 @@ int residual_tc_from_split(const Workspace& w, const float* const rep_src[4], in
     if (rc) return rc;
   }
   const int64_t m_blk = compressor == SA_COMPRESSOR_NONE ? block_size : (block_size + 1) / 2;
-  return launch_residual_tc(maps, q, rep_w, w.r_pad, low, out, status, bh, n, d, dv, degree, block_size, m_blk,
-                            scale, eps, s);
+  return launch_residual_tc(maps, q, rep_w, w.r_pad, low, groups, out, status, bh, n, d, dv, degree, block_size,
+                            m_blk, scale, eps, s);
+}
+
+// Tensor-core moments into `part` ([groups, bh, n, dv+1]) from the split v.
+int moments_tc_from_split(const Workspace& w, const float* vhi, const float* vlo, const float* q, const float* k,
+                          float* part, int* status, int64_t bh, int64_t n, int d, int dv, int degree, int block_size,
+                          float scale, cudaStream_t s) {
+  CUtensorMap maps[2];
+  int rc = encode_map_3d(&maps[0], vhi, w.dvp, n, bh, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+  if (rc) return rc;
+  rc = encode_map_3d(&maps[1], vlo, w.dvp, n, bh, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+  if (rc) return rc;
+  return launch_moments_tc(maps, q, k, part, status, bh, n, d, dv, degree, block_size, scale, s);
+}
+
+int check_workspace(const Workspace& w, const void* workspace, size_t workspace_bytes) {
+  if (!workspace || workspace_bytes < w.total)
+    return set_error(SA_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu required", workspace_bytes,
+                     w.total);
+  if (((uintptr_t)workspace) % kAlign)
+    return set_error(SA_ERR_INVALID_ARG, "workspace must be %zu-byte aligned", kAlign);
+  return SA_OK;
+}
+
+int reset_status(int* status, cudaStream_t s) {
+  const cudaError_t ce = cudaMemsetAsync(status, 0, sizeof(int), s);
+  if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "status reset: %s", cudaGetErrorString(ce));
+  return SA_OK;
 }
 
 }  // namespace
@@ -227,12 +283,39 @@ int sa_compress_blocks(const float* k, const float* v, int64_t bh, int64_t n, in
                          rep_w, SplitOut{}, (cudaStream_t)stream);
 }
 
+int sa_low_moments_workspace_size(int64_t bh, int64_t n, int d, int dv, int degree, int block_size, size_t* bytes) {
+  if (!bytes) return set_error(SA_ERR_INVALID_ARG, "null output pointer");
+  int rc = check_common(nullptr, nullptr, nullptr, 0, n, d, dv, degree, block_size);
+  if (rc) return rc;
+  if (bh < 0) return set_error(SA_ERR_INVALID_ARG, "bh must be non-negative");
+  const Workspace w = plan(bh, n, d, dv, degree, block_size, SA_COMPRESSOR_NONE, Plan::kMomentsOnly);
+  *bytes = w.groups > 0 ? w.total : 0;
+  return SA_OK;
+}
+
 int sa_low_moments(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d, int dv, int degree,
-                   int block_size, float scale, float* low, void* stream) {
+                   int block_size, float scale, float* low, void* workspace, size_t workspace_bytes, void* stream) {
   int rc = check_common(q, k, v, bh, n, d, dv, degree, block_size);
   if (rc) return rc;
-  if (bh > 0 && n > 0 && !low) return set_error(SA_ERR_INVALID_ARG, "null output pointer");
-  return launch_low_moments(q, k, v, bh, n, d, dv, degree, block_size, scale, low, (cudaStream_t)stream);
+  if (bh == 0 || n == 0) return SA_OK;
+  if (!low) return set_error(SA_ERR_INVALID_ARG, "null output pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  const Workspace w = plan(bh, n, d, dv, degree, block_size, SA_COMPRESSOR_NONE, Plan::kMomentsOnly);
+  if (w.groups == 0) return launch_low_moments(q, k, v, bh, n, d, dv, degree, block_size, scale, low, s);
+  rc = check_workspace(w, workspace, workspace_bytes);
+  if (rc) return rc;
+  char* ws = static_cast<char*>(workspace);
+  int* status = reinterpret_cast<int*>(ws + w.status);
+  rc = reset_status(status, s);
+  if (rc) return rc;
+  float* vhi = reinterpret_cast<float*>(ws + w.vhi);
+  float* vlo = reinterpret_cast<float*>(ws + w.vlo);
+  float* part = reinterpret_cast<float*>(ws + w.low);
+  rc = launch_split(v, bh * n, dv, w.dvp, vhi, vlo, s);
+  if (rc) return rc;
+  rc = moments_tc_from_split(w, vhi, vlo, q, k, part, status, bh, n, d, dv, degree, block_size, scale, s);
+  if (rc) return rc;
+  return launch_sum_groups(part, w.groups, bh * n * (dv + 1), low, s);
 }
 
 int sa_residual_combine_workspace_size(int64_t bh, int64_t n, int d, int dv, int block_size, int compressor,
@@ -243,7 +326,7 @@ int sa_residual_combine_workspace_size(int64_t bh, int64_t n, int d, int dv, int
   if (bh < 0) return set_error(SA_ERR_INVALID_ARG, "bh must be non-negative");
   rc = check_compressor(compressor);
   if (rc) return rc;
-  const Workspace w = plan(bh, n, d, dv, block_size, compressor);
+  const Workspace w = plan(bh, n, d, dv, 0, block_size, compressor, Plan::kResidualOnly);
   *bytes = w.tc ? w.total : 0;
   return SA_OK;
 }
@@ -262,19 +345,16 @@ int sa_residual_combine(const float* q, const float* k, const float* v, const fl
   const bool have_reps = compressor != SA_COMPRESSOR_NONE && nc > 0;
   if (have_reps && (!rep_k || !rep_v || !rep_w)) return set_error(SA_ERR_INVALID_ARG, "null rep pointer");
   cudaStream_t s = (cudaStream_t)stream;
-  const Workspace w = plan(bh, n, d, dv, block_size, compressor);
+  const Workspace w = plan(bh, n, d, dv, degree, block_size, compressor, Plan::kResidualOnly);
   if (!w.tc)
     return launch_residual(q, k, v, rep_k, rep_v, rep_w, low, bh, n, d, dv, degree, block_size, compressor, scale,
                            eps, out, s);
-  if (!workspace || workspace_bytes < w.total)
-    return set_error(SA_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu required", workspace_bytes,
-                     w.total);
-  if (((uintptr_t)workspace) % kAlign)
-    return set_error(SA_ERR_INVALID_ARG, "workspace must be %zu-byte aligned", kAlign);
+  rc = check_workspace(w, workspace, workspace_bytes);
+  if (rc) return rc;
   char* ws = static_cast<char*>(workspace);
   int* status = reinterpret_cast<int*>(ws + w.status);
-  cudaError_t ce = cudaMemsetAsync(status, 0, sizeof(int), s);
-  if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "status reset: %s", cudaGetErrorString(ce));
+  rc = reset_status(status, s);
+  if (rc) return rc;
   float* cur[4] = {reinterpret_cast<float*>(ws + w.khi), reinterpret_cast<float*>(ws + w.klo),
                    reinterpret_cast<float*>(ws + w.vhi), reinterpret_cast<float*>(ws + w.vlo)};
   rc = launch_split(k, bh * n, d, w.dp, cur[0], cur[1], s);
@@ -293,7 +373,7 @@ int sa_residual_combine(const float* q, const float* k, const float* v, const fl
     rc = launch_split(rep_v, bh * w.R, dv, w.dvp, r[2], r[3], s);
     if (rc) return rc;
     wpad = reinterpret_cast<float*>(ws + w.rep_w);
-    ce = cudaMemsetAsync(wpad, 0, (size_t)bh * w.r_pad * sizeof(float), s);
+    cudaError_t ce = cudaMemsetAsync(wpad, 0, (size_t)bh * w.r_pad * sizeof(float), s);
     if (ce == cudaSuccess)
       ce = cudaMemcpy2DAsync(wpad, (size_t)w.r_pad * sizeof(float), rep_w, (size_t)w.R * sizeof(float),
                              (size_t)w.R * sizeof(float), (size_t)bh, cudaMemcpyDeviceToDevice, s);
@@ -301,7 +381,7 @@ int sa_residual_combine(const float* q, const float* k, const float* v, const fl
     for (int j = 0; j < 4; ++j) rep_src[j] = r[j];
     rep_rows = w.R;
   }
-  return residual_tc_from_split(w, rep_src, rep_rows, cur_src, wpad, q, low, out, status, bh, n, d, dv, degree,
+  return residual_tc_from_split(w, rep_src, rep_rows, cur_src, wpad, q, low, 1, out, status, bh, n, d, dv, degree,
                                 block_size, compressor, scale, eps, s);
 }
 
@@ -313,7 +393,7 @@ int sa_fast_attention_workspace_size(int64_t bh, int64_t n, int d, int dv, int d
   if (bh < 0) return set_error(SA_ERR_INVALID_ARG, "bh must be non-negative");
   rc = check_compressor(compressor);
   if (rc) return rc;
-  *bytes = plan(bh, n, d, dv, block_size, compressor).total;
+  *bytes = plan(bh, n, d, dv, degree, block_size, compressor, Plan::kFull).total;
   return SA_OK;
 }
 
@@ -327,12 +407,9 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
   if (rc) return rc;
   if (bh == 0 || n == 0) return SA_OK;
   if (!out) return set_error(SA_ERR_INVALID_ARG, "null output pointer");
-  const Workspace w = plan(bh, n, d, dv, block_size, compressor);
-  if (!workspace || workspace_bytes < w.total)
-    return set_error(SA_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu required", workspace_bytes,
-                     w.total);
-  if (((uintptr_t)workspace) % kAlign)
-    return set_error(SA_ERR_INVALID_ARG, "workspace must be %zu-byte aligned", kAlign);
+  const Workspace w = plan(bh, n, d, dv, degree, block_size, compressor, Plan::kFull);
+  rc = check_workspace(w, workspace, workspace_bytes);
+  if (rc) return rc;
   char* ws = static_cast<char*>(workspace);
   float* low = reinterpret_cast<float*>(ws + w.low);
   int* status = reinterpret_cast<int*>(ws + w.status);
@@ -340,68 +417,81 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
   const int64_t nc = (n - 1) / block_size;
   const bool compress = compressor != SA_COMPRESSOR_NONE && nc > 0;
   int32_t* ridx = rep_idx ? rep_idx : reinterpret_cast<int32_t*>(ws + w.rep_idx);
-  cudaError_t ce = cudaMemsetAsync(status, 0, sizeof(int), s);
-  if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "status reset: %s", cudaGetErrorString(ce));
+  rc = reset_status(status, s);
+  if (rc) return rc;
 
-  if (!w.tc) {
-    const float* rk = k;
-    const float* rv = v;
-    const float* rw = nullptr;
-    if (compress) {
-      float* rep_k = reinterpret_cast<float*>(ws + w.rep_k);
-      float* rep_v = reinterpret_cast<float*>(ws + w.rep_v);
-      float* rep_w = reinterpret_cast<float*>(ws + w.rep_w);
-      rc = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, ridx, rep_k, rep_v, rep_w,
-                           SplitOut{}, s);
-      if (rc) return rc;
-      rk = rep_k;
-      rv = rep_v;
-      rw = rep_w;
-    }
-    rc = launch_low_moments(q, k, v, bh, n, d, dv, degree, block_size, scale, low, s);
-    if (rc) return rc;
-    return launch_residual(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, block_size, compressor, scale, eps, out,
-                           s);
-  }
-
-  // tensor-core path
+  // operand splits shared by the tensor-core kernels
   float* khi = reinterpret_cast<float*>(ws + w.khi);
   float* klo = reinterpret_cast<float*>(ws + w.klo);
   float* vhi = reinterpret_cast<float*>(ws + w.vhi);
   float* vlo = reinterpret_cast<float*>(ws + w.vlo);
-  rc = launch_split(k, bh * n, d, w.dp, khi, klo, s);
-  if (rc) return rc;
-  rc = launch_split(v, bh * n, dv, w.dvp, vhi, vlo, s);
-  if (rc) return rc;
-  float* rep_w = nullptr;
-  const float* maps_src[4] = {khi, klo, vhi, vlo};
+  if (w.tc) {
+    rc = launch_split(k, bh * n, d, w.dp, khi, klo, s);
+    if (rc) return rc;
+  }
+  if (w.tc || w.groups > 0) {
+    rc = launch_split(v, bh * n, dv, w.dvp, vhi, vlo, s);
+    if (rc) return rc;
+  }
+
+  // C1: compressor
+  const float* rk = k;
+  const float* rv = v;
+  float* rw = nullptr;
+  const float* rep_src[4] = {khi, klo, vhi, vlo};
   int64_t rep_rows = n;
   if (compress) {
-    SplitOut sp;
-    sp.khi = reinterpret_cast<float*>(ws + w.rkhi);
-    sp.klo = reinterpret_cast<float*>(ws + w.rklo);
-    sp.vhi = reinterpret_cast<float*>(ws + w.rvhi);
-    sp.vlo = reinterpret_cast<float*>(ws + w.rvlo);
-    sp.dp = w.dp;
-    sp.dvp = w.dvp;
-    sp.w_stride = w.r_pad;
-    rep_w = reinterpret_cast<float*>(ws + w.rep_w);
-    ce = cudaMemsetAsync(rep_w, 0, (size_t)bh * w.r_pad * sizeof(float), s);
-    if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "rep weight reset: %s", cudaGetErrorString(ce));
-    rc = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, ridx, nullptr, nullptr,
-                         rep_w, sp, s);
-    if (rc) return rc;
-    maps_src[0] = sp.khi;
-    maps_src[1] = sp.klo;
-    maps_src[2] = sp.vhi;
-    maps_src[3] = sp.vlo;
-    rep_rows = w.R;
+    if (w.tc) {
+      SplitOut sp;
+      sp.khi = reinterpret_cast<float*>(ws + w.rkhi);
+      sp.klo = reinterpret_cast<float*>(ws + w.rklo);
+      sp.vhi = reinterpret_cast<float*>(ws + w.rvhi);
+      sp.vlo = reinterpret_cast<float*>(ws + w.rvlo);
+      sp.dp = w.dp;
+      sp.dvp = w.dvp;
+      sp.w_stride = w.r_pad;
+      rw = reinterpret_cast<float*>(ws + w.rep_w);
+      const cudaError_t ce = cudaMemsetAsync(rw, 0, (size_t)bh * w.r_pad * sizeof(float), s);
+      if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "rep weight reset: %s", cudaGetErrorString(ce));
+      rc = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, ridx, nullptr, nullptr, rw,
+                           sp, s);
+      if (rc) return rc;
+      rep_src[0] = sp.khi;
+      rep_src[1] = sp.klo;
+      rep_src[2] = sp.vhi;
+      rep_src[3] = sp.vlo;
+      rep_rows = w.R;
+    } else {
+      float* rep_k = reinterpret_cast<float*>(ws + w.rep_k);
+      float* rep_v = reinterpret_cast<float*>(ws + w.rep_v);
+      rw = reinterpret_cast<float*>(ws + w.rep_w);
+      rc = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, ridx, rep_k, rep_v, rw,
+                           SplitOut{}, s);
+      if (rc) return rc;
+      rk = rep_k;
+      rv = rep_v;
+    }
   }
-  rc = launch_low_moments(q, k, v, bh, n, d, dv, degree, block_size, scale, low, s);
+
+  // M: low-degree moments
+  if (w.groups > 0)
+    rc = moments_tc_from_split(w, vhi, vlo, q, k, low, status, bh, n, d, dv, degree, block_size, scale, s);
+  else
+    rc = launch_low_moments(q, k, v, bh, n, d, dv, degree, block_size, scale, low, s);
   if (rc) return rc;
-  const float* cur_src[4] = {khi, klo, vhi, vlo};
-  return residual_tc_from_split(w, maps_src, rep_rows, cur_src, rep_w, q, low, out, status, bh, n, d, dv, degree,
-                                block_size, compressor, scale, eps, s);
+  const int groups = w.groups > 0 ? w.groups : 1;
+
+  // R: residual + combine
+  if (w.tc) {
+    const float* cur_src[4] = {khi, klo, vhi, vlo};
+    return residual_tc_from_split(w, rep_src, rep_rows, cur_src, rw, q, low, groups, out, status, bh, n, d, dv,
+                                  degree, block_size, compressor, scale, eps, s);
+  }
+  if (groups > 1) {  // the CUDA-core residual reads one summed slice
+    rc = launch_sum_groups(low, groups, bh * n * (dv + 1), low, s);
+    if (rc) return rc;
+  }
+  return launch_residual(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, block_size, compressor, scale, eps, out, s);
 }
 
 }  // extern "C"

@@ -1,0 +1,481 @@
+// Low-degree Taylor moments on the tensor cores (tcgen05 / TMEM / TMA), 3xTF32.
+//
+// Same quantity as moments.cu: for query i of block c,
+//   low[i, :dv] = phi_q(scale q_i) . S_{<c},  low[i, dv] = phi_q(scale q_i) . s_{<c}
+// with S = sum phi_k(k_j) v_j^T and s = sum phi_k(k_j) over the keys of the
+// completed blocks before c (fast_article_attention.py:151-259,
+// streaming_taylor_coreset_attention.py:118-296).
+//
+// Work split: one CTA per (group of up to FT feature tiles of 128, sequence).
+// The CTA scans the sequence block by block.  For every block it
+//   query phase  Out[128 tokens x dv] = Phi_q[tokens x features] . S_j   (M = tokens)
+//   update phase S_j[128 features x dv] += Phi_k^T[features x tokens] . V (M = features)
+// Both feature matrices are generated on the CUDA cores directly into TMEM
+// (tcgen05.st), where they are the A operand; thread t of the four generator
+// warps owns TMEM lane t, i.e. token t in the query phase and feature t of the
+// tile in the update phase.  S_j accumulates in TMEM; before each query phase
+// it is copied (split hi/lo, K-major, 128-byte swizzle) into shared memory as
+// the B operand.  V chunks (tf32 hi/lo copies made by the split pass) arrive by
+// TMA, MN-major with the 32-byte-atom swizzle.  The denominator column is a
+// dot product with the same features on the CUDA cores.  Each CTA writes its
+// partial sums; the residual kernel adds the groups.
+#include "sa_common.cuh"
+#include "tc_util.cuh"
+
+namespace sa {
+
+namespace {
+
+using namespace tc;
+
+constexpr int kRows = 128;      // tokens per sub-tile = features per tile = TMEM lanes
+constexpr int kChunk = 32;      // K columns per staged feature chunk
+constexpr int kThreads = 192;   // warp 0 TMA, warp 1 MMA, warps 2..5 generators
+
+constexpr int kErrMomWait = 201, kErrMomDrain = 202;
+
+struct MomTCParams {
+  const float* q;     // [bh, n, d]
+  const float* k;     // [bh, n, d]
+  float* part;        // [G, bh, n, dv+1] partial low sums
+  int* status;
+  int64_t n, bh;
+  int d, dv, bs, F, G;
+  float scale;
+};
+
+template <int DVP>
+struct MomLayout {
+  static constexpr int kFT = (512 - DVP - 2 * 2 * kChunk) / DVP;   // state tiles per CTA
+  static_assert(kFT >= 1, "TMEM");
+  // TMEM columns
+  static constexpr uint32_t kOut = kFT * DVP;
+  static constexpr uint32_t kStg = kOut + DVP;                       // 2 buffers x (32 hi + 32 lo)
+  static_assert(kStg + 4 * kChunk <= 512, "TMEM columns");
+  // shared memory
+  static constexpr uint32_t kSbufHalf = (kRows / 32) * DVP * 128;    // one of hi / lo: 4 atoms x DVP rows x 128 B
+  static constexpr uint32_t kSbuf = 2 * kSbufHalf;                   // hi + lo
+  static constexpr uint32_t kVHalf = (DVP / 32) * kChunk * 128;     // V chunk hi or lo
+  static constexpr uint32_t kVStage = 2 * kVHalf;
+  static constexpr int kVStages = 2;
+};
+
+__device__ __forceinline__ float key_coef_tc(int a, int b, int c, int d) {
+  const bool ab = (a == b) && (a < d);
+  const bool bc = (b == c) && (b < d);
+  return (ab && bc) ? (1.0f / 6.0f) : ((ab || bc) ? 0.5f : 1.0f);
+}
+
+// named barrier among the 128 generator threads (warps 2..5)
+__device__ __forceinline__ void gen_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int DVP>
+__global__ void __launch_bounds__(kThreads, 1)
+moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl,
+                  const MomTCParams p) {
+  using L = MomLayout<DVP>;
+  constexpr int FT = L::kFT;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sbuf = smem;                                   // [2][hi, lo]
+  uint8_t* vst = sbuf + 2 * L::kSbuf;                     // [kVStages][hi, lo]
+  const int xs = (p.d + 1) | 1;                           // odd row stride, x[d] = 1
+  float* X = reinterpret_cast<float*>(vst + L::kVStages * L::kVStage);     // [128][xs]
+  uint32_t* ftab = reinterpret_cast<uint32_t*>(X + kRows * xs);            // [FT*128]
+  float* sden = reinterpret_cast<float*>(ftab + FT * kRows);               // [FT*128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(sden + FT * kRows) + 7) & ~uintptr_t(7));
+  uint64_t* stg_full = bars;        // [2] 128 arrivals
+  uint64_t* stg_free = bars + 2;    // [2] commit
+  uint64_t* sb_full = bars + 4;     // [2] 128 arrivals
+  uint64_t* sb_free = bars + 6;     // [2] commit
+  uint64_t* v_full = bars + 8;      // [2] TMA
+  uint64_t* v_free = bars + 10;     // [2] commit
+  uint64_t* out_full = bars + 12;   // commit
+  uint64_t* out_free = bars + 13;   // 128 arrivals
+  uint64_t* u_done = bars + 14;     // commit
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  int* abort_word = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = blockIdx.x;
+  const int64_t h = blockIdx.y;
+  const int f0 = g * FT * kRows;                      // first feature of this group
+  const int ntiles = min(FT, (p.F - f0 + kRows - 1) / kRows);
+  const int64_t nb = (p.n + p.bs - 1) / p.bs;
+  const int sub = (p.bs + kRows - 1) / kRows;          // 128-token sub-tiles per block
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&stg_full[b], 128);
+      mbar_init(&stg_free[b], 1);
+      mbar_init(&sb_full[b], 128);
+      mbar_init(&sb_free[b], 1);
+      mbar_init(&v_full[b], 1);
+      mbar_init(&v_free[b], 1);
+    }
+    mbar_init(out_full, 1);
+    mbar_init(out_free, 128);
+    mbar_init(u_done, 1);
+    mbar_init(drain, 1);
+    *abort_word = 0;
+    fence_mbar_init();
+  }
+  for (int f = threadIdx.x; f < FT * kRows; f += kThreads) {
+    const int ff = f0 + f;
+    if (ff < p.F) {
+      const Monomial mo = monomial_of(ff, p.d);
+      ftab[f] = (uint32_t)mo.a | ((uint32_t)mo.b << 10) | ((uint32_t)mo.c << 20);
+    } else {
+      ftab[f] = 0xFFFFFFFFu;  // padding feature: value 0
+    }
+    sden[f] = 0.0f;
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const Abort ab{abort_word, p.status};
+  const float* qh = p.q + h * p.n * p.d;
+  const float* kh = p.k + h * p.n * p.d;
+
+  if (warp == 0) {
+    // -------------------------------------------------------------- V chunks
+    if (lane == 0) {
+      int use = 0;
+      bool ok = true;
+      for (int64_t c = 0; ok && c + 1 < nb; ++c) {
+        for (int st = 0; ok && st < sub; ++st) {
+          const int64_t t0 = c * p.bs + (int64_t)st * kRows;
+          for (int tc = 0; tc < kRows / kChunk; ++tc, ++use) {
+            const int s = use & 1;
+            if (use >= 2 && !mbar_wait(&v_free[s], ((use >> 1) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+            mbar_arrive_expect_tx(&v_full[s], L::kVStage);
+            uint8_t* dst = vst + s * L::kVStage;
+            const int row = (int)(t0 + tc * kChunk);
+#pragma unroll
+            for (int a = 0; a < DVP / 32; ++a) {
+              tma_load_3d(dst + a * (kChunk * 128), &tm_vh, &v_full[s], a * 32, row, (int)h);
+              tma_load_3d(dst + L::kVHalf + a * (kChunk * 128), &tm_vl, &v_full[s], a * 32, row, (int)h);
+            }
+          }
+        }
+      }
+      for (int u = max(0, use - 2); u < use; ++u) {  // no copies left in flight
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&v_full[u & 1], (u >> 1) & 1) && globaltimer_ns() - t0 < 1000000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_q = idesc_tf32(128, DVP, false, false);  // B = S copy, K-major
+      constexpr uint32_t idesc_u = idesc_tf32(128, DVP, false, true);   // B = V chunk, MN-major
+      int stg_use = 0, sb_use = 0, v_use = 0, out_use = 0;
+      bool ok = true;
+      bool s_init = false;
+      for (int64_t c = 0; ok && c < nb; ++c) {
+        if (c > 0) {
+          const int64_t b1 = min((c + 1) * (int64_t)p.bs, p.n);
+          const int nsq = (int)((b1 - c * (int64_t)p.bs + kRows - 1) / kRows);  // query sub-tiles of block c
+          for (int st = 0; ok && st < nsq; ++st) {
+            if (out_use >= 1 && !mbar_wait(out_free, (out_use - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+            tc_fence_after();
+            for (int j = 0; ok && j < ntiles; ++j, ++sb_use) {
+              const int sb = sb_use & 1;
+              if (!mbar_wait(&sb_full[sb], (sb_use >> 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+              tc_fence_after();
+              const uint32_t bhi = smem_u32(sbuf + sb * L::kSbuf);
+              const uint32_t blo = bhi + L::kSbufHalf;
+              for (int kc = 0; kc < kRows / kChunk; ++kc, ++stg_use) {
+                const int b = stg_use & 1;
+                if (!mbar_wait(&stg_full[b], (stg_use >> 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t ahi = tmem + L::kStg + b * 2 * kChunk;
+                const uint32_t alo = ahi + kChunk;
+#pragma unroll
+                for (int kk = 0; kk < kChunk / 8; ++kk) {
+                  const uint32_t off = kc * (DVP * 128) + kk * 32;
+                  const uint64_t dh = sdesc_sw128(bhi + off, 16, 1024);
+                  const uint64_t dl = sdesc_sw128(blo + off, 16, 1024);
+                  const uint32_t acc = (j > 0 || kc > 0 || kk > 0) ? 1u : 0u;
+                  mma_tf32_ts(tmem + L::kOut, ahi + kk * 8, dh, idesc_q, acc);
+                  mma_tf32_ts(tmem + L::kOut, ahi + kk * 8, dl, idesc_q, 1u);
+                  mma_tf32_ts(tmem + L::kOut, alo + kk * 8, dh, idesc_q, 1u);
+                }
+                mma_commit(&stg_free[b]);
+              }
+              mma_commit(&sb_free[sb]);
+            }
+            if (ok) mma_commit(out_full);
+            ++out_use;
+          }
+        }
+        if (ok && c + 1 < nb) {
+          for (int st = 0; ok && st < sub; ++st) {
+            for (int tc = 0; ok && tc < kRows / kChunk; ++tc, ++v_use) {
+              const int vs = v_use & 1;
+              if (!mbar_wait(&v_full[vs], (v_use >> 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+              const uint32_t vhi = smem_u32(vst + vs * L::kVStage);
+              const uint32_t vlo = vhi + L::kVHalf;
+              for (int j = 0; ok && j < ntiles; ++j, ++stg_use) {
+                const int b = stg_use & 1;
+                if (!mbar_wait(&stg_full[b], (stg_use >> 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t ahi = tmem + L::kStg + b * 2 * kChunk;
+                const uint32_t alo = ahi + kChunk;
+                const uint32_t dS = tmem + j * DVP;
+#pragma unroll
+                for (int kk = 0; kk < kChunk / 8; ++kk) {
+                  const uint64_t dh = sdesc_sw128_atom32(vhi + kk * 1024, kChunk * 128, 512);
+                  const uint64_t dl = sdesc_sw128_atom32(vlo + kk * 1024, kChunk * 128, 512);
+                  const uint32_t acc = (s_init || kk > 0) ? 1u : 0u;
+                  mma_tf32_ts(dS, ahi + kk * 8, dh, idesc_u, acc);
+                  mma_tf32_ts(dS, ahi + kk * 8, dl, idesc_u, 1u);
+                  mma_tf32_ts(dS, alo + kk * 8, dh, idesc_u, 1u);
+                }
+                mma_commit(&stg_free[b]);
+              }
+              mma_commit(&v_free[vs]);
+              // every tile was written by its first chunk of the first completed block
+              if (st == 0 && tc == 0) s_init = true;
+            }
+          }
+          if (ok) mma_commit(u_done);
+        }
+      }
+      mma_commit(drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0)) {
+        if (globaltimer_ns() - t0 > 2000000000ull) {
+          atomicCAS(p.status, 0, kErrMomDrain);
+          break;
+        }
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- generators
+    const int quarter = warp & 3;
+    const int t = quarter * 32 + lane;                   // TMEM lane = token or feature
+    const uint32_t la = tmem + ((uint32_t)(quarter * 32) << 16);
+    int stg_use = 0, sb_use = 0, out_use = 0;
+    bool ok = true;
+    float* myrow = X + t * xs;
+    const int64_t col_stride = p.dv + 1;
+    for (int64_t c = 0; ok && c < nb; ++c) {
+      const int64_t b0 = c * p.bs;
+      const int64_t b1 = min(b0 + (int64_t)p.bs, p.n);
+      // ---------------- query phase: tokens of block c read S_{<c}
+      if (c == 0) {
+        for (int64_t i = b0 + t; i < b1; i += kRows) {
+          float* dst = p.part + ((int64_t)g * p.bh + h) * p.n * col_stride + i * col_stride;
+          for (int col = 0; col <= p.dv; ++col) dst[col] = 0.0f;
+        }
+      } else {
+        if (!mbar_wait(u_done, (int)((c - 1) & 1), ab, kErrMomWait)) { ok = false; break; }
+        tc_fence_after();
+        gen_sync();  // sden of the previous update phase is visible
+        const int nsq = (int)((b1 - b0 + kRows - 1) / kRows);  // query sub-tiles of block c
+        for (int st = 0; ok && st < nsq; ++st) {
+          const int64_t t0 = b0 + (int64_t)st * kRows;
+          const int64_t i = t0 + t;
+          const bool valid = i < b1;
+          for (int a = 0; a < p.d; ++a) myrow[a] = valid ? __ldg(qh + i * p.d + a) * p.scale : 0.0f;
+          myrow[p.d] = 1.0f;
+          float den_acc = 0.0f;
+          for (int j = 0; ok && j < ntiles; ++j, ++sb_use) {
+            // copy S_j (this thread: feature t of tile j) into the K-major B buffer
+            const int sb = sb_use & 1;
+            if (sb_use >= 2 && !mbar_wait(&sb_free[sb], ((sb_use >> 1) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+            uint8_t* bhi = sbuf + sb * L::kSbuf;
+            uint8_t* blo = bhi + L::kSbufHalf;
+            const uint32_t atom = (uint32_t)(t >> 5) * (DVP * 128);
+#pragma unroll
+            for (int cc = 0; cc < DVP / 32; ++cc) {
+              float sv[32];
+              tmem_ld32(la + j * DVP + cc * 32, sv);
+              tmem_wait_ld();
+#pragma unroll
+              for (int u = 0; u < 32; ++u) {
+                const int nrow = cc * 32 + u;
+                const uint32_t chunk = ((uint32_t)((t & 31) >> 2)) ^ (uint32_t)(nrow & 7);
+                const uint32_t off = atom + nrow * 128 + chunk * 16 + (t & 3) * 4;
+                const float hi = __uint_as_float(to_tf32(sv[u]));
+                *reinterpret_cast<float*>(bhi + off) = hi;
+                *reinterpret_cast<float*>(blo + off) = sv[u] - hi;
+              }
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&sb_full[sb]);
+            // Phi_q chunks of tile j for this thread's token
+            for (int kc = 0; kc < kRows / kChunk; ++kc, ++stg_use) {
+              const int b = stg_use & 1;
+              if (stg_use >= 2 && !mbar_wait(&stg_free[b], ((stg_use >> 1) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+              uint32_t hi[32], lo[32];
+              const int fl = j * kRows + kc * kChunk;
+#pragma unroll
+              for (int u = 0; u < 32; ++u) {
+                const uint32_t pk = ftab[fl + u];
+                float phi = 0.0f;
+                if (pk != 0xFFFFFFFFu) phi = myrow[pk & 1023] * myrow[(pk >> 10) & 1023] * myrow[pk >> 20];
+                den_acc = fmaf(phi, sden[fl + u], den_acc);
+                hi[u] = to_tf32(phi);
+                lo[u] = __float_as_uint(phi - __uint_as_float(hi[u]));
+              }
+              tmem_st32(la + L::kStg + b * 2 * kChunk, hi);
+              tmem_st32(la + L::kStg + b * 2 * kChunk + kChunk, lo);
+              tmem_wait_st();
+              tc_fence_before();
+              mbar_arrive(&stg_full[b]);
+            }
+          }
+          if (!ok) break;
+          // partial sums of this sub-tile
+          if (!mbar_wait(out_full, out_use & 1, ab, kErrMomWait)) { ok = false; break; }
+          tc_fence_after();
+          float* dst = p.part + ((int64_t)g * p.bh + h) * p.n * col_stride + i * col_stride;
+#pragma unroll
+          for (int cc = 0; cc < DVP / 32; ++cc) {
+            float ov[32];
+            tmem_ld32(la + L::kOut + cc * 32, ov);
+            tmem_wait_ld();
+            if (valid) {
+#pragma unroll
+              for (int u = 0; u < 32; ++u)
+                if (cc * 32 + u < p.dv) dst[cc * 32 + u] = ov[u];
+            }
+          }
+          if (valid) dst[p.dv] = den_acc;
+          tc_fence_before();
+          mbar_arrive(out_free);
+          ++out_use;
+        }
+      }
+      if (!ok || c + 1 >= nb) continue;
+      // ---------------- update phase: add the keys of block c
+      float sd[FT];
+#pragma unroll
+      for (int j = 0; j < FT; ++j) sd[j] = 0.0f;
+      for (int st = 0; ok && st < sub; ++st) {
+        const int64_t t0 = b0 + (int64_t)st * kRows;
+        gen_sync();  // everyone is done with X
+        {
+          const int64_t i = t0 + t;
+          const bool valid = i < b1;
+          for (int a = 0; a < p.d; ++a) myrow[a] = valid ? __ldg(kh + i * p.d + a) : 0.0f;
+          myrow[p.d] = valid ? 1.0f : 0.0f;   // an invalid token's features are all zero
+        }
+        gen_sync();
+        for (int tcn = 0; ok && tcn < kRows / kChunk; ++tcn) {
+          for (int j = 0; ok && j < ntiles; ++j, ++stg_use) {
+            const int b = stg_use & 1;
+            if (stg_use >= 2 && !mbar_wait(&stg_free[b], ((stg_use >> 1) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+            const uint32_t pk = ftab[j * kRows + t];
+            const bool live = pk != 0xFFFFFFFFu;
+            const int ia = live ? (int)(pk & 1023) : 0, ib = live ? (int)((pk >> 10) & 1023) : 0,
+                      ic = live ? (int)(pk >> 20) : 0;
+            const float cf = live ? key_coef_tc(ia, ib, ic, p.d) : 0.0f;
+            uint32_t hi[32], lo[32];
+            float acc = 0.0f;
+#pragma unroll
+            for (int u = 0; u < 32; ++u) {
+              const float* xr = X + (tcn * kChunk + u) * xs;
+              const float phi = xr[ia] * xr[ib] * xr[ic] * cf;
+              acc += phi;
+              hi[u] = to_tf32(phi);
+              lo[u] = __float_as_uint(phi - __uint_as_float(hi[u]));
+            }
+            sd[j] += acc;
+            tmem_st32(la + L::kStg + b * 2 * kChunk, hi);
+            tmem_st32(la + L::kStg + b * 2 * kChunk + kChunk, lo);
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&stg_full[b]);
+          }
+        }
+      }
+      gen_sync();  // all reads of sden by the query phase are done
+#pragma unroll
+      for (int j = 0; j < FT; ++j)
+        if (j < ntiles) sden[j * kRows + t] += sd[j];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int DVP>
+size_t mom_smem(int d) {
+  using L = MomLayout<DVP>;
+  const int xs = (d + 1) | 1;
+  return 1024 + 2 * L::kSbuf + L::kVStages * L::kVStage + (size_t)kRows * xs * 4 + (size_t)L::kFT * kRows * 8 + 16 +
+         17 * 8 + 16;
+}
+
+template <int DVP>
+int launch_mom_tc(const CUtensorMap* maps, const MomTCParams& prm, cudaStream_t stream) {
+  auto kern = moments_tc_kernel<DVP>;
+  const size_t smem = mom_smem<DVP>(prm.d);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return set_error(SA_ERR_CUDA, "moments_tc smem attribute: %s", cudaGetErrorString(e));
+  dim3 grid((unsigned)prm.G, (unsigned)prm.bh);
+  kern<<<grid, kThreads, smem, stream>>>(maps[0], maps[1], prm);
+  return check_launch("moments_tc_kernel");
+}
+
+}  // namespace
+
+// Feature groups (CTAs per sequence) the tensor-core moment kernel uses, or 0
+// when the shape is not supported (then the CUDA-core kernel runs).
+int moments_tc_groups(int d, int dv, int degree) {
+  if (dv > 64 || d > 128) return 0;
+  const int dvp = dv <= 32 ? 32 : 64;
+  const int ft = dvp == 32 ? MomLayout<32>::kFT : MomLayout<64>::kFT;
+  const int64_t F = feature_count(d, degree);
+  const int64_t tiles = (F + kRows - 1) / kRows;
+  const size_t smem = dvp == 32 ? mom_smem<32>(d) : mom_smem<64>(d);
+  if (smem > 227 * 1024) return 0;
+  return (int)((tiles + ft - 1) / ft);
+}
+
+namespace {
+__global__ void sum_groups_kernel(const float* __restrict__ part, int groups, int64_t stride, float* __restrict__ out) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < stride; e += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.0f;
+    for (int g = 0; g < groups; ++g) s += __ldg(part + g * stride + e);
+    out[e] = s;
+  }
+}
+}  // namespace
+
+// out[e] = sum_g part[g * stride + e]: the low sums from the per-group partials.
+int launch_sum_groups(const float* part, int groups, int64_t stride, float* out, cudaStream_t stream) {
+  if (stride == 0) return SA_OK;
+  const int threads = 256;
+  const int64_t blocks = min((stride + threads - 1) / threads, (int64_t)148 * 16);
+  sum_groups_kernel<<<(unsigned)blocks, threads, 0, stream>>>(part, groups, stride, out);
+  return check_launch("sum_groups_kernel");
+}
+
+// maps: split v hi / lo ([bh, n, dvp], box {32, 32, 1}, 128-byte swizzle with 32-byte atoms).
+int launch_moments_tc(const CUtensorMap* maps, const float* q, const float* k, float* part, int* status, int64_t bh,
+                      int64_t n, int d, int dv, int degree, int bs, float scale, cudaStream_t stream) {
+  if (bh == 0 || n == 0) return SA_OK;
+  const int G = moments_tc_groups(d, dv, degree);
+  if (G <= 0) return set_error(SA_ERR_UNSUPPORTED, "tensor-core moments: shape not supported");
+  if (bh > 65535) return set_error(SA_ERR_UNSUPPORTED, "too many sequences for one launch");
+  MomTCParams prm{q, k, part, status, n, bh, d, dv, bs, (int)feature_count(d, degree), G, scale};
+  if (dv <= 32) return launch_mom_tc<32>(maps, prm, stream);
+  return launch_mom_tc<64>(maps, prm, stream);
+}
+
+}  // namespace sa

@@ -42,7 +42,7 @@ constexpr int kErrWaitQ = 101, kErrWaitFull = 102, kErrWaitSfree = 103, kErrWait
 struct ResTCParams {
   const float* q;        // [bh, n, d] raw queries
   const float* rep_w;    // [bh, r_pad] rep weights (nullptr: every weight is 1)
-  const float* low;      // [bh, n, dv+1]
+  const float* low;      // [groups, bh, n, dv+1] partial low sums (summed here)
   float* out;            // [bh, n, dv]
   int* status;           // launch status word (0 = ok)
   int64_t n;
@@ -50,6 +50,8 @@ struct ResTCParams {
   int64_t r_pad;         // per-sequence stride of rep_w
   int d, dv, bs;
   float scale, eps;
+  int groups;            // partial slices in `low`
+  int64_t group_stride;  // floats between slices (bh * n * (dv+1))
 };
 
 template <int DP, int DVP>
@@ -334,8 +336,11 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     }
     if (ok && mbar_wait(ofull, 0, ab, kErrWaitO)) {
       tc_fence_after();
+      // low term: the sum of the moment kernel's `groups` partial slices
       const float* lrow = p.low + (h * p.n + (valid ? i : 0)) * (int64_t)(p.dv + 1);
-      const float dtot = valid ? __ldg(lrow + p.dv) + den : 1.0f;
+      float ldsum = 0.0f;
+      for (int gi = 0; gi < p.groups; ++gi) ldsum += valid ? __ldg(lrow + gi * p.group_stride + p.dv) : 0.0f;
+      const float dtot = valid ? ldsum + den : 1.0f;
       const float dmax = fmaxf(dtot, p.eps);
       float* orow = p.out + (h * p.n + (valid ? i : 0)) * (int64_t)p.dv;
 #pragma unroll
@@ -347,7 +352,11 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int col = cchunk * 32 + j;
-            if (col < p.dv) orow[col] = __fdiv_rn(ov[j] + __ldg(lrow + col), dmax);
+            if (col < p.dv) {
+              float lv = 0.0f;
+              for (int gi = 0; gi < p.groups; ++gi) lv += __ldg(lrow + gi * p.group_stride + col);
+              orow[col] = __fdiv_rn(ov[j] + lv, dmax);
+            }
           }
         }
       }
@@ -391,12 +400,12 @@ int residual_tc_dvp(int dv) { return dv <= 32 ? 32 : (dv <= 64 ? 64 : (dv <= 128
 
 // maps: rep_k_hi, rep_k_lo, rep_v_hi, rep_v_lo, k_hi, k_lo, v_hi, v_lo (3-D, box {32, 64, 1}).
 int launch_residual_tc(const CUtensorMap* maps, const float* q, const float* rep_w, int64_t r_pad, const float* low,
-                       float* out, int* status, int64_t bh, int64_t n, int d, int dv, int degree, int bs,
+                       int groups, float* out, int* status, int64_t bh, int64_t n, int d, int dv, int degree, int bs,
                        int64_t m_blk, float scale, float eps, cudaStream_t stream) {
   if (bh == 0 || n == 0) return SA_OK;
   if (bh > 65535 || (n + kRowsQ - 1) / kRowsQ > 2147483647LL)
     return set_error(SA_ERR_UNSUPPORTED, "grid too large for the tensor-core residual");
-  ResTCParams prm{q, rep_w, low, out, status, n, m_blk, r_pad, d, dv, bs, scale, eps};
+  ResTCParams prm{q, rep_w, low, out, status, n, m_blk, r_pad, d, dv, bs, scale, eps, groups, bh * n * (dv + 1)};
   const int dp = residual_tc_dp(d), dvp = residual_tc_dvp(dv);
   if (dp == 32 && dvp == 32) return launch_deg<32, 32>(degree, maps, prm, bh, stream);
   if (dp == 32 && dvp == 64) return launch_deg<32, 64>(degree, maps, prm, bh, stream);

@@ -78,8 +78,9 @@ def test_workspace_size_and_argument_errors_without_gpu():
     sz = ctypes.c_size_t(0)
     assert lib.sa_fast_attention_workspace_size(256, 8192, 64, 64, 2, 128, 1, ctypes.byref(sz)) == 0
     R = 63 * 64
-    # tensor-core layout: low sums, hi/lo copies of k, v and of the reps, rep weights and indices
-    expect_min = (256 * 8192 * 65 * 4 + 4 * 256 * 8192 * 64 * 4 + 4 * 256 * R * 64 * 4 + 256 * R * 4
+    # tensor-core layout: 4 partial slices of the low sums (17 feature tiles in groups of 5),
+    # hi/lo copies of k, v and of the reps, rep weights and indices
+    expect_min = (4 * 256 * 8192 * 65 * 4 + 4 * 256 * 8192 * 64 * 4 + 4 * 256 * R * 64 * 4 + 256 * R * 4
                   + 256 * R * 4)
     assert sz.value >= expect_min and sz.value < expect_min + 4096
     # argument errors return before any CUDA call

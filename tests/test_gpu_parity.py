@@ -140,8 +140,13 @@ def test_low_moment_entry_point_through_the_c_abi(dev):
     s = workloads.attention_scale(c)
     qd, kd, vd = (x.reshape(bh, n, -1).contiguous().to(dev) for x in (q, k, v))
     low = torch.empty(bh, n, dv + 1, device=dev)
+    lib = _lib.load()
+    nbytes = ctypes.c_size_t(0)
+    _lib.check(lib.sa_low_moments_workspace_size(bh, n, d, dv, 2, 96, ctypes.byref(nbytes)), "ws")
+    ws = torch.empty(max(nbytes.value, 256), device=dev, dtype=torch.uint8)
     _lib.call("sa_low_moments", qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), bh, n, d, dv, 2, 96, s,
-              low.data_ptr(), torch.cuda.current_stream().cuda_stream)
+              low.data_ptr(), ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+    assert int(ws[:4].view(torch.int32).item()) == 0
     low = low.cpu().numpy()
     for h in range(bh):
         ln, ld = O.low_terms_before_block(q.reshape(bh, n, d)[h].numpy(), k.reshape(bh, n, d)[h].numpy(),
