@@ -32,8 +32,10 @@ int launch_residual_tc(const CUtensorMap* maps, const float* q, const float* rep
                        int groups, float* out, int* status, int64_t bh, int64_t n, int d, int dv, int degree, int bs,
                        int64_t m_blk, float scale, float eps, cudaStream_t stream);
 int moments_tc_groups(int d, int dv, int degree);
-int launch_moments_tc(const CUtensorMap* maps, const float* q, const float* k, float* part, int* status, int64_t bh,
-                      int64_t n, int d, int dv, int degree, int bs, float scale, cudaStream_t stream);
+int64_t moments_tc_master_floats(int64_t bh, int d, int dv, int degree);
+int launch_moments_tc(const CUtensorMap* maps, const float* q, const float* k, float* part, float* master,
+                      int* status, int64_t bh, int64_t n, int d, int dv, int degree, int bs, float scale,
+                      cudaStream_t stream);
 int launch_sum_groups(const float* part, int groups, int64_t stride, float* out, cudaStream_t stream);
 int launch_low_moments(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d, int dv,
                        int degree, int bs, float scale, float* low, cudaStream_t stream);
@@ -99,7 +101,7 @@ struct Workspace {
   int groups = 0;
   int dp = 0, dvp = 0;
   int64_t R = 0, r_pad = 0;
-  size_t status = 0, low = 0, khi = 0, klo = 0, vhi = 0, vlo = 0;
+  size_t status = 0, low = 0, master = 0, khi = 0, klo = 0, vhi = 0, vlo = 0;
   size_t rkhi = 0, rklo = 0, rvhi = 0, rvlo = 0, rep_k = 0, rep_v = 0, rep_w = 0, rep_idx = 0, total = 0;
 };
 
@@ -125,6 +127,7 @@ Workspace plan(int64_t bh, int64_t n, int d, int dv, int degree, int bs, int com
   const size_t f = sizeof(float);
   w.status = take(sizeof(int));
   if (what != Plan::kResidualOnly) w.low = take((size_t)(w.groups > 0 ? w.groups : 1) * bh * n * (dv + 1) * f);
+  if (w.groups > 0) w.master = take((size_t)moments_tc_master_floats(bh, d, dv, degree) * f);
   const bool need_v_split = w.groups > 0 || (w.tc && what != Plan::kMomentsOnly);
   if (w.tc && what != Plan::kMomentsOnly) {
     w.khi = take((size_t)bh * n * w.dp * f);
@@ -213,15 +216,16 @@ int residual_tc_from_split(const Workspace& w, const float* const rep_src[4], in
 }
 
 // Tensor-core moments into `part` ([groups, bh, n, dv+1]) from the split v.
-int moments_tc_from_split(const Workspace& w, const float* vhi, const float* vlo, const float* q, const float* k,
-                          float* part, int* status, int64_t bh, int64_t n, int d, int dv, int degree, int block_size,
-                          float scale, cudaStream_t s) {
+int moments_tc_from_split(const Workspace& w, char* ws, const float* vhi, const float* vlo, const float* q,
+                          const float* k, float* part, int* status, int64_t bh, int64_t n, int d, int dv, int degree,
+                          int block_size, float scale, cudaStream_t s) {
   CUtensorMap maps[2];
   int rc = encode_map_3d(&maps[0], vhi, w.dvp, n, bh, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
   if (rc) return rc;
   rc = encode_map_3d(&maps[1], vlo, w.dvp, n, bh, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
   if (rc) return rc;
-  return launch_moments_tc(maps, q, k, part, status, bh, n, d, dv, degree, block_size, scale, s);
+  float* master = reinterpret_cast<float*>(ws + w.master);
+  return launch_moments_tc(maps, q, k, part, master, status, bh, n, d, dv, degree, block_size, scale, s);
 }
 
 int check_workspace(const Workspace& w, const void* workspace, size_t workspace_bytes) {
@@ -313,7 +317,7 @@ int sa_low_moments(const float* q, const float* k, const float* v, int64_t bh, i
   float* part = reinterpret_cast<float*>(ws + w.low);
   rc = launch_split(v, bh * n, dv, w.dvp, vhi, vlo, s);
   if (rc) return rc;
-  rc = moments_tc_from_split(w, vhi, vlo, q, k, part, status, bh, n, d, dv, degree, block_size, scale, s);
+  rc = moments_tc_from_split(w, ws, vhi, vlo, q, k, part, status, bh, n, d, dv, degree, block_size, scale, s);
   if (rc) return rc;
   return launch_sum_groups(part, w.groups, bh * n * (dv + 1), low, s);
 }
@@ -475,7 +479,7 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
 
   // M: low-degree moments
   if (w.groups > 0)
-    rc = moments_tc_from_split(w, vhi, vlo, q, k, low, status, bh, n, d, dv, degree, block_size, scale, s);
+    rc = moments_tc_from_split(w, ws, vhi, vlo, q, k, low, status, bh, n, d, dv, degree, block_size, scale, s);
   else
     rc = launch_low_moments(q, k, v, bh, n, d, dv, degree, block_size, scale, low, s);
   if (rc) return rc;

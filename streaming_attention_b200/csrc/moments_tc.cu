@@ -7,18 +7,24 @@
 // streaming_taylor_coreset_attention.py:118-296).
 //
 // Work split: one CTA per (group of up to FT feature tiles of 128, sequence).
-// The CTA scans the sequence block by block.  For every block it
-//   query phase  Out[128 tokens x dv] = Phi_q[tokens x features] . S_j   (M = tokens)
-//   update phase S_j[128 features x dv] += Phi_k^T[features x tokens] . V (M = features)
+// The CTA scans the sequence block by block:
+//   update phase  dS_j[128 features x dv] = Phi_k^T[features x tokens] . V   (M = features)
+//   query phase   Out_j[128 tokens x dv]  = Phi_q[tokens x features of j] . S_j (M = tokens)
 // Both feature matrices are generated on the CUDA cores directly into TMEM
 // (tcgen05.st), where they are the A operand; thread t of the four generator
 // warps owns TMEM lane t, i.e. token t in the query phase and feature t of the
-// tile in the update phase.  S_j accumulates in TMEM; before each query phase
-// it is copied (split hi/lo, K-major, 128-byte swizzle) into shared memory as
-// the B operand.  V chunks (tf32 hi/lo copies made by the split pass) arrive by
-// TMA, MN-major with the 32-byte-atom swizzle.  The denominator column is a
-// dot product with the same features on the CUDA cores.  Each CTA writes its
-// partial sums; the residual kernel adds the groups.
+// tile in the update phase.  V chunks (tf32 hi / fp32 remainder copies made
+// by the split pass) arrive by TMA, MN-major with the 32-byte-atom swizzle.
+//
+// Accumulation: tensor-core accumulation into TMEM does not round to nearest,
+// so no long sum stays there.  dS_j covers one block (<= 96 MMA steps) and is
+// folded into an fp32 master state in global memory (L2-resident, RN adds on
+// the CUDA cores) at the start of the next query phase, where the same thread
+// also writes the state's K-major hi/lo copy that is the B operand of the
+// query product.  Out_j covers one tile (48 MMA steps) and lands in tile j's
+// own TMEM columns (free after the fold); the tiles are summed in registers.
+// The denominator column is a dot product with the same features on the CUDA
+// cores.  Each CTA writes its partial sums; the residual kernel adds the groups.
 #include "sa_common.cuh"
 #include "tc_util.cuh"
 
@@ -38,6 +44,7 @@ struct MomTCParams {
   const float* q;     // [bh, n, d]
   const float* k;     // [bh, n, d]
   float* part;        // [G, bh, n, dv+1] partial low sums
+  float* master;      // [G, bh, FT*128, DVP] fp32 moment state
   int* status;
   int64_t n, bh;
   int d, dv, bs, F, G;
@@ -46,11 +53,9 @@ struct MomTCParams {
 
 template <int DVP>
 struct MomLayout {
-  static constexpr int kFT = (512 - DVP - 2 * 2 * kChunk) / DVP;   // state tiles per CTA
-  static_assert(kFT >= 1, "TMEM");
-  // TMEM columns
-  static constexpr uint32_t kOut = kFT * DVP;
-  static constexpr uint32_t kStg = kOut + DVP;                       // 2 buffers x (32 hi + 32 lo)
+  static constexpr int kFT = (512 - 2 * 2 * kChunk) / DVP;          // state tiles per CTA
+  // TMEM columns: tile j at j*DVP (dS_j, then Out_j); staging after the tiles
+  static constexpr uint32_t kStg = kFT * DVP;
   static_assert(kStg + 4 * kChunk <= 512, "TMEM columns");
   // shared memory
   static constexpr uint32_t kSbufHalf = (kRows / 32) * DVP * 128;    // one of hi / lo: 4 atoms x DVP rows x 128 B
@@ -90,9 +95,9 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
   uint64_t* sb_free = bars + 6;     // [2] commit
   uint64_t* v_full = bars + 8;      // [2] TMA
   uint64_t* v_free = bars + 10;     // [2] commit
-  uint64_t* out_full = bars + 12;   // commit
-  uint64_t* out_free = bars + 13;   // 128 arrivals
-  uint64_t* u_done = bars + 14;     // commit
+  uint64_t* out_full = bars + 12;   // commit, once per (sub-tile, tile)
+  uint64_t* out_free = bars + 13;   // 128 arrivals, once per sub-tile
+  uint64_t* u_done = bars + 14;     // commit, once per update phase
   uint64_t* drain = bars + 15;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   int* abort_word = reinterpret_cast<int*>(tmem_slot + 1);
@@ -103,7 +108,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
   const int f0 = g * FT * kRows;                      // first feature of this group
   const int ntiles = min(FT, (p.F - f0 + kRows - 1) / kRows);
   const int64_t nb = (p.n + p.bs - 1) / p.bs;
-  const int sub = (p.bs + kRows - 1) / kRows;          // 128-token sub-tiles per block
+  const int sub = (p.bs + kRows - 1) / kRows;          // 128-token sub-tiles of a full block
 
   if (threadIdx.x == 0) {
     for (int b = 0; b < 2; ++b) {
@@ -174,17 +179,16 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_q = idesc_tf32(128, DVP, false, false);  // B = S copy, K-major
+      constexpr uint32_t idesc_q = idesc_tf32(128, DVP, false, false);  // B = state copy, K-major
       constexpr uint32_t idesc_u = idesc_tf32(128, DVP, false, true);   // B = V chunk, MN-major
-      int stg_use = 0, sb_use = 0, v_use = 0, out_use = 0;
+      int stg_use = 0, sb_use = 0, v_use = 0, sub_use = 0;
       bool ok = true;
-      bool s_init = false;
       for (int64_t c = 0; ok && c < nb; ++c) {
         if (c > 0) {
           const int64_t b1 = min((c + 1) * (int64_t)p.bs, p.n);
           const int nsq = (int)((b1 - c * (int64_t)p.bs + kRows - 1) / kRows);  // query sub-tiles of block c
-          for (int st = 0; ok && st < nsq; ++st) {
-            if (out_use >= 1 && !mbar_wait(out_free, (out_use - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+          for (int st = 0; ok && st < nsq; ++st, ++sub_use) {
+            if (sub_use >= 1 && !mbar_wait(out_free, (sub_use - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
             tc_fence_after();
             for (int j = 0; ok && j < ntiles; ++j, ++sb_use) {
               const int sb = sb_use & 1;
@@ -192,6 +196,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
               tc_fence_after();
               const uint32_t bhi = smem_u32(sbuf + sb * L::kSbuf);
               const uint32_t blo = bhi + L::kSbufHalf;
+              const uint32_t dO = tmem + j * DVP;
               for (int kc = 0; kc < kRows / kChunk; ++kc, ++stg_use) {
                 const int b = stg_use & 1;
                 if (!mbar_wait(&stg_full[b], (stg_use >> 1) & 1, ab, kErrMomWait)) { ok = false; break; }
@@ -203,17 +208,15 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
                   const uint32_t off = kc * (DVP * 128) + kk * 32;
                   const uint64_t dh = sdesc_sw128(bhi + off, 16, 1024);
                   const uint64_t dl = sdesc_sw128(blo + off, 16, 1024);
-                  const uint32_t acc = (j > 0 || kc > 0 || kk > 0) ? 1u : 0u;
-                  mma_tf32_ts(tmem + L::kOut, ahi + kk * 8, dh, idesc_q, acc);
-                  mma_tf32_ts(tmem + L::kOut, ahi + kk * 8, dl, idesc_q, 1u);
-                  mma_tf32_ts(tmem + L::kOut, alo + kk * 8, dh, idesc_q, 1u);
+                  mma_tf32_ts(dO, ahi + kk * 8, dh, idesc_q, (kc > 0 || kk > 0) ? 1u : 0u);
+                  mma_tf32_ts(dO, ahi + kk * 8, dl, idesc_q, 1u);
+                  mma_tf32_ts(dO, alo + kk * 8, dh, idesc_q, 1u);
                 }
                 mma_commit(&stg_free[b]);
               }
               mma_commit(&sb_free[sb]);
+              mma_commit(out_full);
             }
-            if (ok) mma_commit(out_full);
-            ++out_use;
           }
         }
         if (ok && c + 1 < nb) {
@@ -234,7 +237,8 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
                 for (int kk = 0; kk < kChunk / 8; ++kk) {
                   const uint64_t dh = sdesc_sw128_atom32(vhi + kk * 1024, kChunk * 128, 512);
                   const uint64_t dl = sdesc_sw128_atom32(vlo + kk * 1024, kChunk * 128, 512);
-                  const uint32_t acc = (s_init || kk > 0) ? 1u : 0u;
+                  // dS_j starts from zero in every block
+                  const uint32_t acc = (st > 0 || tc > 0 || kk > 0) ? 1u : 0u;
                   mma_tf32_ts(dS, ahi + kk * 8, dh, idesc_u, acc);
                   mma_tf32_ts(dS, ahi + kk * 8, dl, idesc_u, 1u);
                   mma_tf32_ts(dS, alo + kk * 8, dh, idesc_u, 1u);
@@ -242,8 +246,6 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
                 mma_commit(&stg_free[b]);
               }
               mma_commit(&v_free[vs]);
-              // every tile was written by its first chunk of the first completed block
-              if (st == 0 && tc == 0) s_init = true;
             }
           }
           if (ok) mma_commit(u_done);
@@ -267,13 +269,15 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     bool ok = true;
     float* myrow = X + t * xs;
     const int64_t col_stride = p.dv + 1;
+    float* part_h = p.part + ((int64_t)g * p.bh + h) * p.n * col_stride;
+    float* master_h = p.master + ((int64_t)g * p.bh + h) * (int64_t)(FT * kRows) * DVP;
     for (int64_t c = 0; ok && c < nb; ++c) {
       const int64_t b0 = c * p.bs;
       const int64_t b1 = min(b0 + (int64_t)p.bs, p.n);
       // ---------------- query phase: tokens of block c read S_{<c}
       if (c == 0) {
         for (int64_t i = b0 + t; i < b1; i += kRows) {
-          float* dst = p.part + ((int64_t)g * p.bh + h) * p.n * col_stride + i * col_stride;
+          float* dst = part_h + i * col_stride;
           for (int col = 0; col <= p.dv; ++col) dst[col] = 0.0f;
         }
       } else {
@@ -282,24 +286,52 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
         gen_sync();  // sden of the previous update phase is visible
         const int nsq = (int)((b1 - b0 + kRows - 1) / kRows);  // query sub-tiles of block c
         for (int st = 0; ok && st < nsq; ++st) {
-          const int64_t t0 = b0 + (int64_t)st * kRows;
-          const int64_t i = t0 + t;
+          const int64_t i = b0 + (int64_t)st * kRows + t;
           const bool valid = i < b1;
           for (int a = 0; a < p.d; ++a) myrow[a] = valid ? __ldg(qh + i * p.d + a) * p.scale : 0.0f;
           myrow[p.d] = 1.0f;
           float den_acc = 0.0f;
+          float acc[DVP];
+#pragma unroll
+          for (int u = 0; u < DVP; ++u) acc[u] = 0.0f;
           for (int j = 0; ok && j < ntiles; ++j, ++sb_use) {
-            // copy S_j (this thread: feature t of tile j) into the K-major B buffer
+            // state row of feature t of tile j: fold dS_j (first sub-tile) into the fp32
+            // master, and write its hi/lo split into the K-major B buffer
             const int sb = sb_use & 1;
             if (sb_use >= 2 && !mbar_wait(&sb_free[sb], ((sb_use >> 1) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
             uint8_t* bhi = sbuf + sb * L::kSbuf;
             uint8_t* blo = bhi + L::kSbufHalf;
             const uint32_t atom = (uint32_t)(t >> 5) * (DVP * 128);
+            float4* mrow = reinterpret_cast<float4*>(master_h + (int64_t)(j * kRows + t) * DVP);
 #pragma unroll
             for (int cc = 0; cc < DVP / 32; ++cc) {
               float sv[32];
-              tmem_ld32(la + j * DVP + cc * 32, sv);
-              tmem_wait_ld();
+              if (st == 0) {
+                tmem_ld32(la + j * DVP + cc * 32, sv);
+                tmem_wait_ld();
+                if (c >= 2) {
+#pragma unroll
+                  for (int u4 = 0; u4 < 8; ++u4) {
+                    const float4 m4 = mrow[cc * 8 + u4];
+                    sv[4 * u4 + 0] += m4.x;
+                    sv[4 * u4 + 1] += m4.y;
+                    sv[4 * u4 + 2] += m4.z;
+                    sv[4 * u4 + 3] += m4.w;
+                  }
+                }
+#pragma unroll
+                for (int u4 = 0; u4 < 8; ++u4)
+                  mrow[cc * 8 + u4] = make_float4(sv[4 * u4], sv[4 * u4 + 1], sv[4 * u4 + 2], sv[4 * u4 + 3]);
+              } else {
+#pragma unroll
+                for (int u4 = 0; u4 < 8; ++u4) {
+                  const float4 m4 = mrow[cc * 8 + u4];
+                  sv[4 * u4 + 0] = m4.x;
+                  sv[4 * u4 + 1] = m4.y;
+                  sv[4 * u4 + 2] = m4.z;
+                  sv[4 * u4 + 3] = m4.w;
+                }
+              }
 #pragma unroll
               for (int u = 0; u < 32; ++u) {
                 const int nrow = cc * 32 + u;
@@ -310,6 +342,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
                 *reinterpret_cast<float*>(blo + off) = sv[u] - hi;
               }
             }
+            tc_fence_before();   // the dS_j reads are ordered before the MMAs that reuse its columns
             fence_proxy_async_smem();
             mbar_arrive(&sb_full[sb]);
             // Phi_q chunks of tile j for this thread's token
@@ -333,31 +366,47 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
               tc_fence_before();
               mbar_arrive(&stg_full[b]);
             }
+            if (!ok) break;
+            // Out of the previous tile (its MMAs overlap this tile's generation)
+            if (j >= 1) {
+              if (!mbar_wait(out_full, out_use & 1, ab, kErrMomWait)) { ok = false; break; }
+              ++out_use;
+              tc_fence_after();
+#pragma unroll
+              for (int cc = 0; cc < DVP / 32; ++cc) {
+                float ov[32];
+                tmem_ld32(la + (j - 1) * DVP + cc * 32, ov);
+                tmem_wait_ld();
+#pragma unroll
+                for (int u = 0; u < 32; ++u) acc[cc * 32 + u] += ov[u];
+              }
+            }
           }
           if (!ok) break;
-          // partial sums of this sub-tile
           if (!mbar_wait(out_full, out_use & 1, ab, kErrMomWait)) { ok = false; break; }
+          ++out_use;
           tc_fence_after();
-          float* dst = p.part + ((int64_t)g * p.bh + h) * p.n * col_stride + i * col_stride;
 #pragma unroll
           for (int cc = 0; cc < DVP / 32; ++cc) {
             float ov[32];
-            tmem_ld32(la + L::kOut + cc * 32, ov);
+            tmem_ld32(la + (ntiles - 1) * DVP + cc * 32, ov);
             tmem_wait_ld();
-            if (valid) {
 #pragma unroll
-              for (int u = 0; u < 32; ++u)
-                if (cc * 32 + u < p.dv) dst[cc * 32 + u] = ov[u];
-            }
+            for (int u = 0; u < 32; ++u) acc[cc * 32 + u] += ov[u];
           }
-          if (valid) dst[p.dv] = den_acc;
           tc_fence_before();
           mbar_arrive(out_free);
-          ++out_use;
+          if (valid) {
+            float* dst = part_h + i * col_stride;
+#pragma unroll
+            for (int u = 0; u < DVP; ++u)
+              if (u < p.dv) dst[u] = acc[u];
+            dst[p.dv] = den_acc;
+          }
         }
       }
       if (!ok || c + 1 >= nb) continue;
-      // ---------------- update phase: add the keys of block c
+      // ---------------- update phase: dS_j of block c
       float sd[FT];
 #pragma unroll
       for (int j = 0; j < FT; ++j) sd[j] = 0.0f;
@@ -372,25 +421,28 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
         }
         gen_sync();
         for (int tcn = 0; ok && tcn < kRows / kChunk; ++tcn) {
-          for (int j = 0; ok && j < ntiles; ++j, ++stg_use) {
+#pragma unroll
+          for (int j = 0; j < FT; ++j) {
+            if (!ok || j >= ntiles) break;
             const int b = stg_use & 1;
             if (stg_use >= 2 && !mbar_wait(&stg_free[b], ((stg_use >> 1) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+            ++stg_use;
             const uint32_t pk = ftab[j * kRows + t];
             const bool live = pk != 0xFFFFFFFFu;
             const int ia = live ? (int)(pk & 1023) : 0, ib = live ? (int)((pk >> 10) & 1023) : 0,
                       ic = live ? (int)(pk >> 20) : 0;
             const float cf = live ? key_coef_tc(ia, ib, ic, p.d) : 0.0f;
             uint32_t hi[32], lo[32];
-            float acc = 0.0f;
+            float fsum = 0.0f;
 #pragma unroll
             for (int u = 0; u < 32; ++u) {
               const float* xr = X + (tcn * kChunk + u) * xs;
               const float phi = xr[ia] * xr[ib] * xr[ic] * cf;
-              acc += phi;
+              fsum += phi;
               hi[u] = to_tf32(phi);
               lo[u] = __float_as_uint(phi - __uint_as_float(hi[u]));
             }
-            sd[j] += acc;
+            sd[j] += fsum;
             tmem_st32(la + L::kStg + b * 2 * kChunk, hi);
             tmem_st32(la + L::kStg + b * 2 * kChunk + kChunk, lo);
             tmem_wait_st();
@@ -432,6 +484,14 @@ int launch_mom_tc(const CUtensorMap* maps, const MomTCParams& prm, cudaStream_t 
   return check_launch("moments_tc_kernel");
 }
 
+__global__ void sum_groups_kernel(const float* __restrict__ part, int groups, int64_t stride, float* __restrict__ out) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < stride; e += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.0f;
+    for (int g = 0; g < groups; ++g) s += __ldg(part + g * stride + e);
+    out[e] = s;
+  }
+}
+
 }  // namespace
 
 // Feature groups (CTAs per sequence) the tensor-core moment kernel uses, or 0
@@ -447,15 +507,14 @@ int moments_tc_groups(int d, int dv, int degree) {
   return (int)((tiles + ft - 1) / ft);
 }
 
-namespace {
-__global__ void sum_groups_kernel(const float* __restrict__ part, int groups, int64_t stride, float* __restrict__ out) {
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < stride; e += (int64_t)gridDim.x * blockDim.x) {
-    float s = 0.0f;
-    for (int g = 0; g < groups; ++g) s += __ldg(part + g * stride + e);
-    out[e] = s;
-  }
+// Floats of the fp32 master state: [G, bh, FT*128, dvp].
+int64_t moments_tc_master_floats(int64_t bh, int d, int dv, int degree) {
+  const int G = moments_tc_groups(d, dv, degree);
+  if (G <= 0) return 0;
+  const int dvp = dv <= 32 ? 32 : 64;
+  const int ft = dvp == 32 ? MomLayout<32>::kFT : MomLayout<64>::kFT;
+  return (int64_t)G * bh * ft * kRows * dvp;
 }
-}  // namespace
 
 // out[e] = sum_g part[g * stride + e]: the low sums from the per-group partials.
 int launch_sum_groups(const float* part, int groups, int64_t stride, float* out, cudaStream_t stream) {
@@ -467,13 +526,14 @@ int launch_sum_groups(const float* part, int groups, int64_t stride, float* out,
 }
 
 // maps: split v hi / lo ([bh, n, dvp], box {32, 32, 1}, 128-byte swizzle with 32-byte atoms).
-int launch_moments_tc(const CUtensorMap* maps, const float* q, const float* k, float* part, int* status, int64_t bh,
-                      int64_t n, int d, int dv, int degree, int bs, float scale, cudaStream_t stream) {
+int launch_moments_tc(const CUtensorMap* maps, const float* q, const float* k, float* part, float* master,
+                      int* status, int64_t bh, int64_t n, int d, int dv, int degree, int bs, float scale,
+                      cudaStream_t stream) {
   if (bh == 0 || n == 0) return SA_OK;
   const int G = moments_tc_groups(d, dv, degree);
   if (G <= 0) return set_error(SA_ERR_UNSUPPORTED, "tensor-core moments: shape not supported");
   if (bh > 65535) return set_error(SA_ERR_UNSUPPORTED, "too many sequences for one launch");
-  MomTCParams prm{q, k, part, status, n, bh, d, dv, bs, (int)feature_count(d, degree), G, scale};
+  MomTCParams prm{q, k, part, master, status, n, bh, d, dv, bs, (int)feature_count(d, degree), G, scale};
   if (dv <= 32) return launch_mom_tc<32>(maps, prm, stream);
   return launch_mom_tc<64>(maps, prm, stream);
 }
