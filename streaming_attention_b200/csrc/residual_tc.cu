@@ -11,8 +11,10 @@
 // of the current block(s).  Roles:
 //   warp 0      TMA producer: K_hi, K_lo, V_hi, V_lo (+ rep weights) per stage
 //   warp 1      TMEM owner; lane 0 issues every tcgen05.mma and commit
-//   warps 2..5  one query row per thread (TMEM lane): write the scaled query
-//               into TMEM, turn each S tile into P = f(S), then the epilogue
+//   warps 2..9  query rows: two warps per TMEM lane quarter, one row per
+//               thread, each warp of a pair owning 32 of a tile's 64 columns;
+//               they write the scaled query into TMEM, turn each S tile into
+//               P = f(S), then run the epilogue
 // Precision: 3xTF32.  Every fp32 operand x is carried as hi = rna_tf32(x) and
 // lo = x - hi, and each product uses hi*hi + hi*lo + lo*hi, which keeps the
 // result within a few fp32 ulps (a single TF32 product loses ~11 bits).
@@ -33,7 +35,7 @@ using namespace tc;
 
 constexpr int kRowsQ = 128;    // queries per CTA = UMMA M
 constexpr int kTile = 64;      // keys per tile = N of S = K of PV
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 query rows
 
 // status codes written to the launch's status word
 constexpr int kErrWaitQ = 101, kErrWaitFull = 102, kErrWaitSfree = 103, kErrWaitP = 104, kErrWaitS = 105,
@@ -67,7 +69,7 @@ struct Layout {
   static constexpr uint32_t kS0 = 2 * DP;           // buffer b: S/P_hi at kS0 + 128 b, P_lo at kS0 + 128 b + 64
   static constexpr uint32_t kO = 2 * DP + 256;
   static_assert(kO + DVP <= 512, "TMEM columns");
-  static constexpr uint32_t kSmemBytes = kStages * kStage + kW + (2 * kStages + 10) * 8 + 64 + 1024;
+  static constexpr uint32_t kSmemBytes = kStages * kStage + kW + (2 * kStages + 10) * 8 + 64 + 2 * 128 * 4 + 1024;
 };
 
 template <int DEG>
@@ -87,6 +89,16 @@ __device__ __forceinline__ float taylor_t(float x) {
     }
   }
   return out;
+}
+
+// P_t(x) in Horner form with fused multiply-adds (within a rounding or two
+// of the reference's term recurrence).
+template <int DEG>
+__device__ __forceinline__ float taylor_fma(float x) {
+  if (DEG == 0) return 1.0f;
+  if (DEG == 1) return 1.0f + x;
+  if (DEG == 2) return fmaf(fmaf(x, 0.5f, 1.0f), x, 1.0f);
+  return fmaf(fmaf(fmaf(x, 1.0f / 6.0f, 0.5f), x, 1.0f), x, 1.0f);
 }
 
 template <int DP, int DVP, int DEG>
@@ -135,10 +147,10 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sfull[b], 1);
-      mbar_init(&pfull[b], 128);
+      mbar_init(&pfull[b], 256);
       mbar_init(&sfree[b], 1);
     }
-    mbar_init(qready, 128);
+    mbar_init(qready, 256);
     mbar_init(ofull, 1);
     mbar_init(drain, 1);
     *abort_word = 0;
@@ -257,16 +269,20 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     }
   } else {
     // ------------------------------------------------------------ query rows
+    // two warps per TMEM lane quarter: `half` 0 (warps 2..5) and 1 (warps 6..9)
+    // each own 32 of the 64 columns of every tile
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const int64_t i = q0 + row;
     const bool valid = i < p.n;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
-    // scaled query, split hi/lo, into TMEM
+    // scaled query, split hi/lo, into TMEM (each half writes its 32-column chunks)
     {
       const float* qr = p.q + (h * p.n + (valid ? i : 0)) * p.d;
 #pragma unroll
       for (int cchunk = 0; cchunk < DP / 32; ++cchunk) {
+        if ((cchunk & 1) != half) continue;
         uint32_t hi[32], lo[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
@@ -294,57 +310,79 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
       const bool with_w = rep && p.rep_w != nullptr;
       if (with_w && !mbar_wait(&full[s], (t / kStages) & 1, ab, kErrWaitFull)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t tS = lane_addr + L::kS0 + 128 * b;
+      const uint32_t tS = lane_addr + L::kS0 + 128 * b + half * 32;
       const int64_t row0 = rep ? (int64_t)t * kTile : kb0 + (int64_t)(t - n_rep) * kTile;
+      const int64_t col0 = row0 + half * 32;
+      float sv[32];
+      tmem_ld32(tS, sv);
+      tmem_wait_ld();
+      uint32_t hi[32], lo[32];
+      if (rep) {
+        const bool all_on = col0 + 32 <= lim;
+        if (with_w) {
+          const float4* w4 = reinterpret_cast<const float4*>(wbuf + s * kTile + half * 32);
 #pragma unroll
-      for (int cchunk = 0; cchunk < kTile / 32; ++cchunk) {
-        float sv[32];
-        tmem_ld32(tS + cchunk * 32, sv);
-        tmem_wait_ld();
-        uint32_t hi[32], lo[32];
-        const int64_t col0 = row0 + cchunk * 32;
-        if (rep) {
-          const float* w = with_w ? wbuf + s * kTile + cchunk * 32 : nullptr;
-          const bool all_on = col0 + 32 <= lim;
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 w = w4[j4];
+            const float ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int j = 4 * j4 + u;
+              const float x = sv[j];
+              float e = (__expf(x) - taylor_fma<DEG>(x)) * ww[u];
+              if (!all_on && col0 + j >= lim) e = 0.0f;
+              den += e;
+              hi[j] = to_tf32(e);
+              lo[j] = __float_as_uint(e - __uint_as_float(hi[j]));
+            }
+          }
+        } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const float x = sv[j];
-            float e = __expf(x) - taylor_t<DEG>(x);
-            if (w) e *= w[j];
+            float e = __expf(x) - taylor_fma<DEG>(x);
             if (!all_on && col0 + j >= lim) e = 0.0f;
             den += e;
             hi[j] = to_tf32(e);
             lo[j] = __float_as_uint(e - __uint_as_float(hi[j]));
           }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int64_t key = col0 + j;
-            float e = __expf(sv[j]);
-            if (key > i || key < bst) e = 0.0f;
-            den += e;
-            hi[j] = to_tf32(e);
-            lo[j] = __float_as_uint(e - __uint_as_float(hi[j]));
-          }
         }
-        tmem_st32(tS + cchunk * 32, hi);
-        tmem_st32(tS + 64 + cchunk * 32, lo);
+      } else {
+        const bool all_on = col0 >= bst && col0 + 31 <= i;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int64_t key = col0 + j;
+          float e = __expf(sv[j]);
+          if (!all_on && (key > i || key < bst)) e = 0.0f;
+          den += e;
+          hi[j] = to_tf32(e);
+          lo[j] = __float_as_uint(e - __uint_as_float(hi[j]));
+        }
       }
+      tmem_st32(tS, hi);
+      tmem_st32(tS + 64, lo);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&pfull[b]);
     }
+    // the two halves' denominators
+    float* den_x = reinterpret_cast<float*>(abort_word + 1);   // [2][128]
+    den_x[half * 128 + row] = den;
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    const float den_all = den_x[row] + den_x[128 + row];
     if (ok && mbar_wait(ofull, 0, ab, kErrWaitO)) {
       tc_fence_after();
       // low term: the sum of the moment kernel's `groups` partial slices
       const float* lrow = p.low + (h * p.n + (valid ? i : 0)) * (int64_t)(p.dv + 1);
       float ldsum = 0.0f;
       for (int gi = 0; gi < p.groups; ++gi) ldsum += valid ? __ldg(lrow + gi * p.group_stride + p.dv) : 0.0f;
-      const float dtot = valid ? ldsum + den : 1.0f;
+      const float dtot = valid ? ldsum + den_all : 1.0f;
       const float dmax = fmaxf(dtot, p.eps);
       float* orow = p.out + (h * p.n + (valid ? i : 0)) * (int64_t)p.dv;
 #pragma unroll
       for (int cchunk = 0; cchunk < DVP / 32; ++cchunk) {
+        if (DVP > 32 && (cchunk & 1) != half) continue;
+        if (DVP == 32 && half != 0) continue;
         float ov[32];
         tmem_ld32(lane_addr + L::kO + cchunk * 32, ov);
         tmem_wait_ld();
