@@ -11,9 +11,10 @@
 //   update phase  dS_j[128 features x dv] = Phi_k^T[features x tokens] . V   (M = features)
 //   query phase   Out_j[128 tokens x dv]  = Phi_q[tokens x features of j] . S_j (M = tokens)
 // Both feature matrices are generated on the CUDA cores directly into TMEM
-// (tcgen05.st), where they are the A operand; thread t of the four generator
-// warps owns TMEM lane t, i.e. token t in the query phase and feature t of the
-// tile in the update phase.  V chunks (tf32 hi / fp32 remainder copies made
+// (tcgen05.st), where they are the A operand.  Eight generator warps, two per
+// TMEM lane quarter: thread t of each half owns TMEM lane t, i.e. token t in
+// the query phase and feature t of the tile in the update phase, and each half
+// writes half of every chunk's columns.  V chunks (tf32 hi / fp32 remainder copies made
 // by the split pass) arrive by TMA, MN-major with the 32-byte-atom swizzle.
 //
 // Accumulation: tensor-core accumulation into TMEM does not round to nearest,
@@ -36,7 +37,7 @@ using namespace tc;
 
 constexpr int kRows = 128;      // tokens per sub-tile = features per tile = TMEM lanes
 constexpr int kChunk = 32;      // K columns per staged feature chunk
-constexpr int kThreads = 192;   // warp 0 TMA, warp 1 MMA, warps 2..5 generators
+constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 generators
 
 constexpr int kErrMomWait = 201, kErrMomDrain = 202;
 
@@ -71,10 +72,30 @@ __device__ __forceinline__ float key_coef_tc(int a, int b, int c, int d) {
   return (ab && bc) ? (1.0f / 6.0f) : ((ab || bc) ? 0.5f : 1.0f);
 }
 
-// named barrier among the 128 generator threads (warps 2..5)
-__device__ __forceinline__ void gen_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// named barrier among the 256 generator threads (warps 2..9)
+__device__ __forceinline__ void gen_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-template <int DVP>
+// HC consecutive columns (16 or 32) of this thread's TMEM lane
+template <int HC>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[HC]) {
+  if constexpr (HC == 32) {
+    tmem_ld32(taddr, v);
+  } else {
+    static_assert(HC == 16, "16 or 32 columns");
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+  }
+  tmem_wait_ld();
+}
+
+template <int DVP, bool DEG3>
 __global__ void __launch_bounds__(kThreads, 1)
 moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl,
                   const MomTCParams p) {
@@ -88,15 +109,17 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
   float* X = reinterpret_cast<float*>(vst + L::kVStages * L::kVStage);     // [128][xs]
   uint32_t* ftab = reinterpret_cast<uint32_t*>(X + kRows * xs);            // [FT*128]
   float* sden = reinterpret_cast<float*>(ftab + FT * kRows);               // [FT*128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(sden + FT * kRows) + 7) & ~uintptr_t(7));
-  uint64_t* stg_full = bars;        // [2] 128 arrivals
+  // after sden: [2][128] denominator exchange, [FT*128] sden exchange (used by the generators)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(sden + FT * kRows + 2 * kRows + FT * kRows) + 7) & ~uintptr_t(7));
+  uint64_t* stg_full = bars;        // [2] 256 arrivals
   uint64_t* stg_free = bars + 2;    // [2] commit
-  uint64_t* sb_full = bars + 4;     // [2] 128 arrivals
+  uint64_t* sb_full = bars + 4;     // [2] 256 arrivals
   uint64_t* sb_free = bars + 6;     // [2] commit
   uint64_t* v_full = bars + 8;      // [2] TMA
   uint64_t* v_free = bars + 10;     // [2] commit
   uint64_t* out_full = bars + 12;   // commit, once per (sub-tile, tile)
-  uint64_t* out_free = bars + 13;   // 128 arrivals, once per sub-tile
+  uint64_t* out_free = bars + 13;   // 256 arrivals, once per sub-tile
   uint64_t* u_done = bars + 14;     // commit, once per update phase
   uint64_t* drain = bars + 15;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
@@ -112,15 +135,15 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
 
   if (threadIdx.x == 0) {
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&stg_full[b], 128);
+      mbar_init(&stg_full[b], 256);
       mbar_init(&stg_free[b], 1);
-      mbar_init(&sb_full[b], 128);
+      mbar_init(&sb_full[b], 256);
       mbar_init(&sb_free[b], 1);
       mbar_init(&v_full[b], 1);
       mbar_init(&v_free[b], 1);
     }
     mbar_init(out_full, 1);
-    mbar_init(out_free, 128);
+    mbar_init(out_free, 256);
     mbar_init(u_done, 1);
     mbar_init(drain, 1);
     *abort_word = 0;
@@ -262,106 +285,114 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     }
   } else {
     // -------------------------------------------------------------- generators
+    // two warps per TMEM lane quarter: `half` 0 (warps 2..5) and 1 (warps 6..9);
+    // thread t owns TMEM lane t, each half owns half of every chunk's columns
+    constexpr int HC = DVP / 2;                          // state / output columns per half
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int t = quarter * 32 + lane;                   // TMEM lane = token or feature
     const uint32_t la = tmem + ((uint32_t)(quarter * 32) << 16);
     int stg_use = 0, sb_use = 0, out_use = 0;
     bool ok = true;
     float* myrow = X + t * xs;
+    const int dh = (p.d + 1) / 2;                        // row elements loaded by each half
+    const int a0 = half * dh, a1 = min(p.d, a0 + dh);
     const int64_t col_stride = p.dv + 1;
     float* part_h = p.part + ((int64_t)g * p.bh + h) * p.n * col_stride;
     float* master_h = p.master + ((int64_t)g * p.bh + h) * (int64_t)(FT * kRows) * DVP;
+    float* xch = sden + FT * kRows;                      // [2][128] exchange for the denominators
+    float* sdx = xch + 2 * kRows;                        // [FT*128] exchange for the sden sums
     for (int64_t c = 0; ok && c < nb; ++c) {
       const int64_t b0 = c * p.bs;
       const int64_t b1 = min(b0 + (int64_t)p.bs, p.n);
       // ---------------- query phase: tokens of block c read S_{<c}
       if (c == 0) {
-        for (int64_t i = b0 + t; i < b1; i += kRows) {
+        for (int64_t i = b0 + t + half * kRows; i < b1; i += 2 * kRows) {
           float* dst = part_h + i * col_stride;
           for (int col = 0; col <= p.dv; ++col) dst[col] = 0.0f;
         }
       } else {
         if (!mbar_wait(u_done, (int)((c - 1) & 1), ab, kErrMomWait)) { ok = false; break; }
         tc_fence_after();
-        gen_sync();  // sden of the previous update phase is visible
         const int nsq = (int)((b1 - b0 + kRows - 1) / kRows);  // query sub-tiles of block c
         for (int st = 0; ok && st < nsq; ++st) {
           const int64_t i = b0 + (int64_t)st * kRows + t;
           const bool valid = i < b1;
-          for (int a = 0; a < p.d; ++a) myrow[a] = valid ? __ldg(qh + i * p.d + a) * p.scale : 0.0f;
-          myrow[p.d] = 1.0f;
+          gen_sync();  // X is free, and sden of the previous update phase is visible
+          for (int a = a0; a < a1; ++a) myrow[a] = valid ? __ldg(qh + i * p.d + a) * p.scale : 0.0f;
+          if (half == 0) myrow[p.d] = 1.0f;
+          gen_sync();
           float den_acc = 0.0f;
-          float acc[DVP];
+          float acc[HC];
 #pragma unroll
-          for (int u = 0; u < DVP; ++u) acc[u] = 0.0f;
+          for (int u = 0; u < HC; ++u) acc[u] = 0.0f;
           for (int j = 0; ok && j < ntiles; ++j, ++sb_use) {
-            // state row of feature t of tile j: fold dS_j (first sub-tile) into the fp32
-            // master, and write its hi/lo split into the K-major B buffer
+            // state row of feature t of tile j, this half's columns: fold dS_j (first sub-tile)
+            // into the fp32 master and write its hi/lo split into the K-major B buffer
             const int sb = sb_use & 1;
             if (sb_use >= 2 && !mbar_wait(&sb_free[sb], ((sb_use >> 1) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
             uint8_t* bhi = sbuf + sb * L::kSbuf;
             uint8_t* blo = bhi + L::kSbufHalf;
             const uint32_t atom = (uint32_t)(t >> 5) * (DVP * 128);
-            float4* mrow = reinterpret_cast<float4*>(master_h + (int64_t)(j * kRows + t) * DVP);
+            float4* mrow = reinterpret_cast<float4*>(master_h + (int64_t)(j * kRows + t) * DVP + half * HC);
+            float sv[HC];
+            if (st == 0) {
+              tmem_ld_cols<HC>(la + j * DVP + half * HC, sv);
+              if (c >= 2) {
 #pragma unroll
-            for (int cc = 0; cc < DVP / 32; ++cc) {
-              float sv[32];
-              if (st == 0) {
-                tmem_ld32(la + j * DVP + cc * 32, sv);
-                tmem_wait_ld();
-                if (c >= 2) {
-#pragma unroll
-                  for (int u4 = 0; u4 < 8; ++u4) {
-                    const float4 m4 = mrow[cc * 8 + u4];
-                    sv[4 * u4 + 0] += m4.x;
-                    sv[4 * u4 + 1] += m4.y;
-                    sv[4 * u4 + 2] += m4.z;
-                    sv[4 * u4 + 3] += m4.w;
-                  }
-                }
-#pragma unroll
-                for (int u4 = 0; u4 < 8; ++u4)
-                  mrow[cc * 8 + u4] = make_float4(sv[4 * u4], sv[4 * u4 + 1], sv[4 * u4 + 2], sv[4 * u4 + 3]);
-              } else {
-#pragma unroll
-                for (int u4 = 0; u4 < 8; ++u4) {
-                  const float4 m4 = mrow[cc * 8 + u4];
-                  sv[4 * u4 + 0] = m4.x;
-                  sv[4 * u4 + 1] = m4.y;
-                  sv[4 * u4 + 2] = m4.z;
-                  sv[4 * u4 + 3] = m4.w;
+                for (int u4 = 0; u4 < HC / 4; ++u4) {
+                  const float4 m4 = mrow[u4];
+                  sv[4 * u4 + 0] += m4.x;
+                  sv[4 * u4 + 1] += m4.y;
+                  sv[4 * u4 + 2] += m4.z;
+                  sv[4 * u4 + 3] += m4.w;
                 }
               }
 #pragma unroll
-              for (int u = 0; u < 32; ++u) {
-                const int nrow = cc * 32 + u;
-                const uint32_t chunk = ((uint32_t)((t & 31) >> 2)) ^ (uint32_t)(nrow & 7);
-                const uint32_t off = atom + nrow * 128 + chunk * 16 + (t & 3) * 4;
-                const float hi = __uint_as_float(to_tf32(sv[u]));
-                *reinterpret_cast<float*>(bhi + off) = hi;
-                *reinterpret_cast<float*>(blo + off) = sv[u] - hi;
+              for (int u4 = 0; u4 < HC / 4; ++u4)
+                mrow[u4] = make_float4(sv[4 * u4], sv[4 * u4 + 1], sv[4 * u4 + 2], sv[4 * u4 + 3]);
+            } else {
+#pragma unroll
+              for (int u4 = 0; u4 < HC / 4; ++u4) {
+                const float4 m4 = mrow[u4];
+                sv[4 * u4 + 0] = m4.x;
+                sv[4 * u4 + 1] = m4.y;
+                sv[4 * u4 + 2] = m4.z;
+                sv[4 * u4 + 3] = m4.w;
               }
+            }
+#pragma unroll
+            for (int u = 0; u < HC; ++u) {
+              const int nrow = half * HC + u;
+              const uint32_t chunk = ((uint32_t)((t & 31) >> 2)) ^ (uint32_t)(nrow & 7);
+              const uint32_t off = atom + nrow * 128 + chunk * 16 + (t & 3) * 4;
+              const float hi = __uint_as_float(to_tf32(sv[u]));
+              *reinterpret_cast<float*>(bhi + off) = hi;
+              *reinterpret_cast<float*>(blo + off) = sv[u] - hi;
             }
             tc_fence_before();   // the dS_j reads are ordered before the MMAs that reuse its columns
             fence_proxy_async_smem();
             mbar_arrive(&sb_full[sb]);
-            // Phi_q chunks of tile j for this thread's token
+            // Phi_q chunks of tile j for this thread's token: 16 features per half
             for (int kc = 0; kc < kRows / kChunk; ++kc, ++stg_use) {
               const int b = stg_use & 1;
               if (stg_use >= 2 && !mbar_wait(&stg_free[b], ((stg_use >> 1) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
-              uint32_t hi[32], lo[32];
-              const int fl = j * kRows + kc * kChunk;
+              uint32_t hi[16], lo[16];
+              const int fl = j * kRows + kc * kChunk + half * 16;
 #pragma unroll
-              for (int u = 0; u < 32; ++u) {
+              for (int u = 0; u < 16; ++u) {
                 const uint32_t pk = ftab[fl + u];
                 float phi = 0.0f;
-                if (pk != 0xFFFFFFFFu) phi = myrow[pk & 1023] * myrow[(pk >> 10) & 1023] * myrow[pk >> 20];
+                if (pk != 0xFFFFFFFFu) {
+                  phi = myrow[pk & 1023] * myrow[(pk >> 10) & 1023];
+                  if (DEG3) phi *= myrow[pk >> 20];
+                }
                 den_acc = fmaf(phi, sden[fl + u], den_acc);
                 hi[u] = to_tf32(phi);
                 lo[u] = __float_as_uint(phi - __uint_as_float(hi[u]));
               }
-              tmem_st32(la + L::kStg + b * 2 * kChunk, hi);
-              tmem_st32(la + L::kStg + b * 2 * kChunk + kChunk, lo);
+              tmem_st16(la + L::kStg + b * 2 * kChunk + half * 16, hi);
+              tmem_st16(la + L::kStg + b * 2 * kChunk + kChunk + half * 16, lo);
               tmem_wait_st();
               tc_fence_before();
               mbar_arrive(&stg_full[b]);
@@ -372,36 +403,32 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
               if (!mbar_wait(out_full, out_use & 1, ab, kErrMomWait)) { ok = false; break; }
               ++out_use;
               tc_fence_after();
+              float ov[HC];
+              tmem_ld_cols<HC>(la + (j - 1) * DVP + half * HC, ov);
 #pragma unroll
-              for (int cc = 0; cc < DVP / 32; ++cc) {
-                float ov[32];
-                tmem_ld32(la + (j - 1) * DVP + cc * 32, ov);
-                tmem_wait_ld();
-#pragma unroll
-                for (int u = 0; u < 32; ++u) acc[cc * 32 + u] += ov[u];
-              }
+              for (int u = 0; u < HC; ++u) acc[u] += ov[u];
             }
           }
           if (!ok) break;
           if (!mbar_wait(out_full, out_use & 1, ab, kErrMomWait)) { ok = false; break; }
           ++out_use;
           tc_fence_after();
+          {
+            float ov[HC];
+            tmem_ld_cols<HC>(la + (ntiles - 1) * DVP + half * HC, ov);
 #pragma unroll
-          for (int cc = 0; cc < DVP / 32; ++cc) {
-            float ov[32];
-            tmem_ld32(la + (ntiles - 1) * DVP + cc * 32, ov);
-            tmem_wait_ld();
-#pragma unroll
-            for (int u = 0; u < 32; ++u) acc[cc * 32 + u] += ov[u];
+            for (int u = 0; u < HC; ++u) acc[u] += ov[u];
           }
           tc_fence_before();
           mbar_arrive(out_free);
+          xch[half * kRows + t] = den_acc;
+          gen_sync();
           if (valid) {
             float* dst = part_h + i * col_stride;
 #pragma unroll
-            for (int u = 0; u < DVP; ++u)
-              if (u < p.dv) dst[u] = acc[u];
-            dst[p.dv] = den_acc;
+            for (int u = 0; u < HC; ++u)
+              if (half * HC + u < p.dv) dst[half * HC + u] = acc[u];
+            if (half == 0) dst[p.dv] = xch[t] + xch[kRows + t];
           }
         }
       }
@@ -416,8 +443,8 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
         {
           const int64_t i = t0 + t;
           const bool valid = i < b1;
-          for (int a = 0; a < p.d; ++a) myrow[a] = valid ? __ldg(kh + i * p.d + a) : 0.0f;
-          myrow[p.d] = valid ? 1.0f : 0.0f;   // an invalid token's features are all zero
+          for (int a = a0; a < a1; ++a) myrow[a] = valid ? __ldg(kh + i * p.d + a) : 0.0f;
+          if (half == 0) myrow[p.d] = valid ? 1.0f : 0.0f;   // an invalid token's features are all zero
         }
         gen_sync();
         for (int tcn = 0; ok && tcn < kRows / kChunk; ++tcn) {
@@ -432,29 +459,38 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
             const int ia = live ? (int)(pk & 1023) : 0, ib = live ? (int)((pk >> 10) & 1023) : 0,
                       ic = live ? (int)(pk >> 20) : 0;
             const float cf = live ? key_coef_tc(ia, ib, ic, p.d) : 0.0f;
-            uint32_t hi[32], lo[32];
+            uint32_t hi[16], lo[16];
             float fsum = 0.0f;
 #pragma unroll
-            for (int u = 0; u < 32; ++u) {
-              const float* xr = X + (tcn * kChunk + u) * xs;
-              const float phi = xr[ia] * xr[ib] * xr[ic] * cf;
+            for (int u = 0; u < 16; ++u) {
+              const float* xr = X + (tcn * kChunk + half * 16 + u) * xs;
+              float phi = xr[ia] * cf * xr[ib];
+              if (DEG3) phi *= xr[ic];
               fsum += phi;
               hi[u] = to_tf32(phi);
               lo[u] = __float_as_uint(phi - __uint_as_float(hi[u]));
             }
             sd[j] += fsum;
-            tmem_st32(la + L::kStg + b * 2 * kChunk, hi);
-            tmem_st32(la + L::kStg + b * 2 * kChunk + kChunk, lo);
+            tmem_st16(la + L::kStg + b * 2 * kChunk + half * 16, hi);
+            tmem_st16(la + L::kStg + b * 2 * kChunk + kChunk + half * 16, lo);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&stg_full[b]);
           }
         }
       }
-      gen_sync();  // all reads of sden by the query phase are done
+      // s += the features of this block's keys: the halves' sums meet in shared memory
+      if (half == 1) {
 #pragma unroll
-      for (int j = 0; j < FT; ++j)
-        if (j < ntiles) sden[j * kRows + t] += sd[j];
+        for (int j = 0; j < FT; ++j)
+          if (j < ntiles) sdx[j * kRows + t] = sd[j];
+      }
+      gen_sync();  // all reads of sden by the query phase are done; sdx is written
+      if (half == 0) {
+#pragma unroll
+        for (int j = 0; j < FT; ++j)
+          if (j < ntiles) sden[j * kRows + t] += sd[j] + sdx[j * kRows + t];
+      }
     }
   }
   tc_fence_before();
@@ -469,13 +505,13 @@ template <int DVP>
 size_t mom_smem(int d) {
   using L = MomLayout<DVP>;
   const int xs = (d + 1) | 1;
-  return 1024 + 2 * L::kSbuf + L::kVStages * L::kVStage + (size_t)kRows * xs * 4 + (size_t)L::kFT * kRows * 8 + 16 +
-         17 * 8 + 16;
+  return 1024 + 2 * L::kSbuf + L::kVStages * L::kVStage + (size_t)kRows * xs * 4 + (size_t)L::kFT * kRows * 12 +
+         2 * kRows * 4 + 16 + 17 * 8 + 16;
 }
 
-template <int DVP>
+template <int DVP, bool DEG3>
 int launch_mom_tc(const CUtensorMap* maps, const MomTCParams& prm, cudaStream_t stream) {
-  auto kern = moments_tc_kernel<DVP>;
+  auto kern = moments_tc_kernel<DVP, DEG3>;
   const size_t smem = mom_smem<DVP>(prm.d);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_error(SA_ERR_CUDA, "moments_tc smem attribute: %s", cudaGetErrorString(e));
@@ -534,8 +570,8 @@ int launch_moments_tc(const CUtensorMap* maps, const float* q, const float* k, f
   if (G <= 0) return set_error(SA_ERR_UNSUPPORTED, "tensor-core moments: shape not supported");
   if (bh > 65535) return set_error(SA_ERR_UNSUPPORTED, "too many sequences for one launch");
   MomTCParams prm{q, k, part, master, status, n, bh, d, dv, bs, (int)feature_count(d, degree), G, scale};
-  if (dv <= 32) return launch_mom_tc<32>(maps, prm, stream);
-  return launch_mom_tc<64>(maps, prm, stream);
+  if (degree == 3) return dv <= 32 ? launch_mom_tc<32, true>(maps, prm, stream) : launch_mom_tc<64, true>(maps, prm, stream);
+  return dv <= 32 ? launch_mom_tc<32, false>(maps, prm, stream) : launch_mom_tc<64, false>(maps, prm, stream);
 }
 
 }  // namespace sa
