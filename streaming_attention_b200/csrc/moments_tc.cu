@@ -6,6 +6,18 @@
 // completed blocks before c (fast_article_attention.py:151-259,
 // streaming_taylor_coreset_attention.py:118-296).
 //
+// Feature layout.  The monomials are enumerated in aligned runs of 8
+// ("segments") that share a prefix: value = x~[p1] * x~[p2] * x~[c0 + u],
+// u = 0..7, over the extended row x~ of DX = dp + 8 entries (dp = d rounded up
+// to 8): x~[0,d) = x, x~[d,dp) = 0, x~[dp] = 1, the rest 0.  Rows:
+//   constant + linear   p1 = p2 = dp, c over [0, DX)
+//   degree 2            p1 = a, p2 = dp, c over [8 floor(a/8), dp), a < d
+//   degree 3            p1 = a, p2 = b, c over [8 floor(b/8), dp), a <= b < d
+// A segment position that is not a canonical monomial (c below the prefix, or
+// past d) gets key coefficient 0, so its state row stays exactly zero and its
+// query-side value never matters.  This spends ~10% extra MMA work (degree 2,
+// d = 64) to let every feature run be produced with vector loads.
+//
 // Work split: one CTA per (group of up to FT feature tiles of 128, sequence).
 // The CTA scans the sequence block by block:
 //   update phase  dS_j[128 features x dv] = Phi_k^T[features x tokens] . V   (M = features)
@@ -13,19 +25,21 @@
 // Both feature matrices are generated on the CUDA cores directly into TMEM
 // (tcgen05.st), where they are the A operand.  Eight generator warps, two per
 // TMEM lane quarter: thread t of each half owns TMEM lane t, i.e. token t in
-// the query phase and feature t of the tile in the update phase, and each half
-// writes half of every chunk's columns.  V chunks (tf32 hi / fp32 remainder copies made
-// by the split pass) arrive by TMA, MN-major with the 32-byte-atom swizzle.
+// the query phase and feature t of the tile in the update phase, and each
+// half writes half of every chunk's columns.  V chunks (tf32 hi / fp32
+// remainder copies made by the split pass) arrive by TMA, MN-major with the
+// 32-byte-atom swizzle.
 //
 // Accumulation: tensor-core accumulation into TMEM does not round to nearest,
 // so no long sum stays there.  dS_j covers one block (<= 96 MMA steps) and is
 // folded into an fp32 master state in global memory (L2-resident, RN adds on
 // the CUDA cores) at the start of the next query phase, where the same thread
-// also writes the state's K-major hi/lo copy that is the B operand of the
-// query product.  Out_j covers one tile (48 MMA steps) and lands in tile j's
-// own TMEM columns (free after the fold); the tiles are summed in registers.
-// The denominator column is a dot product with the same features on the CUDA
-// cores.  Each CTA writes its partial sums; the residual kernel adds the groups.
+// also writes the state's hi/lo split (MN-major, 32-byte-atom swizzle) that is
+// the B operand of the query product.  Out_j covers one tile (48 MMA steps)
+// and lands in tile j's own TMEM columns (free after the fold); the tiles are
+// summed in registers.  The denominator column is a dot product with the same
+// features on the CUDA cores.  Each CTA writes its partial sums; the residual
+// kernel adds the groups.
 #include "sa_common.cuh"
 #include "tc_util.cuh"
 
@@ -38,6 +52,8 @@ using namespace tc;
 constexpr int kRows = 128;      // tokens per sub-tile = features per tile = TMEM lanes
 constexpr int kChunk = 32;      // K columns per staged feature chunk
 constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 generators
+constexpr int kNStg = 3;        // TMEM staging buffers (32 hi + 32 lo columns each)
+constexpr int kXtStride = kRows + 4;   // transposed key tile row (floats)
 
 constexpr int kErrMomWait = 201, kErrMomDrain = 202;
 
@@ -48,28 +64,103 @@ struct MomTCParams {
   float* master;      // [G, bh, FT*128, DVP] fp32 moment state
   int* status;
   int64_t n, bh;
-  int d, dv, bs, F, G;
+  int d, dv, bs, degree, nseg, G;
   float scale;
 };
 
 template <int DVP>
 struct MomLayout {
-  static constexpr int kFT = (512 - 2 * 2 * kChunk) / DVP;          // state tiles per CTA
+  static constexpr int kFT = (512 - kNStg * 2 * kChunk) / DVP;      // state tiles per CTA
   // TMEM columns: tile j at j*DVP (dS_j, then Out_j); staging after the tiles
   static constexpr uint32_t kStg = kFT * DVP;
-  static_assert(kStg + 4 * kChunk <= 512, "TMEM columns");
+  static_assert(kStg + kNStg * 2 * kChunk <= 512, "TMEM columns");
   // shared memory
-  static constexpr uint32_t kSbufHalf = (kRows / 32) * DVP * 128;    // one of hi / lo: 4 atoms x DVP rows x 128 B
+  static constexpr uint32_t kSbufHalf = (DVP / 32) * kRows * 128;    // hi or lo: DVP/32 chunks x 128 rows x 128 B
   static constexpr uint32_t kSbuf = 2 * kSbufHalf;                   // hi + lo
   static constexpr uint32_t kVHalf = (DVP / 32) * kChunk * 128;     // V chunk hi or lo
   static constexpr uint32_t kVStage = 2 * kVHalf;
   static constexpr int kVStages = 2;
 };
 
-__device__ __forceinline__ float key_coef_tc(int a, int b, int c, int d) {
-  const bool ab = (a == b) && (a < d);
-  const bool bc = (b == c) && (b < d);
-  return (ab && bc) ? (1.0f / 6.0f) : ((ab || bc) ? 0.5f : 1.0f);
+__host__ __device__ inline int dpad8(int d) { return (d + 7) / 8 * 8; }
+
+}  // namespace
+
+// Number of 8-feature segments (see the layout above).
+__host__ __device__ int64_t mom_seg_count(int d, int t) {
+  const int dp = dpad8(d), w = dp / 8;
+  int64_t n = w + 1;
+  if (t >= 2)
+    for (int a = 0; a < d; ++a) n += w - a / 8;
+  if (t >= 3)
+    for (int b = 0; b < d; ++b) n += (int64_t)(b + 1) * (w - b / 8);
+  return n;
+}
+
+namespace {
+
+// segment s -> prefix indices and first c; past the end: a zero segment
+__device__ void seg_of(int64_t s, int d, int t, int& p1, int& p2, int& c0) {
+  const int dp = dpad8(d), w = dp / 8;
+  if (s < w + 1) {
+    p1 = p2 = dp;
+    c0 = 8 * (int)s;
+    return;
+  }
+  s -= w + 1;
+  if (t >= 2) {
+    for (int a = 0; a < d; ++a) {
+      const int cnt = w - a / 8;
+      if (s < cnt) {
+        p1 = a;
+        p2 = dp;
+        c0 = 8 * (a / 8 + (int)s);
+        return;
+      }
+      s -= cnt;
+    }
+  }
+  if (t >= 3) {
+    for (int b = 0; b < d; ++b) {
+      const int cnt = w - b / 8;
+      for (int a = 0; a <= b; ++a) {
+        if (s < cnt) {
+          p1 = a;
+          p2 = b;
+          c0 = 8 * (b / 8 + (int)s);
+          return;
+        }
+        s -= cnt;
+      }
+    }
+  }
+  p1 = p2 = dp + 1;  // x~[dp+1] == 0
+  c0 = dp;
+}
+
+// Key-side factor of x~[p1] x~[p2] x~[c]: 1/prod(alpha_j!) for a canonical
+// monomial of degree <= t (streaming_taylor_coreset_attention.py:78-93), else 0.
+__device__ float seg_key_coef(int p1, int p2, int c, int d, int t) {
+  const int dp = dpad8(d);
+  if (p1 > dp || p2 > dp) return 0.0f;
+  if (c >= d && c != dp) return 0.0f;
+  int idx[3];
+  int k = 0;
+  if (p1 < d) idx[k++] = p1;
+  if (p2 < d) idx[k++] = p2;
+  if (c < d) idx[k++] = c;
+  if (k > t) return 0.0f;
+  if (p2 < d) {
+    if (c < p2) return 0.0f;
+  } else if (p1 < d) {
+    if (c < p1) return 0.0f;
+  }
+  if (k == 2 && idx[0] == idx[1]) return 0.5f;
+  if (k == 3) {
+    if (idx[0] == idx[1] && idx[1] == idx[2]) return 1.0f / 6.0f;
+    if (idx[0] == idx[1] || idx[1] == idx[2]) return 0.5f;
+  }
+  return 1.0f;
 }
 
 // named barrier among the 256 generator threads (warps 2..9)
@@ -95,48 +186,56 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[HC]) {
   tmem_wait_ld();
 }
 
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
 template <int DVP, bool DEG3>
 __global__ void __launch_bounds__(kThreads, 1)
 moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl,
                   const MomTCParams p) {
   using L = MomLayout<DVP>;
   constexpr int FT = L::kFT;
+  constexpr int HC = DVP / 2;                              // state / output columns per half
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sbuf = smem;                                   // [2][hi, lo]
-  uint8_t* vst = sbuf + 2 * L::kSbuf;                     // [kVStages][hi, lo]
-  const int xs = (p.d + 1) | 1;                           // odd row stride, x[d] = 1
-  float* X = reinterpret_cast<float*>(vst + L::kVStages * L::kVStage);     // [128][xs]
-  uint32_t* ftab = reinterpret_cast<uint32_t*>(X + kRows * xs);            // [FT*128]
-  float* sden = reinterpret_cast<float*>(ftab + FT * kRows);               // [FT*128]
-  // after sden: [2][128] denominator exchange, [FT*128] sden exchange (used by the generators)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(
-      (reinterpret_cast<uintptr_t>(sden + FT * kRows + 2 * kRows + FT * kRows) + 7) & ~uintptr_t(7));
-  uint64_t* stg_full = bars;        // [2] 256 arrivals
-  uint64_t* stg_free = bars + 2;    // [2] commit
-  uint64_t* sb_full = bars + 4;     // [2] 256 arrivals
-  uint64_t* sb_free = bars + 6;     // [2] commit
-  uint64_t* v_full = bars + 8;      // [2] TMA
-  uint64_t* v_free = bars + 10;     // [2] commit
-  uint64_t* out_full = bars + 12;   // commit, once per (sub-tile, tile)
-  uint64_t* out_free = bars + 13;   // 256 arrivals, once per sub-tile
-  uint64_t* u_done = bars + 14;     // commit, once per update phase
-  uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint8_t* sbuf = smem;                                    // [2][hi, lo]
+  uint8_t* vst = sbuf + 2 * L::kSbuf;                      // [kVStages][hi, lo]
+  const int dp = dpad8(p.d);
+  const int DX = dp + 8;                                   // extended row length
+  const int XS = DX + 4;                                   // query tile row stride
+  float* X = reinterpret_cast<float*>(vst + L::kVStages * L::kVStage);   // query: [128][XS]; update: [DX][kXtStride]
+  const int xwords = max(kRows * XS, DX * kXtStride);
+  uint32_t* segtab = reinterpret_cast<uint32_t*>(X + xwords);            // [FT*16]
+  float* sden = reinterpret_cast<float*>(segtab + FT * 16);              // [FT*128]
+  float* xch = sden + FT * kRows;                                        // [2][128]
+  float* sdx = xch + 2 * kRows;                                          // [FT*128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(sdx + FT * kRows) + 7) & ~uintptr_t(7));
+  uint64_t* stg_full = bars;                // [kNStg] 256 arrivals
+  uint64_t* stg_free = bars + kNStg;        // [kNStg] commit
+  uint64_t* sb_full = bars + 2 * kNStg;     // [2] 256 arrivals
+  uint64_t* sb_free = sb_full + 2;          // [2] commit
+  uint64_t* v_full = sb_free + 2;           // [2] TMA
+  uint64_t* v_free = v_full + 2;            // [2] commit
+  uint64_t* out_full = v_free + 2;          // commit, once per (sub-tile, tile)
+  uint64_t* out_free = out_full + 1;        // 256 arrivals, once per sub-tile
+  uint64_t* u_done = out_free + 1;          // commit, once per update phase
+  uint64_t* drain = u_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_word = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = blockIdx.x;
   const int64_t h = blockIdx.y;
-  const int f0 = g * FT * kRows;                      // first feature of this group
-  const int ntiles = min(FT, (p.F - f0 + kRows - 1) / kRows);
+  const int seg0 = g * FT * 16;                       // first segment of this group
+  const int ntiles = min(FT, (p.nseg - seg0 + 15) / 16);
   const int64_t nb = (p.n + p.bs - 1) / p.bs;
   const int sub = (p.bs + kRows - 1) / kRows;          // 128-token sub-tiles of a full block
 
   if (threadIdx.x == 0) {
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kNStg; ++b) {
       mbar_init(&stg_full[b], 256);
       mbar_init(&stg_free[b], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
       mbar_init(&sb_full[b], 256);
       mbar_init(&sb_free[b], 1);
       mbar_init(&v_full[b], 1);
@@ -149,16 +248,12 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     *abort_word = 0;
     fence_mbar_init();
   }
-  for (int f = threadIdx.x; f < FT * kRows; f += kThreads) {
-    const int ff = f0 + f;
-    if (ff < p.F) {
-      const Monomial mo = monomial_of(ff, p.d);
-      ftab[f] = (uint32_t)mo.a | ((uint32_t)mo.b << 10) | ((uint32_t)mo.c << 20);
-    } else {
-      ftab[f] = 0xFFFFFFFFu;  // padding feature: value 0
-    }
-    sden[f] = 0.0f;
+  for (int s = threadIdx.x; s < FT * 16; s += kThreads) {
+    int p1, p2, c0;
+    seg_of(seg0 + s, p.d, p.degree, p1, p2, c0);
+    segtab[s] = (uint32_t)p1 | ((uint32_t)p2 << 10) | ((uint32_t)c0 << 20);
   }
+  for (int f = threadIdx.x; f < FT * kRows; f += kThreads) sden[f] = 0.0f;
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -202,8 +297,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_q = idesc_tf32(128, DVP, false, false);  // B = state copy, K-major
-      constexpr uint32_t idesc_u = idesc_tf32(128, DVP, false, true);   // B = V chunk, MN-major
+      constexpr uint32_t idesc = idesc_tf32(128, DVP, false, true);  // B MN-major in both products
       int stg_use = 0, sb_use = 0, v_use = 0, sub_use = 0;
       bool ok = true;
       for (int64_t c = 0; ok && c < nb; ++c) {
@@ -221,19 +315,19 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
               const uint32_t blo = bhi + L::kSbufHalf;
               const uint32_t dO = tmem + j * DVP;
               for (int kc = 0; kc < kRows / kChunk; ++kc, ++stg_use) {
-                const int b = stg_use & 1;
-                if (!mbar_wait(&stg_full[b], (stg_use >> 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+                const int b = stg_use % kNStg;
+                if (!mbar_wait(&stg_full[b], (stg_use / kNStg) & 1, ab, kErrMomWait)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t ahi = tmem + L::kStg + b * 2 * kChunk;
                 const uint32_t alo = ahi + kChunk;
 #pragma unroll
                 for (int kk = 0; kk < kChunk / 8; ++kk) {
-                  const uint32_t off = kc * (DVP * 128) + kk * 32;
-                  const uint64_t dh = sdesc_sw128(bhi + off, 16, 1024);
-                  const uint64_t dl = sdesc_sw128(blo + off, 16, 1024);
-                  mma_tf32_ts(dO, ahi + kk * 8, dh, idesc_q, (kc > 0 || kk > 0) ? 1u : 0u);
-                  mma_tf32_ts(dO, ahi + kk * 8, dl, idesc_q, 1u);
-                  mma_tf32_ts(dO, alo + kk * 8, dh, idesc_q, 1u);
+                  const uint32_t off = (kc * kChunk + kk * 8) * 128;   // 8 feature rows of 128 B
+                  const uint64_t dh = sdesc_sw128_atom32(bhi + off, kRows * 128, 512);
+                  const uint64_t dl = sdesc_sw128_atom32(blo + off, kRows * 128, 512);
+                  mma_tf32_ts(dO, ahi + kk * 8, dh, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+                  mma_tf32_ts(dO, ahi + kk * 8, dl, idesc, 1u);
+                  mma_tf32_ts(dO, alo + kk * 8, dh, idesc, 1u);
                 }
                 mma_commit(&stg_free[b]);
               }
@@ -250,8 +344,8 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
               const uint32_t vhi = smem_u32(vst + vs * L::kVStage);
               const uint32_t vlo = vhi + L::kVHalf;
               for (int j = 0; ok && j < ntiles; ++j, ++stg_use) {
-                const int b = stg_use & 1;
-                if (!mbar_wait(&stg_full[b], (stg_use >> 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+                const int b = stg_use % kNStg;
+                if (!mbar_wait(&stg_full[b], (stg_use / kNStg) & 1, ab, kErrMomWait)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t ahi = tmem + L::kStg + b * 2 * kChunk;
                 const uint32_t alo = ahi + kChunk;
@@ -262,9 +356,9 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
                   const uint64_t dl = sdesc_sw128_atom32(vlo + kk * 1024, kChunk * 128, 512);
                   // dS_j starts from zero in every block
                   const uint32_t acc = (st > 0 || tc > 0 || kk > 0) ? 1u : 0u;
-                  mma_tf32_ts(dS, ahi + kk * 8, dh, idesc_u, acc);
-                  mma_tf32_ts(dS, ahi + kk * 8, dl, idesc_u, 1u);
-                  mma_tf32_ts(dS, alo + kk * 8, dh, idesc_u, 1u);
+                  mma_tf32_ts(dS, ahi + kk * 8, dh, idesc, acc);
+                  mma_tf32_ts(dS, ahi + kk * 8, dl, idesc, 1u);
+                  mma_tf32_ts(dS, alo + kk * 8, dh, idesc, 1u);
                 }
                 mma_commit(&stg_free[b]);
               }
@@ -287,21 +381,26 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     // -------------------------------------------------------------- generators
     // two warps per TMEM lane quarter: `half` 0 (warps 2..5) and 1 (warps 6..9);
     // thread t owns TMEM lane t, each half owns half of every chunk's columns
-    constexpr int HC = DVP / 2;                          // state / output columns per half
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const int t = quarter * 32 + lane;                   // TMEM lane = token or feature
     const uint32_t la = tmem + ((uint32_t)(quarter * 32) << 16);
     int stg_use = 0, sb_use = 0, out_use = 0;
     bool ok = true;
-    float* myrow = X + t * xs;
-    const int dh = (p.d + 1) / 2;                        // row elements loaded by each half
-    const int a0 = half * dh, a1 = min(p.d, a0 + dh);
     const int64_t col_stride = p.dv + 1;
     float* part_h = p.part + ((int64_t)g * p.bh + h) * p.n * col_stride;
     float* master_h = p.master + ((int64_t)g * p.bh + h) * (int64_t)(FT * kRows) * DVP;
-    float* xch = sden + FT * kRows;                      // [2][128] exchange for the denominators
-    float* sdx = xch + 2 * kRows;                        // [FT*128] exchange for the sden sums
+    const bool vec_row = (p.d & 3) == 0;
+    // this thread's feature of every tile in the update phase: indices and key factor
+    uint32_t fidx[FT];
+    float fcoef[FT];
+#pragma unroll
+    for (int j = 0; j < FT; ++j) {
+      const uint32_t sg = segtab[j * 16 + (t >> 3)];
+      const int p1 = sg & 1023, p2 = (sg >> 10) & 1023, c = (int)(sg >> 20) + (t & 7);
+      fidx[j] = (uint32_t)p1 | ((uint32_t)p2 << 10) | ((uint32_t)c << 20);
+      fcoef[j] = j < ntiles ? seg_key_coef(p1, p2, c, p.d, p.degree) : 0.0f;
+    }
     for (int64_t c = 0; ok && c < nb; ++c) {
       const int64_t b0 = c * p.bs;
       const int64_t b1 = min(b0 + (int64_t)p.bs, p.n);
@@ -318,9 +417,25 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
         for (int st = 0; ok && st < nsq; ++st) {
           const int64_t i = b0 + (int64_t)st * kRows + t;
           const bool valid = i < b1;
+          float* xr = X + t * XS;
           gen_sync();  // X is free, and sden of the previous update phase is visible
-          for (int a = a0; a < a1; ++a) myrow[a] = valid ? __ldg(qh + i * p.d + a) * p.scale : 0.0f;
-          if (half == 0) myrow[p.d] = 1.0f;
+          if (half == 0) {
+            const float* src = qh + (valid ? i : 0) * p.d;
+            if (vec_row) {
+              for (int a = 0; a < p.d; a += 4) {
+                float4 v4 = valid ? *reinterpret_cast<const float4*>(src + a) : make_float4(0.f, 0.f, 0.f, 0.f);
+                v4.x *= p.scale;
+                v4.y *= p.scale;
+                v4.z *= p.scale;
+                v4.w *= p.scale;
+                *reinterpret_cast<float4*>(xr + a) = v4;
+              }
+            } else {
+              for (int a = 0; a < p.d; ++a) xr[a] = valid ? __ldg(src + a) * p.scale : 0.0f;
+            }
+          } else {
+            for (int a = p.d; a < DX; ++a) xr[a] = (a == dp) ? 1.0f : 0.0f;
+          }
           gen_sync();
           float den_acc = 0.0f;
           float acc[HC];
@@ -328,12 +443,9 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
           for (int u = 0; u < HC; ++u) acc[u] = 0.0f;
           for (int j = 0; ok && j < ntiles; ++j, ++sb_use) {
             // state row of feature t of tile j, this half's columns: fold dS_j (first sub-tile)
-            // into the fp32 master and write its hi/lo split into the K-major B buffer
+            // into the fp32 master and write its hi/lo split, MN-major, into the B buffer
             const int sb = sb_use & 1;
             if (sb_use >= 2 && !mbar_wait(&sb_free[sb], ((sb_use >> 1) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
-            uint8_t* bhi = sbuf + sb * L::kSbuf;
-            uint8_t* blo = bhi + L::kSbufHalf;
-            const uint32_t atom = (uint32_t)(t >> 5) * (DVP * 128);
             float4* mrow = reinterpret_cast<float4*>(master_h + (int64_t)(j * kRows + t) * DVP + half * HC);
             float sv[HC];
             if (st == 0) {
@@ -361,35 +473,52 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
                 sv[4 * u4 + 3] = m4.w;
               }
             }
+            {
+              // row t of chunk (half*HC)/32, granules of 8 columns: 32-byte granule g sits at g ^ (t & 3)
+              uint8_t* bhi = sbuf + sb * L::kSbuf + ((half * HC) / 32) * (kRows * 128) + t * 128;
+              uint8_t* blo = bhi + L::kSbufHalf;
+              const int g0 = ((half * HC) % 32) / 8;
 #pragma unroll
-            for (int u = 0; u < HC; ++u) {
-              const int nrow = half * HC + u;
-              const uint32_t chunk = ((uint32_t)((t & 31) >> 2)) ^ (uint32_t)(nrow & 7);
-              const uint32_t off = atom + nrow * 128 + chunk * 16 + (t & 3) * 4;
-              const float hi = __uint_as_float(to_tf32(sv[u]));
-              *reinterpret_cast<float*>(bhi + off) = hi;
-              *reinterpret_cast<float*>(blo + off) = sv[u] - hi;
+              for (int gg = 0; gg < HC / 8; ++gg) {
+                const uint32_t off = (uint32_t)(((g0 + gg) ^ (t & 3)) * 32);
+                float hv[8], lv[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                  hv[u] = __uint_as_float(to_tf32(sv[gg * 8 + u]));
+                  lv[u] = sv[gg * 8 + u] - hv[u];
+                }
+                *reinterpret_cast<float4*>(bhi + off) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+                *reinterpret_cast<float4*>(bhi + off + 16) = make_float4(hv[4], hv[5], hv[6], hv[7]);
+                *reinterpret_cast<float4*>(blo + off) = make_float4(lv[0], lv[1], lv[2], lv[3]);
+                *reinterpret_cast<float4*>(blo + off + 16) = make_float4(lv[4], lv[5], lv[6], lv[7]);
+              }
             }
             tc_fence_before();   // the dS_j reads are ordered before the MMAs that reuse its columns
             fence_proxy_async_smem();
             mbar_arrive(&sb_full[sb]);
-            // Phi_q chunks of tile j for this thread's token: 16 features per half
+            // Phi_q chunks of tile j for this thread's token: 2 segments (16 features) per half
             for (int kc = 0; kc < kRows / kChunk; ++kc, ++stg_use) {
-              const int b = stg_use & 1;
-              if (stg_use >= 2 && !mbar_wait(&stg_free[b], ((stg_use >> 1) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+              const int b = stg_use % kNStg;
+              if (stg_use >= kNStg && !mbar_wait(&stg_free[b], ((stg_use / kNStg) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
               uint32_t hi[16], lo[16];
-              const int fl = j * kRows + kc * kChunk + half * 16;
 #pragma unroll
-              for (int u = 0; u < 16; ++u) {
-                const uint32_t pk = ftab[fl + u];
-                float phi = 0.0f;
-                if (pk != 0xFFFFFFFFu) {
-                  phi = myrow[pk & 1023] * myrow[(pk >> 10) & 1023];
-                  if (DEG3) phi *= myrow[pk >> 20];
+              for (int sg = 0; sg < 2; ++sg) {
+                const int sl = j * 16 + kc * 4 + half * 2 + sg;    // segment within the group
+                const uint32_t pk = segtab[sl];
+                float pre = xr[pk & 1023];
+                if (DEG3) pre *= xr[(pk >> 10) & 1023];
+                const float* xc = xr + (pk >> 20);
+                const float4 x0 = ld4(xc), x1 = ld4(xc + 4);
+                const float4 d0 = ld4(sden + sl * 8), d1 = ld4(sden + sl * 8 + 4);
+                const float ph[8] = {pre * x0.x, pre * x0.y, pre * x0.z, pre * x0.w,
+                                     pre * x1.x, pre * x1.y, pre * x1.z, pre * x1.w};
+                const float dd[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                  den_acc = fmaf(ph[u], dd[u], den_acc);
+                  hi[sg * 8 + u] = to_tf32(ph[u]);
+                  lo[sg * 8 + u] = __float_as_uint(ph[u] - __uint_as_float(hi[sg * 8 + u]));
                 }
-                den_acc = fmaf(phi, sden[fl + u], den_acc);
-                hi[u] = to_tf32(phi);
-                lo[u] = __float_as_uint(phi - __uint_as_float(hi[u]));
               }
               tmem_st16(la + L::kStg + b * 2 * kChunk + half * 16, hi);
               tmem_st16(la + L::kStg + b * 2 * kChunk + kChunk + half * 16, lo);
@@ -441,34 +570,50 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
         const int64_t t0 = b0 + (int64_t)st * kRows;
         gen_sync();  // everyone is done with X
         {
+          // transposed key tile: X[a * kXtStride + token]
           const int64_t i = t0 + t;
           const bool valid = i < b1;
-          for (int a = a0; a < a1; ++a) myrow[a] = valid ? __ldg(kh + i * p.d + a) : 0.0f;
-          if (half == 0) myrow[p.d] = valid ? 1.0f : 0.0f;   // an invalid token's features are all zero
+          if (half == 0) {
+            const float* src = kh + (valid ? i : 0) * p.d;
+            for (int a = 0; a < p.d; ++a) X[a * kXtStride + t] = valid ? __ldg(src + a) : 0.0f;
+          } else {
+            // an invalid token's extended row is all zero, so are its features
+            for (int a = p.d; a < DX; ++a) X[a * kXtStride + t] = (a == dp && valid) ? 1.0f : 0.0f;
+          }
         }
         gen_sync();
         for (int tcn = 0; ok && tcn < kRows / kChunk; ++tcn) {
+          const int tok0 = tcn * kChunk + half * 16;
 #pragma unroll
           for (int j = 0; j < FT; ++j) {
             if (!ok || j >= ntiles) break;
-            const int b = stg_use & 1;
-            if (stg_use >= 2 && !mbar_wait(&stg_free[b], ((stg_use >> 1) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+            const int b = stg_use % kNStg;
+            if (stg_use >= kNStg && !mbar_wait(&stg_free[b], ((stg_use / kNStg) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
             ++stg_use;
-            const uint32_t pk = ftab[j * kRows + t];
-            const bool live = pk != 0xFFFFFFFFu;
-            const int ia = live ? (int)(pk & 1023) : 0, ib = live ? (int)((pk >> 10) & 1023) : 0,
-                      ic = live ? (int)(pk >> 20) : 0;
-            const float cf = live ? key_coef_tc(ia, ib, ic, p.d) : 0.0f;
+            const uint32_t fi = fidx[j];
+            const float cf = fcoef[j];
+            const float* r1 = X + (fi & 1023) * kXtStride + tok0;
+            const float* rc = X + (fi >> 20) * kXtStride + tok0;
             uint32_t hi[16], lo[16];
             float fsum = 0.0f;
 #pragma unroll
-            for (int u = 0; u < 16; ++u) {
-              const float* xr = X + (tcn * kChunk + half * 16 + u) * xs;
-              float phi = xr[ia] * cf * xr[ib];
-              if (DEG3) phi *= xr[ic];
-              fsum += phi;
-              hi[u] = to_tf32(phi);
-              lo[u] = __float_as_uint(phi - __uint_as_float(hi[u]));
+            for (int u4 = 0; u4 < 4; ++u4) {
+              float4 a4 = ld4(r1 + 4 * u4);
+              const float4 c4 = ld4(rc + 4 * u4);
+              if (DEG3) {
+                const float4 b4 = ld4(X + ((fi >> 10) & 1023) * kXtStride + tok0 + 4 * u4);
+                a4.x *= b4.x;
+                a4.y *= b4.y;
+                a4.z *= b4.z;
+                a4.w *= b4.w;
+              }
+              const float ph[4] = {a4.x * cf * c4.x, a4.y * cf * c4.y, a4.z * cf * c4.z, a4.w * cf * c4.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                fsum += ph[u];
+                hi[4 * u4 + u] = to_tf32(ph[u]);
+                lo[4 * u4 + u] = __float_as_uint(ph[u] - __uint_as_float(hi[4 * u4 + u]));
+              }
             }
             sd[j] += fsum;
             tmem_st16(la + L::kStg + b * 2 * kChunk + half * 16, hi);
@@ -504,9 +649,10 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
 template <int DVP>
 size_t mom_smem(int d) {
   using L = MomLayout<DVP>;
-  const int xs = (d + 1) | 1;
-  return 1024 + 2 * L::kSbuf + L::kVStages * L::kVStage + (size_t)kRows * xs * 4 + (size_t)L::kFT * kRows * 12 +
-         2 * kRows * 4 + 16 + 17 * 8 + 16;
+  const int dp = dpad8(d), DX = dp + 8, XS = DX + 4;
+  const size_t xwords = (size_t)max(kRows * XS, DX * kXtStride);
+  return 1024 + 2 * L::kSbuf + L::kVStages * L::kVStage + xwords * 4 + (size_t)L::kFT * 16 * 4 +
+         (size_t)L::kFT * kRows * 8 + 2 * kRows * 4 + 16 + (2 * kNStg + 12) * 8 + 16;
 }
 
 template <int DVP, bool DEG3>
@@ -533,11 +679,10 @@ __global__ void sum_groups_kernel(const float* __restrict__ part, int groups, in
 // Feature groups (CTAs per sequence) the tensor-core moment kernel uses, or 0
 // when the shape is not supported (then the CUDA-core kernel runs).
 int moments_tc_groups(int d, int dv, int degree) {
-  if (dv > 64 || d > 128) return 0;
+  if (dv > 64 || d > 128 || degree > 3) return 0;
   const int dvp = dv <= 32 ? 32 : 64;
   const int ft = dvp == 32 ? MomLayout<32>::kFT : MomLayout<64>::kFT;
-  const int64_t F = feature_count(d, degree);
-  const int64_t tiles = (F + kRows - 1) / kRows;
+  const int64_t tiles = (mom_seg_count(d, degree) + 15) / 16;
   const size_t smem = dvp == 32 ? mom_smem<32>(d) : mom_smem<64>(d);
   if (smem > 227 * 1024) return 0;
   return (int)((tiles + ft - 1) / ft);
@@ -569,7 +714,7 @@ int launch_moments_tc(const CUtensorMap* maps, const float* q, const float* k, f
   const int G = moments_tc_groups(d, dv, degree);
   if (G <= 0) return set_error(SA_ERR_UNSUPPORTED, "tensor-core moments: shape not supported");
   if (bh > 65535) return set_error(SA_ERR_UNSUPPORTED, "too many sequences for one launch");
-  MomTCParams prm{q, k, part, master, status, n, bh, d, dv, bs, (int)feature_count(d, degree), G, scale};
+  MomTCParams prm{q, k, part, master, status, n, bh, d, dv, bs, degree, (int)mom_seg_count(d, degree), G, scale};
   if (degree == 3) return dv <= 32 ? launch_mom_tc<32, true>(maps, prm, stream) : launch_mom_tc<64, true>(maps, prm, stream);
   return dv <= 32 ? launch_mom_tc<32, false>(maps, prm, stream) : launch_mom_tc<64, false>(maps, prm, stream);
 }

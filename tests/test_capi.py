@@ -78,12 +78,13 @@ def test_workspace_size_and_argument_errors_without_gpu():
     sz = ctypes.c_size_t(0)
     assert lib.sa_fast_attention_workspace_size(256, 8192, 64, 64, 2, 128, 1, ctypes.byref(sz)) == 0
     R = 63 * 64
-    # tensor-core layout: 3 partial slices of the low sums (17 feature tiles in groups of 6), the
-    # fp32 moment state (3 groups x 6 tiles x 128 features x 64), hi/lo copies of k, v and of the
-    # reps, rep weights and indices
-    expect_min = (3 * 256 * 8192 * 65 * 4 + 3 * 256 * 768 * 64 * 4 + 4 * 256 * 8192 * 64 * 4
-                  + 4 * 256 * R * 64 * 4 + 256 * R * 4 + 256 * R * 4)
-    assert sz.value >= expect_min and sz.value < expect_min + 4096
+    # tensor-core layout: G partial slices of the low sums and the fp32 moment state of G
+    # feature groups, hi/lo copies of k, v and of the reps, rep weights and indices
+    fixed = 4 * 256 * 8192 * 64 * 4 + 4 * 256 * R * 64 * 4 + 256 * R * 4 + 256 * R * 4
+    per_group = 256 * 8192 * 65 * 4 + 256 * 5 * 128 * 64 * 4
+    groups = (sz.value - fixed) // per_group
+    assert 2 <= groups <= 6
+    assert fixed + groups * per_group <= sz.value < fixed + groups * per_group + 4096
     # argument errors return before any CUDA call
     assert lib.sa_fast_attention(None, None, None, 1, 16, 8, 8, 2, 0, 1.0, 1, None, None, None, 1e-12, None, None,
                                  None, 0, None) == _lib.SA_ERR_INVALID_ARG
