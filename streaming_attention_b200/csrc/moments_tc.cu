@@ -30,12 +30,18 @@
 // remainder copies made by the split pass) arrive by TMA, MN-major with the
 // 32-byte-atom swizzle.
 //
+// Each 8-wide K step takes two MMAs of N = 2*DVP: A_hi and A_lo times
+// B = [B_hi | B_lo] (the hi and remainder copies of V or of the state sit one
+// chunk stride apart in shared memory).  A tf32 MMA costs about the same time
+// for any N up to 256, so this beats three N = DVP products; the two column
+// halves of the result are added on the CUDA cores.
+//
 // Accumulation: tensor-core accumulation into TMEM does not round to nearest,
-// so no long sum stays there.  dS_j covers one block (<= 96 MMA steps) and is
+// so no long sum stays there.  dS_j covers one block (<= 64 MMA steps) and is
 // folded into an fp32 master state in global memory (L2-resident, RN adds on
 // the CUDA cores) at the start of the next query phase, where the same thread
 // also writes the state's hi/lo split (MN-major, 32-byte-atom swizzle) that is
-// the B operand of the query product.  Out_j covers one tile (48 MMA steps)
+// the B operand of the query product.  Out_j covers one tile (32 MMA steps)
 // and lands in tile j's own TMEM columns (free after the fold); the tiles are
 // summed in registers.  The denominator column is a dot product with the same
 // features on the CUDA cores.  Each CTA writes its partial sums; the residual
@@ -52,7 +58,7 @@ using namespace tc;
 constexpr int kRows = 128;      // tokens per sub-tile = features per tile = TMEM lanes
 constexpr int kChunk = 32;      // K columns per staged feature chunk
 constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 generators
-constexpr int kNStg = 3;        // TMEM staging buffers (32 hi + 32 lo columns each)
+constexpr int kNStg = 2;        // TMEM staging buffers (32 hi + 32 lo columns each)
 constexpr int kXtStride = kRows + 4;   // transposed key tile row (floats)
 
 constexpr int kErrMomWait = 201, kErrMomDrain = 202;
@@ -70,9 +76,11 @@ struct MomTCParams {
 
 template <int DVP>
 struct MomLayout {
-  static constexpr int kFT = (512 - kNStg * 2 * kChunk) / DVP;      // state tiles per CTA
-  // TMEM columns: tile j at j*DVP (dS_j, then Out_j); staging after the tiles
-  static constexpr uint32_t kStg = kFT * DVP;
+  // TMEM columns of a tile: the product with [hi | lo] of the B operand, 2*DVP columns
+  static constexpr int kTC = 2 * DVP;
+  static constexpr int kFT = (512 - kNStg * 2 * kChunk) / kTC;      // state tiles per CTA
+  // TMEM columns: tile j at j*kTC (dS_j, then Out_j); staging after the tiles
+  static constexpr uint32_t kStg = kFT * kTC;
   static_assert(kStg + kNStg * 2 * kChunk <= 512, "TMEM columns");
   // shared memory
   static constexpr uint32_t kSbufHalf = (DVP / 32) * kRows * 128;    // hi or lo: DVP/32 chunks x 128 rows x 128 B
@@ -186,7 +194,90 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[HC]) {
   tmem_wait_ld();
 }
 
+// v[u] = TMEM column u + column u + off of this thread's lane, u < HC: the two
+// halves of a [hi | lo] product (A times the hi copy, A times the remainder).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+template <int HC>
+__device__ __forceinline__ void tmem_ld_sum(uint32_t taddr, uint32_t off, float (&v)[HC]) {
+#pragma unroll
+  for (int q = 0; q < HC / 16; ++q) {
+    uint32_t a[16], b[16];
+    tmem_ld16(taddr + 16 * q, a);
+    tmem_ld16(taddr + off + 16 * q, b);
+    tmem_wait_ld();
+#pragma unroll
+    for (int u = 0; u < 16; ++u) v[16 * q + u] = __uint_as_float(a[u]) + __uint_as_float(b[u]);
+  }
+}
+
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+// Loads of one 128-row tile of q or k rows into registers, issued one tile
+// ahead of use so that their latency hides behind a phase of generation.
+//
+// Vector path (d % 4 == 0, 16-byte aligned rows): the first min(d, 64) columns
+// of the tile are cut into blocks of 8 rows x 4 float4 (64 contiguous bytes per
+// row); generator warp w takes blocks k * 8 + w, k < 8, and lane l the float4
+// (row 8 rb + l / 4, float4 column 4 cb + l % 4) of block (rb, cb).  A warp
+// access then covers eight 64-byte segments, and the transposed store of a key
+// tile meets at most two-way bank conflicts.  Scalar path: thread t reads row
+// t, columns [32 half, 32 half + 32).  Columns from 64 on are read when the
+// tile is stored.
+// The eight (row, float4 column) pairs of a thread, packed as 16-bit
+// (row << 8 | col4) entries of a uint4, 0xffff where the thread has no element;
+// built once per CTA and kept in shared memory (not in registers across phases).
+__device__ __forceinline__ uint4 tile_map_entries(int d, int wg, int l) {
+  const int d4 = min(d, 64) >> 2, cb = (d4 + 3) >> 2;
+  uint32_t w[4];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int b = k * 8 + wg;
+    const int rb = b / cb;
+    const int row = 8 * rb + (l >> 2), col4 = 4 * (b - rb * cb) + (l & 3);
+    const uint32_t e = (rb < 16 && col4 < d4) ? (uint32_t)((row << 8) | col4) : 0xffffu;
+    if (k & 1) w[k >> 1] |= e << 16;
+    else w[k >> 1] = e;
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ uint32_t tile_entry(const uint4& m, int k) {
+  const uint32_t w = (k >> 1) == 0 ? m.x : (k >> 1) == 1 ? m.y : (k >> 1) == 2 ? m.z : m.w;
+  return (k & 1) ? (w >> 16) : (w & 0xffffu);
+}
+
+__device__ __forceinline__ void rows_issue(const float* head, int64_t i0, int nvalid, int d, int t, int half,
+                                           bool vec, const uint4* tmap, float (&v)[32]) {
+  if (vec) {
+    const uint4 m = *tmap;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t e = tile_entry(m, k);
+      const int row = (int)(e >> 8), col4 = (int)(e & 255);
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (e != 0xffffu && row < nvalid)
+        x = __ldg(reinterpret_cast<const float4*>(head + (i0 + row) * d) + col4);
+      v[4 * k + 0] = x.x;
+      v[4 * k + 1] = x.y;
+      v[4 * k + 2] = x.z;
+      v[4 * k + 3] = x.w;
+    }
+  } else {
+    const int a0 = half * 32;
+    const bool valid = t < nvalid;
+    const float* src = head + (i0 + (valid ? t : 0)) * d + a0;
+#pragma unroll
+    for (int u = 0; u < 32; ++u) v[u] = (valid && a0 + u < d) ? __ldg(src + u) : 0.0f;
+  }
+}
 
 template <int DVP, bool DEG3>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -203,19 +294,21 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
   const int DX = dp + 8;                                   // extended row length
   const int XS = DX + 4;                                   // query tile row stride
   float* X = reinterpret_cast<float*>(vst + L::kVStages * L::kVStage);   // query: [128][XS]; update: [DX][kXtStride]
-  const int xwords = max(kRows * XS, DX * kXtStride);
+  const int xwords = max(max(kRows * XS, DX * kXtStride), kRows * (DVP + 1));
   uint32_t* segtab = reinterpret_cast<uint32_t*>(X + xwords);            // [FT*16]
   float* sden = reinterpret_cast<float*>(segtab + FT * 16);              // [FT*128]
   float* xch = sden + FT * kRows;                                        // [2][128]
   float* sdx = xch + 2 * kRows;                                          // [FT*128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(sdx + FT * kRows) + 7) & ~uintptr_t(7));
+  uint4* tmaps = reinterpret_cast<uint4*>(
+      (reinterpret_cast<uintptr_t>(sdx + FT * kRows) + 15) & ~uintptr_t(15));   // [256] tile load maps
+  uint64_t* bars = reinterpret_cast<uint64_t*>(tmaps + 256);
   uint64_t* stg_full = bars;                // [kNStg] 256 arrivals
   uint64_t* stg_free = bars + kNStg;        // [kNStg] commit
   uint64_t* sb_full = bars + 2 * kNStg;     // [2] 256 arrivals
   uint64_t* sb_free = sb_full + 2;          // [2] commit
   uint64_t* v_full = sb_free + 2;           // [2] TMA
   uint64_t* v_free = v_full + 2;            // [2] commit
-  uint64_t* out_full = v_free + 2;          // commit, once per (sub-tile, tile)
+  uint64_t* out_full = v_free + 2;          // commit, once per query sub-tile
   uint64_t* out_free = out_full + 1;        // 256 arrivals, once per sub-tile
   uint64_t* u_done = out_free + 1;          // commit, once per update phase
   uint64_t* drain = u_done + 1;
@@ -254,6 +347,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     segtab[s] = (uint32_t)p1 | ((uint32_t)p2 << 10) | ((uint32_t)c0 << 20);
   }
   for (int f = threadIdx.x; f < FT * kRows; f += kThreads) sden[f] = 0.0f;
+  if (threadIdx.x >= 64) tmaps[threadIdx.x - 64] = tile_map_entries(p.d, (threadIdx.x >> 5) - 2, threadIdx.x & 31);
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -297,7 +391,9 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(128, DVP, false, true);  // B MN-major in both products
+      // B = [hi | lo] of V or of the state: both copies sit at one chunk stride, so a
+      // single MMA of N = 2*DVP multiplies A by both; B MN-major in both products
+      constexpr uint32_t idesc = idesc_tf32(128, 2 * DVP, false, true);
       int stg_use = 0, sb_use = 0, v_use = 0, sub_use = 0;
       bool ok = true;
       for (int64_t c = 0; ok && c < nb; ++c) {
@@ -312,8 +408,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
               if (!mbar_wait(&sb_full[sb], (sb_use >> 1) & 1, ab, kErrMomWait)) { ok = false; break; }
               tc_fence_after();
               const uint32_t bhi = smem_u32(sbuf + sb * L::kSbuf);
-              const uint32_t blo = bhi + L::kSbufHalf;
-              const uint32_t dO = tmem + j * DVP;
+              const uint32_t dO = tmem + j * L::kTC;
               for (int kc = 0; kc < kRows / kChunk; ++kc, ++stg_use) {
                 const int b = stg_use % kNStg;
                 if (!mbar_wait(&stg_full[b], (stg_use / kNStg) & 1, ab, kErrMomWait)) { ok = false; break; }
@@ -323,17 +418,17 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
 #pragma unroll
                 for (int kk = 0; kk < kChunk / 8; ++kk) {
                   const uint32_t off = (kc * kChunk + kk * 8) * 128;   // 8 feature rows of 128 B
-                  const uint64_t dh = sdesc_sw128_atom32(bhi + off, kRows * 128, 512);
-                  const uint64_t dl = sdesc_sw128_atom32(blo + off, kRows * 128, 512);
-                  mma_tf32_ts(dO, ahi + kk * 8, dh, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
-                  mma_tf32_ts(dO, ahi + kk * 8, dl, idesc, 1u);
-                  mma_tf32_ts(dO, alo + kk * 8, dh, idesc, 1u);
+                  const uint64_t db = sdesc_sw128_atom32(bhi + off, kRows * 128, 512);
+                  mma_tf32_ts(dO, ahi + kk * 8, db, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+                  mma_tf32_ts(dO, alo + kk * 8, db, idesc, 1u);
                 }
                 mma_commit(&stg_free[b]);
               }
               mma_commit(&sb_free[sb]);
-              mma_commit(out_full);
             }
+            // one commit per sub-tile: it completes once every tile's MMAs are done
+            // (a waiter must never fall two phases behind an mbarrier)
+            if (ok) mma_commit(out_full);
           }
         }
         if (ok && c + 1 < nb) {
@@ -342,23 +437,20 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
               const int vs = v_use & 1;
               if (!mbar_wait(&v_full[vs], (v_use >> 1) & 1, ab, kErrMomWait)) { ok = false; break; }
               const uint32_t vhi = smem_u32(vst + vs * L::kVStage);
-              const uint32_t vlo = vhi + L::kVHalf;
               for (int j = 0; ok && j < ntiles; ++j, ++stg_use) {
                 const int b = stg_use % kNStg;
                 if (!mbar_wait(&stg_full[b], (stg_use / kNStg) & 1, ab, kErrMomWait)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t ahi = tmem + L::kStg + b * 2 * kChunk;
                 const uint32_t alo = ahi + kChunk;
-                const uint32_t dS = tmem + j * DVP;
+                const uint32_t dS = tmem + j * L::kTC;
 #pragma unroll
                 for (int kk = 0; kk < kChunk / 8; ++kk) {
-                  const uint64_t dh = sdesc_sw128_atom32(vhi + kk * 1024, kChunk * 128, 512);
-                  const uint64_t dl = sdesc_sw128_atom32(vlo + kk * 1024, kChunk * 128, 512);
+                  const uint64_t db = sdesc_sw128_atom32(vhi + kk * 1024, kChunk * 128, 512);
                   // dS_j starts from zero in every block
                   const uint32_t acc = (st > 0 || tc > 0 || kk > 0) ? 1u : 0u;
-                  mma_tf32_ts(dS, ahi + kk * 8, dh, idesc, acc);
-                  mma_tf32_ts(dS, ahi + kk * 8, dl, idesc, 1u);
-                  mma_tf32_ts(dS, alo + kk * 8, dh, idesc, 1u);
+                  mma_tf32_ts(dS, ahi + kk * 8, db, idesc, acc);
+                  mma_tf32_ts(dS, alo + kk * 8, db, idesc, 1u);
                 }
                 mma_commit(&stg_free[b]);
               }
@@ -390,7 +482,51 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     const int64_t col_stride = p.dv + 1;
     float* part_h = p.part + ((int64_t)g * p.bh + h) * p.n * col_stride;
     float* master_h = p.master + ((int64_t)g * p.bh + h) * (int64_t)(FT * kRows) * DVP;
-    const bool vec_row = (p.d & 3) == 0;
+    const bool vec = (p.d & 3) == 0 &&
+                     ((reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.k)) & 15) == 0;
+    // Row tiles are loaded one tile ahead, in the order the phases consume them:
+    // per block c, the query sub-tiles of c (c > 0), then the key sub-tiles of c
+    // (c + 1 < nb).  rowv holds this thread's share of the next tile.
+    const uint4* my_map = tmaps + (threadIdx.x - 64);
+    float rowv[32];
+    auto issue_tile = [&](int64_t uc, bool uq, int ust) {
+      const int64_t i0 = uc * p.bs + (int64_t)ust * kRows;
+      const int nvalid = (int)min((int64_t)kRows, min(uc * p.bs + p.bs, p.n) - i0);
+      rows_issue(uq ? qh : kh, i0, nvalid, p.d, t, half, vec, my_map, rowv);
+    };
+    // issue the loads of the tile after (uc, uq, ust), if there is one
+    auto issue_next = [&](int64_t uc, bool uq, int ust) {
+      if (uq) {
+        const int64_t ub0 = uc * p.bs, ub1 = min(ub0 + p.bs, p.n);
+        if ((int64_t)(ust + 1) * kRows < ub1 - ub0) issue_tile(uc, true, ust + 1);
+        else if (uc + 1 < nb) issue_tile(uc, false, 0);
+      } else if (ust + 1 < sub) {
+        issue_tile(uc, false, ust + 1);
+      } else {
+        issue_tile(uc + 1, true, 0);
+      }
+    };
+    if (nb > 1) issue_tile(0, false, 0);
+    // Master state: only the thread that owns feature t of a tile (and its half of
+    // the columns) ever touches those entries, so they are stored in the order
+    // that makes a warp's accesses contiguous: float4 u4 of (tile j, half, lane
+    // t) at float4 index ((j * 2 + half) * (HC / 4) + u4) * 128 + t.
+    auto mrow_of = [&](int j) {
+      return reinterpret_cast<float4*>(master_h) + (int64_t)((j * 2 + half) * (HC / 4)) * kRows + t;
+    };
+    // master state row of the next tile to fold (prefetched one tile ahead)
+    float mp[HC];
+    auto mload = [&](int j) {
+      const float4* mrow = mrow_of(j);
+#pragma unroll
+      for (int u4 = 0; u4 < HC / 4; ++u4) {
+        const float4 m4 = mrow[u4 * kRows];
+        mp[4 * u4 + 0] = m4.x;
+        mp[4 * u4 + 1] = m4.y;
+        mp[4 * u4 + 2] = m4.z;
+        mp[4 * u4 + 3] = m4.w;
+      }
+    };
     // this thread's feature of every tile in the update phase: indices and key factor
     uint32_t fidx[FT];
     float fcoef[FT];
@@ -411,6 +547,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
           for (int col = 0; col <= p.dv; ++col) dst[col] = 0.0f;
         }
       } else {
+        if (c >= 2) mload(0);   // the state rows written by the previous query phase
         if (!mbar_wait(u_done, (int)((c - 1) & 1), ab, kErrMomWait)) { ok = false; break; }
         tc_fence_after();
         const int nsq = (int)((b1 - b0 + kRows - 1) / kRows);  // query sub-tiles of block c
@@ -419,79 +556,88 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
           const bool valid = i < b1;
           float* xr = X + t * XS;
           gen_sync();  // X is free, and sden of the previous update phase is visible
-          if (half == 0) {
-            const float* src = qh + (valid ? i : 0) * p.d;
-            if (vec_row) {
-              for (int a = 0; a < p.d; a += 4) {
-                float4 v4 = valid ? *reinterpret_cast<const float4*>(src + a) : make_float4(0.f, 0.f, 0.f, 0.f);
-                v4.x *= p.scale;
-                v4.y *= p.scale;
-                v4.z *= p.scale;
-                v4.w *= p.scale;
-                *reinterpret_cast<float4*>(xr + a) = v4;
+          {
+            // x~ = [scale q_i, zeros, 1 at dp, zeros]
+            const int a0 = half * 32;
+            if (vec) {
+              const uint4 m = *my_map;
+#pragma unroll
+              for (int k = 0; k < 8; ++k) {
+                const uint32_t e = tile_entry(m, k);
+                const int row = (int)(e >> 8), col4 = (int)(e & 255);
+                if (e != 0xffffu)
+                  *reinterpret_cast<float4*>(X + row * XS + 4 * col4) =
+                      make_float4(rowv[4 * k] * p.scale, rowv[4 * k + 1] * p.scale, rowv[4 * k + 2] * p.scale,
+                                  rowv[4 * k + 3] * p.scale);
               }
             } else {
-              for (int a = 0; a < p.d; ++a) xr[a] = valid ? __ldg(src + a) * p.scale : 0.0f;
+#pragma unroll
+              for (int u = 0; u < 32; ++u)
+                if (a0 + u < p.d) xr[a0 + u] = rowv[u] * p.scale;
             }
-          } else {
-            for (int a = p.d; a < DX; ++a) xr[a] = (a == dp) ? 1.0f : 0.0f;
+            const float* src = qh + (valid ? i : 0) * p.d;
+            for (int a = 64 + half; a < p.d; a += 2) xr[a] = valid ? __ldg(src + a) * p.scale : 0.0f;
+            if (half == 1)
+              for (int a = p.d; a < DX; ++a) xr[a] = (a == dp) ? 1.0f : 0.0f;
           }
+          issue_next(c, true, st);
           gen_sync();
           float den_acc = 0.0f;
-          float acc[HC];
-#pragma unroll
-          for (int u = 0; u < HC; ++u) acc[u] = 0.0f;
           for (int j = 0; ok && j < ntiles; ++j, ++sb_use) {
-            // state row of feature t of tile j, this half's columns: fold dS_j (first sub-tile)
-            // into the fp32 master and write its hi/lo split, MN-major, into the B buffer
             const int sb = sb_use & 1;
             if (sb_use >= 2 && !mbar_wait(&sb_free[sb], ((sb_use >> 1) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
-            float4* mrow = reinterpret_cast<float4*>(master_h + (int64_t)(j * kRows + t) * DVP + half * HC);
-            float sv[HC];
-            if (st == 0) {
-              tmem_ld_cols<HC>(la + j * DVP + half * HC, sv);
-              if (c >= 2) {
-#pragma unroll
-                for (int u4 = 0; u4 < HC / 4; ++u4) {
-                  const float4 m4 = mrow[u4];
-                  sv[4 * u4 + 0] += m4.x;
-                  sv[4 * u4 + 1] += m4.y;
-                  sv[4 * u4 + 2] += m4.z;
-                  sv[4 * u4 + 3] += m4.w;
-                }
-              }
-#pragma unroll
-              for (int u4 = 0; u4 < HC / 4; ++u4)
-                mrow[u4] = make_float4(sv[4 * u4], sv[4 * u4 + 1], sv[4 * u4 + 2], sv[4 * u4 + 3]);
-            } else {
-#pragma unroll
-              for (int u4 = 0; u4 < HC / 4; ++u4) {
-                const float4 m4 = mrow[u4];
-                sv[4 * u4 + 0] = m4.x;
-                sv[4 * u4 + 1] = m4.y;
-                sv[4 * u4 + 2] = m4.z;
-                sv[4 * u4 + 3] = m4.w;
-              }
-            }
             {
-              // row t of chunk (half*HC)/32, granules of 8 columns: 32-byte granule g sits at g ^ (t & 3)
+              // State row of feature t of tile j, this half's columns, 16 at a time:
+              // fold dS_j (first sub-tile) into the fp32 master and write the hi/lo
+              // split into the B buffer (MN-major: row t of chunk (half * HC) / 32,
+              // 32-byte granule g stored at g ^ (t & 3)).
+              float4* mrow = mrow_of(j);
               uint8_t* bhi = sbuf + sb * L::kSbuf + ((half * HC) / 32) * (kRows * 128) + t * 128;
               uint8_t* blo = bhi + L::kSbufHalf;
               const int g0 = ((half * HC) % 32) / 8;
 #pragma unroll
-              for (int gg = 0; gg < HC / 8; ++gg) {
-                const uint32_t off = (uint32_t)(((g0 + gg) ^ (t & 3)) * 32);
-                float hv[8], lv[8];
+              for (int q = 0; q < HC / 16; ++q) {
+                float sv[16];
+                if (st == 0) {
+                  uint32_t a[16], b[16];
+                  tmem_ld16(la + j * L::kTC + half * HC + 16 * q, a);
+                  tmem_ld16(la + j * L::kTC + DVP + half * HC + 16 * q, b);
+                  tmem_wait_ld();
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                  hv[u] = __uint_as_float(to_tf32(sv[gg * 8 + u]));
-                  lv[u] = sv[gg * 8 + u] - hv[u];
+                  for (int u = 0; u < 16; ++u) sv[u] = __uint_as_float(a[u]) + __uint_as_float(b[u]);
+                  if (c >= 2) {
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) sv[u] += mp[16 * q + u];
+                  }
+#pragma unroll
+                  for (int u4 = 0; u4 < 4; ++u4)
+                    mrow[(4 * q + u4) * kRows] = make_float4(sv[4 * u4], sv[4 * u4 + 1], sv[4 * u4 + 2], sv[4 * u4 + 3]);
+                } else {
+#pragma unroll
+                  for (int u = 0; u < 16; ++u) sv[u] = mp[16 * q + u];
                 }
-                *reinterpret_cast<float4*>(bhi + off) = make_float4(hv[0], hv[1], hv[2], hv[3]);
-                *reinterpret_cast<float4*>(bhi + off + 16) = make_float4(hv[4], hv[5], hv[6], hv[7]);
-                *reinterpret_cast<float4*>(blo + off) = make_float4(lv[0], lv[1], lv[2], lv[3]);
-                *reinterpret_cast<float4*>(blo + off + 16) = make_float4(lv[4], lv[5], lv[6], lv[7]);
+#pragma unroll
+                for (int gg = 0; gg < 2; ++gg) {
+                  const uint32_t off = (uint32_t)(((g0 + 2 * q + gg) ^ (t & 3)) * 32);
+                  float hv[8], lv[8];
+#pragma unroll
+                  for (int u = 0; u < 8; ++u) {
+                    hv[u] = __uint_as_float(to_tf32(sv[gg * 8 + u]));
+                    lv[u] = sv[gg * 8 + u] - hv[u];
+                  }
+                  *reinterpret_cast<float4*>(bhi + off) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+                  *reinterpret_cast<float4*>(bhi + off + 16) = make_float4(hv[4], hv[5], hv[6], hv[7]);
+                  *reinterpret_cast<float4*>(blo + off) = make_float4(lv[0], lv[1], lv[2], lv[3]);
+                  *reinterpret_cast<float4*>(blo + off + 16) = make_float4(lv[4], lv[5], lv[6], lv[7]);
+                }
               }
+            }
+            // prefetch the state row of the next tile to fold: tile j + 1, or tile 0 of
+            // the next sub-tile (written by the fold of sub-tile 0 above)
+            if (j + 1 < ntiles) {
+              if (st > 0 || c >= 2) mload(j + 1);
+            } else if (st + 1 < nsq) {
+              mload(0);
             }
             tc_fence_before();   // the dS_j reads are ordered before the MMAs that reuse its columns
             fence_proxy_async_smem();
@@ -526,38 +672,43 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
               tc_fence_before();
               mbar_arrive(&stg_full[b]);
             }
-            if (!ok) break;
-            // Out of the previous tile (its MMAs overlap this tile's generation)
-            if (j >= 1) {
-              if (!mbar_wait(out_full, out_use & 1, ab, kErrMomWait)) { ok = false; break; }
-              ++out_use;
-              tc_fence_after();
-              float ov[HC];
-              tmem_ld_cols<HC>(la + (j - 1) * DVP + half * HC, ov);
-#pragma unroll
-              for (int u = 0; u < HC; ++u) acc[u] += ov[u];
-            }
           }
           if (!ok) break;
+          // Out_j of every tile sits in the tile's own TMEM columns: once all the
+          // sub-tile's MMAs are done, add them up in tile order
           if (!mbar_wait(out_full, out_use & 1, ab, kErrMomWait)) { ok = false; break; }
           ++out_use;
           tc_fence_after();
-          {
+          float acc[HC];
+#pragma unroll
+          for (int u = 0; u < HC; ++u) acc[u] = 0.0f;
+          for (int j = 0; j < ntiles; ++j) {
             float ov[HC];
-            tmem_ld_cols<HC>(la + (ntiles - 1) * DVP + half * HC, ov);
+            tmem_ld_sum<HC>(la + j * L::kTC + half * HC, DVP, ov);
 #pragma unroll
             for (int u = 0; u < HC; ++u) acc[u] += ov[u];
           }
+          if (!ok) break;
           tc_fence_before();
           mbar_arrive(out_free);
           xch[half * kRows + t] = den_acc;
           gen_sync();
-          if (valid) {
-            float* dst = part_h + i * col_stride;
+          {
+            // X is free: stage the sub-tile's [rows, dv + 1] sums (row stride dv + 1
+            // is odd, so the column writes are conflict-free), then copy the
+            // contiguous block out with consecutive threads on consecutive words
+            const int cs = (int)col_stride;
 #pragma unroll
             for (int u = 0; u < HC; ++u)
-              if (half * HC + u < p.dv) dst[half * HC + u] = acc[u];
-            if (half == 0) dst[p.dv] = xch[t] + xch[kRows + t];
+              if (half * HC + u < p.dv) X[t * cs + half * HC + u] = acc[u];
+            if (half == 0) X[t * cs + p.dv] = xch[t] + xch[kRows + t];
+          }
+          gen_sync();
+          {
+            const int64_t i0 = b0 + (int64_t)st * kRows;
+            const int total = (int)min((int64_t)kRows, b1 - i0) * (int)col_stride;
+            float* dst = part_h + i0 * col_stride;
+            for (int e = threadIdx.x - 64; e < total; e += 256) dst[e] = X[e];
           }
         }
       }
@@ -573,14 +724,30 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
           // transposed key tile: X[a * kXtStride + token]
           const int64_t i = t0 + t;
           const bool valid = i < b1;
-          if (half == 0) {
-            const float* src = kh + (valid ? i : 0) * p.d;
-            for (int a = 0; a < p.d; ++a) X[a * kXtStride + t] = valid ? __ldg(src + a) : 0.0f;
+          const int a0 = half * 32;
+          if (vec) {
+            const uint4 m = *my_map;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const uint32_t e = tile_entry(m, k);
+              const int row = (int)(e >> 8), col4 = (int)(e & 255);
+              if (e != 0xffffu) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) X[(4 * col4 + e) * kXtStride + row] = rowv[4 * k + e];
+              }
+            }
           } else {
-            // an invalid token's extended row is all zero, so are its features
-            for (int a = p.d; a < DX; ++a) X[a * kXtStride + t] = (a == dp && valid) ? 1.0f : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 32; ++u)
+              if (a0 + u < p.d) X[(a0 + u) * kXtStride + t] = rowv[u];
           }
+          const float* src = kh + (valid ? i : 0) * p.d;
+          for (int a = 64 + half; a < p.d; a += 2) X[a * kXtStride + t] = valid ? __ldg(src + a) : 0.0f;
+          // an invalid token's extended row is all zero, so are its features
+          if (half == 1)
+            for (int a = p.d; a < DX; ++a) X[a * kXtStride + t] = (a == dp && valid) ? 1.0f : 0.0f;
         }
+        issue_next(c, false, st);
         gen_sync();
         for (int tcn = 0; ok && tcn < kRows / kChunk; ++tcn) {
           const int tok0 = tcn * kChunk + half * 16;
@@ -650,9 +817,9 @@ template <int DVP>
 size_t mom_smem(int d) {
   using L = MomLayout<DVP>;
   const int dp = dpad8(d), DX = dp + 8, XS = DX + 4;
-  const size_t xwords = (size_t)max(kRows * XS, DX * kXtStride);
+  const size_t xwords = (size_t)max(max(kRows * XS, DX * kXtStride), kRows * (DVP + 1));
   return 1024 + 2 * L::kSbuf + L::kVStages * L::kVStage + xwords * 4 + (size_t)L::kFT * 16 * 4 +
-         (size_t)L::kFT * kRows * 8 + 2 * kRows * 4 + 16 + (2 * kNStg + 12) * 8 + 16;
+         (size_t)L::kFT * kRows * 8 + 2 * kRows * 4 + 16 + 256 * 16 + (2 * kNStg + 12) * 8 + 16;
 }
 
 template <int DVP, bool DEG3>
