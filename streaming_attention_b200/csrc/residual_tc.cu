@@ -22,6 +22,14 @@
 // back to TMEM in place of S and is the A operand of O += P V.  K tiles are
 // K-major (128-byte swizzle); V tiles are MN-major (128-byte swizzle with
 // 32-byte atoms, the MN-major tf32 layout), both written by TMA.
+//
+// A tf32 MMA costs about the same for N = 64 as for N = 128, so both products
+// put the hi and remainder copies of their B operand side by side and take two
+// MMAs of twice the width per 8-wide K step instead of three:
+//   S' = Q_hi [K_hi; K_lo]^T + Q_lo [K_hi; K_lo]^T   (N = 128: each 32-column
+//        K chunk holds the 64 hi rows, then the 64 lo rows), S = S'[:, :64] + S'[:, 64:]
+//   O' = P_hi [V_hi | V_lo] + P_lo [V_hi | V_lo]     (N = 2 dv), O = O'[:, :dv] + O'[:, dv:]
+// (when 2 dv more TMEM columns do not fit, O takes the three-product form).
 #include <math.h>
 
 #include "sa_common.cuh"
@@ -58,7 +66,8 @@ struct ResTCParams {
 
 template <int DP, int DVP>
 struct Layout {
-  static constexpr uint32_t kKT = DP * kTile * 4;   // one K tile (hi or lo)
+  static constexpr uint32_t kKT = DP * kTile * 4;   // one K tile (hi or lo); chunk a: hi rows at
+                                                    // a * 2 * kTile * 128, lo rows 64 rows further
   static constexpr uint32_t kVT = DVP * kTile * 4;  // one V tile
   static constexpr uint32_t kStage = 2 * kKT + 2 * kVT;
   static constexpr int kStages = (200u * 1024u / kStage) >= 4 ? 4 : (int)(200u * 1024u / kStage);
@@ -68,6 +77,7 @@ struct Layout {
   static constexpr uint32_t kQhi = 0, kQlo = DP;
   static constexpr uint32_t kS0 = 2 * DP;           // buffer b: S/P_hi at kS0 + 128 b, P_lo at kS0 + 128 b + 64
   static constexpr uint32_t kO = 2 * DP + 256;
+  static constexpr bool kPVStack = kO + 2 * DVP <= 512;  // O' = P [V_hi | V_lo] fits
   static_assert(kO + DVP <= 512, "TMEM columns");
   static constexpr uint32_t kSmemBytes = kStages * kStage + kW + (2 * kStages + 10) * 8 + 64 + 2 * 128 * 4 + 1024;
 };
@@ -186,8 +196,8 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
         const CUtensorMap* mvl = rep ? &tm_rvl : &tm_vl;
 #pragma unroll
         for (int a = 0; a < DP / 32; ++a) {
-          tma_load_3d(st + a * (kTile * 128), mkh, &full[s], a * 32, row0, (int)h);
-          tma_load_3d(st + L::kKT + a * (kTile * 128), mkl, &full[s], a * 32, row0, (int)h);
+          tma_load_3d(st + a * (2 * kTile * 128), mkh, &full[s], a * 32, row0, (int)h);
+          tma_load_3d(st + a * (2 * kTile * 128) + kTile * 128, mkl, &full[s], a * 32, row0, (int)h);
         }
 #pragma unroll
         for (int a = 0; a < DVP / 32; ++a) {
@@ -211,8 +221,8 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_qk = idesc_tf32(128, kTile, false, false);
-      constexpr uint32_t idesc_pv = idesc_tf32(128, DVP, false, true);
+      constexpr uint32_t idesc_qk = idesc_tf32(128, 2 * kTile, false, false);
+      constexpr uint32_t idesc_pv = idesc_tf32(128, L::kPVStack ? 2 * DVP : DVP, false, true);
       bool ok = mbar_wait(qready, 0, ab, kErrWaitQ);
       if (ok) tc_fence_after();
       auto issue_pv = [&](int tp) -> bool {
@@ -226,10 +236,14 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
 #pragma unroll
         for (int kk = 0; kk < kTile / 8; ++kk) {
           const uint64_t bh_ = sdesc_sw128_atom32(vh + kk * 1024, kTile * 128, 512);
-          const uint64_t bl_ = sdesc_sw128_atom32(vl + kk * 1024, kTile * 128, 512);
           mma_tf32_ts(tmem + L::kO, ph + kk * 8, bh_, idesc_pv, (tp > 0 || kk > 0) ? 1u : 0u);
-          mma_tf32_ts(tmem + L::kO, ph + kk * 8, bl_, idesc_pv, 1u);
-          mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
+          if (L::kPVStack) {
+            mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
+          } else {
+            const uint64_t bl_ = sdesc_sw128_atom32(vl + kk * 1024, kTile * 128, 512);
+            mma_tf32_ts(tmem + L::kO, ph + kk * 8, bl_, idesc_pv, 1u);
+            mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
+          }
         }
         mma_commit(&empty[sp]);
         mma_commit(&sfree[bp]);
@@ -241,16 +255,14 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
         if (t >= 2 && !mbar_wait(&sfree[b], ((t >> 1) - 1) & 1, ab, kErrWaitSfree)) { ok = false; break; }
         tc_fence_after();
         const uint32_t kh = smem_u32(smem + s * L::kStage);
-        const uint32_t kl = kh + L::kKT;
         const uint32_t dS = tmem + L::kS0 + 128 * b;
 #pragma unroll
         for (int kk = 0; kk < DP / 8; ++kk) {
-          const uint32_t off = (kk >> 2) * (kTile * 128) + (kk & 3) * 32;
-          const uint64_t bh_ = sdesc_sw128(kh + off, 16, 1024);
-          const uint64_t bl_ = sdesc_sw128(kl + off, 16, 1024);
-          mma_tf32_ts(dS, tmem + L::kQhi + kk * 8, bh_, idesc_qk, kk > 0 ? 1u : 0u);
-          mma_tf32_ts(dS, tmem + L::kQhi + kk * 8, bl_, idesc_qk, 1u);
-          mma_tf32_ts(dS, tmem + L::kQlo + kk * 8, bh_, idesc_qk, 1u);
+          // N = 128 rows: the chunk's 64 hi rows, then its 64 lo rows
+          const uint32_t off = (kk >> 2) * (2 * kTile * 128) + (kk & 3) * 32;
+          const uint64_t bk = sdesc_sw128(kh + off, 16, 1024);
+          mma_tf32_ts(dS, tmem + L::kQhi + kk * 8, bk, idesc_qk, kk > 0 ? 1u : 0u);
+          mma_tf32_ts(dS, tmem + L::kQlo + kk * 8, bk, idesc_qk, 1u);
         }
         mma_commit(&sfull[b]);
         if (t >= 1 && !issue_pv(t - 1)) { ok = false; break; }
@@ -314,8 +326,15 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
       const int64_t row0 = rep ? (int64_t)t * kTile : kb0 + (int64_t)(t - n_rep) * kTile;
       const int64_t col0 = row0 + half * 32;
       float sv[32];
-      tmem_ld32(tS, sv);
-      tmem_wait_ld();
+      {
+        // S = Q K_hi^T + Q K_lo^T: the two halves of the N = 128 product
+        float s2[32];
+        tmem_ld32(tS, sv);
+        tmem_ld32(tS + 64, s2);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sv[j] += s2[j];
+      }
       uint32_t hi[32], lo[32];
       if (rep) {
         const bool all_on = col0 + 32 <= lim;
@@ -385,6 +404,13 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
         if (DVP == 32 && half != 0) continue;
         float ov[32];
         tmem_ld32(lane_addr + L::kO + cchunk * 32, ov);
+        if (L::kPVStack) {
+          float o2[32];
+          tmem_ld32(lane_addr + L::kO + DVP + cchunk * 32, o2);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ov[j] += o2[j];
+        }
         tmem_wait_ld();
         if (valid) {
 #pragma unroll
