@@ -26,6 +26,8 @@ int launch_compress(const float* k, const float* v, int64_t bh, int64_t n, int d
                     const float* dirs, const float* coins, const int32_t* perms, int32_t* rep_idx, float* rep_k,
                     float* rep_v, float* rep_w, SplitOut sp, cudaStream_t stream);
 int launch_split(const float* src, int64_t rows, int cols, int cols_pad, float* hi, float* lo, cudaStream_t stream);
+int launch_split_t(const float* src, int64_t bh, int64_t rows, int cols, int cols_pad, int64_t rows_pad, float* hi,
+                   float* lo, cudaStream_t stream);
 int residual_tc_dp(int d);
 int residual_tc_dvp(int dv);
 int launch_residual_tc(const CUtensorMap* maps, const float* q, const float* rep_w, int64_t r_pad, const float* low,
@@ -100,9 +102,11 @@ struct Workspace {
   bool tc = false;
   int groups = 0;
   int dp = 0, dvp = 0;
-  int64_t R = 0, r_pad = 0;
-  size_t status = 0, low = 0, master = 0, khi = 0, klo = 0, vhi = 0, vlo = 0;
-  size_t rkhi = 0, rklo = 0, rvhi = 0, rvlo = 0, rep_k = 0, rep_v = 0, rep_w = 0, rep_idx = 0, total = 0;
+  int64_t R = 0, r_pad = 0, n_pad = 0;
+  // k splits are row-major [bh, rows, dp]; v splits are transposed, [bh, dvp, pitch]
+  // (keys contiguous: the K-major layout of V for the tensor cores)
+  size_t status = 0, low = 0, master = 0, khi = 0, klo = 0, vthi = 0, vtlo = 0;
+  size_t rkhi = 0, rklo = 0, rvthi = 0, rvtlo = 0, rep_k = 0, rep_v = 0, rep_w = 0, rep_idx = 0, total = 0;
 };
 
 enum class Plan { kFull, kResidualOnly, kMomentsOnly };
@@ -112,12 +116,16 @@ Workspace plan(int64_t bh, int64_t n, int d, int dv, int degree, int bs, int com
   const bool simt = force_simt();
   w.dp = residual_tc_dp(d);
   w.dvp = residual_tc_dvp(dv);
-  w.tc = w.dp > 0 && w.dvp > 0 && !simt;
-  w.groups = (!simt && what != Plan::kResidualOnly) ? moments_tc_groups(d, dv, degree) : 0;
+  // TMA reads V^T tiles starting at block boundaries: the key coordinate must be
+  // a multiple of 4 floats (16 bytes)
+  const bool aligned_blocks = bs % 4 == 0;
+  w.tc = w.dp > 0 && w.dvp > 0 && !simt && aligned_blocks;
+  w.groups = (!simt && aligned_blocks && what != Plan::kResidualOnly) ? moments_tc_groups(d, dv, degree) : 0;
   if (w.groups > 0 && w.dvp == 0) w.dvp = dv <= 32 ? 32 : 64;
   const int64_t nc = n > 0 ? (n - 1) / bs : 0;
   w.R = (compressor == SA_COMPRESSOR_NONE) ? 0 : nc * ((bs + 1) / 2);
   w.r_pad = (w.R + 63) / 64 * 64;
+  w.n_pad = (n + 3) / 4 * 4;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t at = off;
@@ -134,16 +142,17 @@ Workspace plan(int64_t bh, int64_t n, int d, int dv, int degree, int bs, int com
     w.klo = take((size_t)bh * n * w.dp * f);
   }
   if (need_v_split) {
-    w.vhi = take((size_t)bh * n * w.dvp * f);
-    w.vlo = take((size_t)bh * n * w.dvp * f);
+    w.vthi = take((size_t)bh * w.dvp * w.n_pad * f);
+    w.vtlo = take((size_t)bh * w.dvp * w.n_pad * f);
   }
   if (what != Plan::kMomentsOnly) {
     if (w.tc) {
       w.rkhi = take((size_t)bh * w.R * w.dp * f);
       w.rklo = take((size_t)bh * w.R * w.dp * f);
-      w.rvhi = take((size_t)bh * w.R * w.dvp * f);
-      w.rvlo = take((size_t)bh * w.R * w.dvp * f);
+      w.rvthi = take((size_t)bh * w.dvp * w.r_pad * f);
+      w.rvtlo = take((size_t)bh * w.dvp * w.r_pad * f);
       w.rep_w = take((size_t)bh * w.r_pad * f);
+      if (what == Plan::kFull) w.rep_v = take((size_t)bh * w.R * dv * f);   // gathered rows, then transposed
     } else if (what == Plan::kFull) {
       w.rep_k = take((size_t)bh * w.R * d * f);
       w.rep_v = take((size_t)bh * w.R * dv * f);
@@ -176,12 +185,15 @@ EncodeTiledFn encode_tiled_fn() {
   return fn;
 }
 
-// 3-D tensor map over a [outer, rows, inner] fp32 array; box {32, box_rows, 1},
-// zero fill out of bounds.
-int encode_map_3d(CUtensorMap* map, const void* base, int inner, int64_t rows, int64_t outer, int box_rows,
-                  CUtensorMapSwizzle swizzle) {
+// 3-D tensor map over a [outer, rows, pitch] fp32 array of which the first
+// `inner` entries of each row are valid; box {32, box_rows, 1}, zero fill out of
+// bounds.
+int encode_map(CUtensorMap* map, const void* base, int64_t inner, int64_t pitch, int64_t rows, int64_t outer,
+               int box_rows, CUtensorMapSwizzle swizzle) {
+  if (inner < 1) inner = 1;
+  if (pitch < inner) pitch = inner;
   cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)(rows > 0 ? rows : 1), (cuuint64_t)(outer > 0 ? outer : 1)};
-  cuuint64_t strides[2] = {(cuuint64_t)inner * 4, (cuuint64_t)inner * 4 * (cuuint64_t)(rows > 0 ? rows : 1)};
+  cuuint64_t strides[2] = {(cuuint64_t)pitch * 4, (cuuint64_t)pitch * 4 * (cuuint64_t)(rows > 0 ? rows : 1)};
   cuuint32_t box[3] = {32, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   const EncodeTiledFn enc = encode_tiled_fn();
@@ -193,21 +205,36 @@ int encode_map_3d(CUtensorMap* map, const void* base, int inner, int64_t rows, i
   return SA_OK;
 }
 
-// Tensor maps over the split operands, then the tensor-core residual.
-// rep_src / cur_src: {k_hi, k_lo, v_hi, v_lo} of the reps (rep_rows rows per
-// sequence) and of all keys (n rows per sequence).
-int residual_tc_from_split(const Workspace& w, const float* const rep_src[4], int64_t rep_rows,
-                           const float* const cur_src[4], const float* rep_w, const float* q, const float* low,
-                           int groups, float* out, int* status, int64_t bh, int64_t n, int d, int dv, int degree,
-                           int block_size, int compressor, float scale, float eps, cudaStream_t s) {
+int encode_map_3d(CUtensorMap* map, const void* base, int inner, int64_t rows, int64_t outer, int box_rows,
+                  CUtensorMapSwizzle swizzle) {
+  return encode_map(map, base, inner, inner, rows, outer, box_rows, swizzle);
+}
+
+// Split operands of one key set (the reps, or every key of the sequences).
+struct TCOperands {
+  const float* khi;
+  const float* klo;
+  int64_t krows;          // k splits: [bh, krows, dp]
+  const float* vthi;
+  const float* vtlo;
+  int64_t vrows, vpitch;  // v splits: [bh, dvp, vpitch], vrows valid keys
+};
+
+// Tensor maps over the split operands, then the tensor-core residual.  Both
+// operands are K-major with the 128-byte swizzle: K tiles are 64 key rows of a
+// 32-column chunk; V^T tiles are dvp value rows of a 32-key chunk.
+int residual_tc_from_split(const Workspace& w, const TCOperands& rep, const TCOperands& cur, const float* rep_w,
+                           const float* q, const float* low, int groups, float* out, int* status, int64_t bh,
+                           int64_t n, int d, int dv, int degree, int block_size, int compressor, float scale,
+                           float eps, cudaStream_t s) {
   CUtensorMap maps[8];
-  const int widths[4] = {w.dp, w.dp, w.dvp, w.dvp};
-  for (int j = 0; j < 4; ++j) {
-    // K tiles: K-major, 128-byte swizzle; V tiles: MN-major, 128-byte swizzle with 32-byte atoms
-    const CUtensorMapSwizzle sw = j < 2 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-    int rc = encode_map_3d(&maps[j], rep_src[j], widths[j], rep_rows, bh, 64, sw);
-    if (rc) return rc;
-    rc = encode_map_3d(&maps[4 + j], cur_src[j], widths[j], n, bh, 64, sw);
+  const TCOperands* ops[2] = {&rep, &cur};
+  for (int j = 0; j < 2; ++j) {
+    const TCOperands& o = *ops[j];
+    int rc = encode_map_3d(&maps[4 * j + 0], o.khi, w.dp, o.krows, bh, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!rc) rc = encode_map_3d(&maps[4 * j + 1], o.klo, w.dp, o.krows, bh, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!rc) rc = encode_map(&maps[4 * j + 2], o.vthi, o.vrows, o.vpitch, w.dvp, bh, w.dvp, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!rc) rc = encode_map(&maps[4 * j + 3], o.vtlo, o.vrows, o.vpitch, w.dvp, bh, w.dvp, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
   const int64_t m_blk = compressor == SA_COMPRESSOR_NONE ? block_size : (block_size + 1) / 2;
@@ -215,14 +242,15 @@ int residual_tc_from_split(const Workspace& w, const float* const rep_src[4], in
                             m_blk, scale, eps, s);
 }
 
-// Tensor-core moments into `part` ([groups, bh, n, dv+1]) from the split v.
-int moments_tc_from_split(const Workspace& w, char* ws, const float* vhi, const float* vlo, const float* q,
+// Tensor-core moments into `part` ([groups, bh, n, dv+1]) from the transposed
+// split v ([bh, dvp, n_pad]; K-major tiles of dvp value rows x 32 keys).
+int moments_tc_from_split(const Workspace& w, char* ws, const float* vthi, const float* vtlo, const float* q,
                           const float* k, float* part, int* status, int64_t bh, int64_t n, int d, int dv, int degree,
                           int block_size, float scale, cudaStream_t s) {
   CUtensorMap maps[2];
-  int rc = encode_map_3d(&maps[0], vhi, w.dvp, n, bh, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+  int rc = encode_map(&maps[0], vthi, n, w.n_pad, w.dvp, bh, w.dvp, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = encode_map_3d(&maps[1], vlo, w.dvp, n, bh, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+  rc = encode_map(&maps[1], vtlo, n, w.n_pad, w.dvp, bh, w.dvp, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   float* master = reinterpret_cast<float*>(ws + w.master);
   return launch_moments_tc(maps, q, k, part, master, status, bh, n, d, dv, degree, block_size, scale, s);
@@ -312,12 +340,12 @@ int sa_low_moments(const float* q, const float* k, const float* v, int64_t bh, i
   int* status = reinterpret_cast<int*>(ws + w.status);
   rc = reset_status(status, s);
   if (rc) return rc;
-  float* vhi = reinterpret_cast<float*>(ws + w.vhi);
-  float* vlo = reinterpret_cast<float*>(ws + w.vlo);
+  float* vthi = reinterpret_cast<float*>(ws + w.vthi);
+  float* vtlo = reinterpret_cast<float*>(ws + w.vtlo);
   float* part = reinterpret_cast<float*>(ws + w.low);
-  rc = launch_split(v, bh * n, dv, w.dvp, vhi, vlo, s);
+  rc = launch_split_t(v, bh, n, dv, w.dvp, w.n_pad, vthi, vtlo, s);
   if (rc) return rc;
-  rc = moments_tc_from_split(w, ws, vhi, vlo, q, k, part, status, bh, n, d, dv, degree, block_size, scale, s);
+  rc = moments_tc_from_split(w, ws, vthi, vtlo, q, k, part, status, bh, n, d, dv, degree, block_size, scale, s);
   if (rc) return rc;
   return launch_sum_groups(part, w.groups, bh * n * (dv + 1), low, s);
 }
@@ -360,21 +388,20 @@ int sa_residual_combine(const float* q, const float* k, const float* v, const fl
   rc = reset_status(status, s);
   if (rc) return rc;
   float* cur[4] = {reinterpret_cast<float*>(ws + w.khi), reinterpret_cast<float*>(ws + w.klo),
-                   reinterpret_cast<float*>(ws + w.vhi), reinterpret_cast<float*>(ws + w.vlo)};
+                   reinterpret_cast<float*>(ws + w.vthi), reinterpret_cast<float*>(ws + w.vtlo)};
   rc = launch_split(k, bh * n, d, w.dp, cur[0], cur[1], s);
   if (rc) return rc;
-  rc = launch_split(v, bh * n, dv, w.dvp, cur[2], cur[3], s);
+  rc = launch_split_t(v, bh, n, dv, w.dvp, w.n_pad, cur[2], cur[3], s);
   if (rc) return rc;
-  const float* rep_src[4] = {cur[0], cur[1], cur[2], cur[3]};
-  const float* cur_src[4] = {cur[0], cur[1], cur[2], cur[3]};
+  const TCOperands cur_ops{cur[0], cur[1], n, cur[2], cur[3], n, w.n_pad};
+  TCOperands rep_ops = cur_ops;
   float* wpad = nullptr;
-  int64_t rep_rows = n;
   if (have_reps) {
     float* r[4] = {reinterpret_cast<float*>(ws + w.rkhi), reinterpret_cast<float*>(ws + w.rklo),
-                   reinterpret_cast<float*>(ws + w.rvhi), reinterpret_cast<float*>(ws + w.rvlo)};
+                   reinterpret_cast<float*>(ws + w.rvthi), reinterpret_cast<float*>(ws + w.rvtlo)};
     rc = launch_split(rep_k, bh * w.R, d, w.dp, r[0], r[1], s);
     if (rc) return rc;
-    rc = launch_split(rep_v, bh * w.R, dv, w.dvp, r[2], r[3], s);
+    rc = launch_split_t(rep_v, bh, w.R, dv, w.dvp, w.r_pad, r[2], r[3], s);
     if (rc) return rc;
     wpad = reinterpret_cast<float*>(ws + w.rep_w);
     cudaError_t ce = cudaMemsetAsync(wpad, 0, (size_t)bh * w.r_pad * sizeof(float), s);
@@ -382,11 +409,10 @@ int sa_residual_combine(const float* q, const float* k, const float* v, const fl
       ce = cudaMemcpy2DAsync(wpad, (size_t)w.r_pad * sizeof(float), rep_w, (size_t)w.R * sizeof(float),
                              (size_t)w.R * sizeof(float), (size_t)bh, cudaMemcpyDeviceToDevice, s);
     if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "rep weight copy: %s", cudaGetErrorString(ce));
-    for (int j = 0; j < 4; ++j) rep_src[j] = r[j];
-    rep_rows = w.R;
+    rep_ops = TCOperands{r[0], r[1], w.R, r[2], r[3], w.R, w.r_pad};
   }
-  return residual_tc_from_split(w, rep_src, rep_rows, cur_src, wpad, q, low, 1, out, status, bh, n, d, dv, degree,
-                                block_size, compressor, scale, eps, s);
+  return residual_tc_from_split(w, rep_ops, cur_ops, wpad, q, low, 1, out, status, bh, n, d, dv, degree, block_size,
+                                compressor, scale, eps, s);
 }
 
 int sa_fast_attention_workspace_size(int64_t bh, int64_t n, int d, int dv, int degree, int block_size, int compressor,
@@ -427,14 +453,14 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
   // operand splits shared by the tensor-core kernels
   float* khi = reinterpret_cast<float*>(ws + w.khi);
   float* klo = reinterpret_cast<float*>(ws + w.klo);
-  float* vhi = reinterpret_cast<float*>(ws + w.vhi);
-  float* vlo = reinterpret_cast<float*>(ws + w.vlo);
+  float* vthi = reinterpret_cast<float*>(ws + w.vthi);
+  float* vtlo = reinterpret_cast<float*>(ws + w.vtlo);
   if (w.tc) {
     rc = launch_split(k, bh * n, d, w.dp, khi, klo, s);
     if (rc) return rc;
   }
   if (w.tc || w.groups > 0) {
-    rc = launch_split(v, bh * n, dv, w.dvp, vhi, vlo, s);
+    rc = launch_split_t(v, bh, n, dv, w.dvp, w.n_pad, vthi, vtlo, s);
     if (rc) return rc;
   }
 
@@ -442,29 +468,27 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
   const float* rk = k;
   const float* rv = v;
   float* rw = nullptr;
-  const float* rep_src[4] = {khi, klo, vhi, vlo};
-  int64_t rep_rows = n;
+  const TCOperands cur_ops{khi, klo, n, vthi, vtlo, n, w.n_pad};
+  TCOperands rep_ops = cur_ops;
   if (compress) {
     if (w.tc) {
       SplitOut sp;
       sp.khi = reinterpret_cast<float*>(ws + w.rkhi);
       sp.klo = reinterpret_cast<float*>(ws + w.rklo);
-      sp.vhi = reinterpret_cast<float*>(ws + w.rvhi);
-      sp.vlo = reinterpret_cast<float*>(ws + w.rvlo);
       sp.dp = w.dp;
-      sp.dvp = w.dvp;
       sp.w_stride = w.r_pad;
       rw = reinterpret_cast<float*>(ws + w.rep_w);
+      float* rep_v = reinterpret_cast<float*>(ws + w.rep_v);
       const cudaError_t ce = cudaMemsetAsync(rw, 0, (size_t)bh * w.r_pad * sizeof(float), s);
       if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "rep weight reset: %s", cudaGetErrorString(ce));
-      rc = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, ridx, nullptr, nullptr, rw,
+      rc = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, ridx, nullptr, rep_v, rw,
                            sp, s);
       if (rc) return rc;
-      rep_src[0] = sp.khi;
-      rep_src[1] = sp.klo;
-      rep_src[2] = sp.vhi;
-      rep_src[3] = sp.vlo;
-      rep_rows = w.R;
+      float* rvthi = reinterpret_cast<float*>(ws + w.rvthi);
+      float* rvtlo = reinterpret_cast<float*>(ws + w.rvtlo);
+      rc = launch_split_t(rep_v, bh, w.R, dv, w.dvp, w.r_pad, rvthi, rvtlo, s);
+      if (rc) return rc;
+      rep_ops = TCOperands{sp.khi, sp.klo, w.R, rvthi, rvtlo, w.R, w.r_pad};
     } else {
       float* rep_k = reinterpret_cast<float*>(ws + w.rep_k);
       float* rep_v = reinterpret_cast<float*>(ws + w.rep_v);
@@ -479,18 +503,16 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
 
   // M: low-degree moments
   if (w.groups > 0)
-    rc = moments_tc_from_split(w, ws, vhi, vlo, q, k, low, status, bh, n, d, dv, degree, block_size, scale, s);
+    rc = moments_tc_from_split(w, ws, vthi, vtlo, q, k, low, status, bh, n, d, dv, degree, block_size, scale, s);
   else
     rc = launch_low_moments(q, k, v, bh, n, d, dv, degree, block_size, scale, low, s);
   if (rc) return rc;
   const int groups = w.groups > 0 ? w.groups : 1;
 
   // R: residual + combine
-  if (w.tc) {
-    const float* cur_src[4] = {khi, klo, vhi, vlo};
-    return residual_tc_from_split(w, rep_src, rep_rows, cur_src, rw, q, low, groups, out, status, bh, n, d, dv,
-                                  degree, block_size, compressor, scale, eps, s);
-  }
+  if (w.tc)
+    return residual_tc_from_split(w, rep_ops, cur_ops, rw, q, low, groups, out, status, bh, n, d, dv, degree,
+                                  block_size, compressor, scale, eps, s);
   if (groups > 1) {  // the CUDA-core residual reads one summed slice
     rc = launch_sum_groups(low, groups, bh * n * (dv + 1), low, s);
     if (rc) return rc;

@@ -134,12 +134,6 @@ compress_blocks_kernel(const float* __restrict__ k, const float* __restrict__ v,
         sp.khi[(rbase + p) * sp.dp + a] = hi;
         sp.klo[(rbase + p) * sp.dp + a] = x - hi;
       }
-      for (int a = lane; a < sp.dvp; a += 32) {
-        const float x = a < dv ? __ldg(v + src * dv + a) : 0.0f;
-        const float hi = __uint_as_float(tc_split_hi(x));
-        sp.vhi[(rbase + p) * sp.dvp + a] = hi;
-        sp.vlo[(rbase + p) * sp.dvp + a] = x - hi;
-      }
     }
   }
 }
@@ -157,6 +151,38 @@ __global__ void split_rows_kernel(const float* __restrict__ src, int64_t rows, i
     const float h = __uint_as_float(tc_split_hi(x));
     hi[e] = h;
     lo[e] = x - h;
+  }
+}
+
+// Transposing split: src [bh, rows, cols] -> hi / lo [bh, cols_pad, rows_pad]
+// (tf32 hi and fp32 remainder, zero padded), through a 32 x 32 shared tile so
+// that both the reads and the writes are coalesced.  This is the K-major
+// layout of V for the tensor cores (keys contiguous per value column).
+__global__ void split_transpose_kernel(const float* __restrict__ src, int64_t rows, int cols, int cols_pad,
+                                       int64_t rows_pad, float* __restrict__ hi, float* __restrict__ lo) {
+  __shared__ float tile[32][33];
+  const int64_t h = blockIdx.z;
+  const int64_t r0 = (int64_t)blockIdx.x * 32;
+  const int c0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;   // 32 x 8
+  const float* sh = src + h * rows * cols;
+  for (int yy = ty; yy < 32; yy += 8) {
+    const int64_t r = r0 + yy;
+    const int c = c0 + tx;
+    tile[yy][tx] = (r < rows && c < cols) ? __ldg(sh + r * cols + c) : 0.0f;
+  }
+  __syncthreads();
+  float* hh = hi + h * cols_pad * rows_pad;
+  float* lh = lo + h * cols_pad * rows_pad;
+  for (int yy = ty; yy < 32; yy += 8) {
+    const int c = c0 + yy;
+    const int64_t r = r0 + tx;
+    if (c < cols_pad && r < rows_pad) {
+      const float x = tile[tx][yy];
+      const float xh = __uint_as_float(tc_split_hi(x));
+      hh[(int64_t)c * rows_pad + r] = xh;
+      lh[(int64_t)c * rows_pad + r] = x - xh;
+    }
   }
 }
 
@@ -185,6 +211,16 @@ int launch_compress(const float* k, const float* v, int64_t bh, int64_t n, int d
                                                                    use_perm ? 1 : 0, dirs, coins, perms, rep_idx,
                                                                    rep_k, rep_v, rep_w, sp);
   return check_launch("compress_blocks_kernel");
+}
+
+int launch_split_t(const float* src, int64_t bh, int64_t rows, int cols, int cols_pad, int64_t rows_pad, float* hi,
+                   float* lo, cudaStream_t stream) {
+  if (bh == 0 || rows_pad == 0) return SA_OK;
+  if (bh > 65535 || (rows_pad + 31) / 32 > 2147483647LL)
+    return set_error(SA_ERR_UNSUPPORTED, "too many sequences for one launch");
+  dim3 grid((unsigned)((rows_pad + 31) / 32), (unsigned)((cols_pad + 31) / 32), (unsigned)bh);
+  split_transpose_kernel<<<grid, dim3(32, 8), 0, stream>>>(src, rows, cols, cols_pad, rows_pad, hi, lo);
+  return check_launch("split_transpose_kernel");
 }
 
 int launch_split(const float* src, int64_t rows, int cols, int cols_pad, float* hi, float* lo, cudaStream_t stream) {

@@ -27,8 +27,8 @@
 // TMEM lane quarter: thread t of each half owns TMEM lane t, i.e. token t in
 // the query phase and feature t of the tile in the update phase, and each
 // half writes half of every chunk's columns.  V chunks (tf32 hi / fp32
-// remainder copies made by the split pass) arrive by TMA, MN-major with the
-// 32-byte-atom swizzle.
+// remainder copies made by the transposing split pass) arrive by TMA, K-major
+// with the 128-byte swizzle: dv hi rows, then dv lo rows, of 32 tokens.
 //
 // Each 8-wide K step takes two MMAs of N = 2*DVP: A_hi and A_lo times
 // B = [B_hi | B_lo] (the hi and remainder copies of V or of the state sit one
@@ -85,8 +85,7 @@ struct MomLayout {
   // shared memory
   static constexpr uint32_t kSbufHalf = (DVP / 32) * kRows * 128;    // hi or lo: DVP/32 chunks x 128 rows x 128 B
   static constexpr uint32_t kSbuf = 2 * kSbufHalf;                   // hi + lo
-  static constexpr uint32_t kVHalf = (DVP / 32) * kChunk * 128;     // V chunk hi or lo
-  static constexpr uint32_t kVStage = 2 * kVHalf;
+  static constexpr uint32_t kVStage = 2 * DVP * 128;                // V^T chunk: DVP hi + DVP lo rows x 32 tokens
   static constexpr int kVStages = 2;
 };
 
@@ -374,11 +373,9 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
             mbar_arrive_expect_tx(&v_full[s], L::kVStage);
             uint8_t* dst = vst + s * L::kVStage;
             const int row = (int)(t0 + tc * kChunk);
-#pragma unroll
-            for (int a = 0; a < DVP / 32; ++a) {
-              tma_load_3d(dst + a * (kChunk * 128), &tm_vh, &v_full[s], a * 32, row, (int)h);
-              tma_load_3d(dst + L::kVHalf + a * (kChunk * 128), &tm_vl, &v_full[s], a * 32, row, (int)h);
-            }
+            // V^T chunk: DVP hi rows, then DVP lo rows, of 32 tokens (128 B) each
+            tma_load_3d(dst, &tm_vh, &v_full[s], row, 0, (int)h);
+            tma_load_3d(dst + DVP * 128, &tm_vl, &v_full[s], row, 0, (int)h);
           }
         }
       }
@@ -391,9 +388,11 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      // B = [hi | lo] of V or of the state: both copies sit at one chunk stride, so a
-      // single MMA of N = 2*DVP multiplies A by both; B MN-major in both products
+      // B = [hi | lo] of V or of the state: both copies sit at one chunk / row
+      // stride, so a single MMA of N = 2*DVP multiplies A by both.  The state is
+      // MN-major (written by the generators); V is K-major (transposed split).
       constexpr uint32_t idesc = idesc_tf32(128, 2 * DVP, false, true);
+      constexpr uint32_t idesc_v = idesc_tf32(128, 2 * DVP, false, false);
       int stg_use = 0, sb_use = 0, v_use = 0, sub_use = 0;
       bool ok = true;
       for (int64_t c = 0; ok && c < nb; ++c) {
@@ -446,11 +445,11 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
                 const uint32_t dS = tmem + j * L::kTC;
 #pragma unroll
                 for (int kk = 0; kk < kChunk / 8; ++kk) {
-                  const uint64_t db = sdesc_sw128_atom32(vhi + kk * 1024, kChunk * 128, 512);
+                  const uint64_t db = sdesc_sw128(vhi + kk * 32, 16, 1024);
                   // dS_j starts from zero in every block
                   const uint32_t acc = (st > 0 || tc > 0 || kk > 0) ? 1u : 0u;
-                  mma_tf32_ts(dS, ahi + kk * 8, db, idesc, acc);
-                  mma_tf32_ts(dS, alo + kk * 8, db, idesc, 1u);
+                  mma_tf32_ts(dS, ahi + kk * 8, db, idesc_v, acc);
+                  mma_tf32_ts(dS, alo + kk * 8, db, idesc_v, 1u);
                 }
                 mma_commit(&stg_free[b]);
               }

@@ -19,16 +19,18 @@
 // lo = x - hi, and each product uses hi*hi + hi*lo + lo*hi, which keeps the
 // result within a few fp32 ulps (a single TF32 product loses ~11 bits).
 // Q (hi/lo) lives in TMEM as the A operand of S = Q K^T; P (hi/lo) is written
-// back to TMEM in place of S and is the A operand of O += P V.  K tiles are
-// K-major (128-byte swizzle); V tiles are MN-major (128-byte swizzle with
-// 32-byte atoms, the MN-major tf32 layout), both written by TMA.
+// back to TMEM in place of S and is the A operand of O += P V.  Both B operands
+// are K-major with the 128-byte swizzle, written by TMA: K tiles from the
+// row-major k split, V tiles from the transposed v split (an MN-major tf32
+// operand runs markedly slower on the tensor cores).
 //
 // A tf32 MMA costs about the same for N = 64 as for N = 128, so both products
 // put the hi and remainder copies of their B operand side by side and take two
 // MMAs of twice the width per 8-wide K step instead of three:
 //   S' = Q_hi [K_hi; K_lo]^T + Q_lo [K_hi; K_lo]^T   (N = 128: each 32-column
 //        K chunk holds the 64 hi rows, then the 64 lo rows), S = S'[:, :64] + S'[:, 64:]
-//   O' = P_hi [V_hi | V_lo] + P_lo [V_hi | V_lo]     (N = 2 dv), O = O'[:, :dv] + O'[:, dv:]
+//   O' = P_hi [V_hi | V_lo] + P_lo [V_hi | V_lo]     (N = 2 dv: each 32-key chunk of
+//        the V^T tile holds the dv hi rows, then the dv lo rows), O = O'[:, :dv] + O'[:, dv:]
 // (when 2 dv more TMEM columns do not fit, O takes the three-product form).
 #include <math.h>
 
@@ -68,7 +70,8 @@ template <int DP, int DVP>
 struct Layout {
   static constexpr uint32_t kKT = DP * kTile * 4;   // one K tile (hi or lo); chunk a: hi rows at
                                                     // a * 2 * kTile * 128, lo rows 64 rows further
-  static constexpr uint32_t kVT = DVP * kTile * 4;  // one V tile
+  static constexpr uint32_t kVT = DVP * kTile * 4;  // one V tile (hi or lo); 32-key chunk a: hi rows at
+                                                    // a * 2 * DVP * 128, lo rows DVP rows further
   static constexpr uint32_t kStage = 2 * kKT + 2 * kVT;
   static constexpr int kStages = (200u * 1024u / kStage) >= 4 ? 4 : (int)(200u * 1024u / kStage);
   static_assert(kStages >= 2, "at least double buffering");
@@ -200,9 +203,10 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
           tma_load_3d(st + a * (2 * kTile * 128) + kTile * 128, mkl, &full[s], a * 32, row0, (int)h);
         }
 #pragma unroll
-        for (int a = 0; a < DVP / 32; ++a) {
-          tma_load_3d(st + 2 * L::kKT + a * (kTile * 128), mvh, &full[s], a * 32, row0, (int)h);
-          tma_load_3d(st + 2 * L::kKT + L::kVT + a * (kTile * 128), mvl, &full[s], a * 32, row0, (int)h);
+        for (int a = 0; a < kTile / 32; ++a) {
+          uint8_t* vd = st + 2 * L::kKT + a * (2 * DVP * 128);
+          tma_load_3d(vd, mvh, &full[s], row0 + a * 32, 0, (int)h);
+          tma_load_3d(vd + DVP * 128, mvl, &full[s], row0 + a * 32, 0, (int)h);
         }
         if (with_w) bulk_load(wbuf + s * kTile, p.rep_w + h * p.r_pad + row0, kTile * 4, &full[s]);
         ++issued;
@@ -222,25 +226,26 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_tf32(128, 2 * kTile, false, false);
-      constexpr uint32_t idesc_pv = idesc_tf32(128, L::kPVStack ? 2 * DVP : DVP, false, true);
+      constexpr uint32_t idesc_pv = idesc_tf32(128, L::kPVStack ? 2 * DVP : DVP, false, false);
       bool ok = mbar_wait(qready, 0, ab, kErrWaitQ);
       if (ok) tc_fence_after();
       auto issue_pv = [&](int tp) -> bool {
         const int sp = tp % kStages, bp = tp & 1;
         if (!mbar_wait(&pfull[bp], (tp >> 1) & 1, ab, kErrWaitP)) return false;
         tc_fence_after();
-        const uint32_t vh = smem_u32(smem + sp * L::kStage + 2 * L::kKT);
-        const uint32_t vl = vh + L::kVT;
+        const uint32_t vt = smem_u32(smem + sp * L::kStage + 2 * L::kKT);
         const uint32_t ph = tmem + L::kS0 + 128 * bp;
         const uint32_t pl = ph + 64;
 #pragma unroll
         for (int kk = 0; kk < kTile / 8; ++kk) {
-          const uint64_t bh_ = sdesc_sw128_atom32(vh + kk * 1024, kTile * 128, 512);
+          // 8 keys of 32-key chunk kk / 4: rows = value columns (hi rows, then lo rows)
+          const uint32_t vc = vt + (kk >> 2) * (2 * DVP * 128) + (kk & 3) * 32;
+          const uint64_t bh_ = sdesc_sw128(vc, 16, 1024);
           mma_tf32_ts(tmem + L::kO, ph + kk * 8, bh_, idesc_pv, (tp > 0 || kk > 0) ? 1u : 0u);
           if (L::kPVStack) {
             mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
           } else {
-            const uint64_t bl_ = sdesc_sw128_atom32(vl + kk * 1024, kTile * 128, 512);
+            const uint64_t bl_ = sdesc_sw128(vc + DVP * 128, 16, 1024);
             mma_tf32_ts(tmem + L::kO, ph + kk * 8, bl_, idesc_pv, 1u);
             mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
           }

@@ -83,11 +83,9 @@ __host__ __device__ inline Monomial monomial_of(int64_t f, int d) {
 // Optional tf32 hi / fp32 remainder copies of the gathered reps, the operand
 // format of the tensor-core residual (zero padded to dp / dvp columns).
 struct SplitOut {
-  float* khi = nullptr;
+  float* khi = nullptr;   // rep keys, tf32 hi / fp32 remainder, [bh, R, dp]
   float* klo = nullptr;
-  float* vhi = nullptr;
-  float* vlo = nullptr;
-  int dp = 0, dvp = 0;
+  int dp = 0;
   int64_t w_stride = 0;  // per-sequence stride of rep_w
 };
 

@@ -79,8 +79,9 @@ def test_workspace_size_and_argument_errors_without_gpu():
     assert lib.sa_fast_attention_workspace_size(256, 8192, 64, 64, 2, 128, 1, ctypes.byref(sz)) == 0
     R = 63 * 64
     # tensor-core layout: G partial slices of the low sums and the fp32 moment state of G
-    # feature groups, hi/lo copies of k, v and of the reps, rep weights and indices
-    fixed = 4 * 256 * 8192 * 64 * 4 + 4 * 256 * R * 64 * 4 + 256 * R * 4 + 256 * R * 4
+    # feature groups, hi/lo copies of k, v (transposed) and of the reps, rep weights and
+    # indices, and the gathered rep values before their transposing split
+    fixed = 4 * 256 * 8192 * 64 * 4 + 4 * 256 * R * 64 * 4 + 256 * R * 4 + 256 * R * 4 + 256 * R * 64 * 4
     per_group = 256 * 8192 * 65 * 4 + 256 * 3 * 128 * 64 * 4   # three state tiles of 128 features per group
     groups = (sz.value - fixed) // per_group
     assert 2 <= groups <= 8
