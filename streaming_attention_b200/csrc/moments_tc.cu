@@ -387,7 +387,8 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     }
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // the whole warp runs the loop; the elected lane issues MMAs and commits
+    {
       // B = [hi | lo] of V or of the state: both copies sit at one chunk / row
       // stride, so a single MMA of N = 2*DVP multiplies A by both.  The state is
       // MN-major (written by the generators); V is K-major (transposed split).
@@ -400,17 +401,17 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
           const int64_t b1 = min((c + 1) * (int64_t)p.bs, p.n);
           const int nsq = (int)((b1 - c * (int64_t)p.bs + kRows - 1) / kRows);  // query sub-tiles of block c
           for (int st = 0; ok && st < nsq; ++st, ++sub_use) {
-            if (sub_use >= 1 && !mbar_wait(out_free, (sub_use - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+            if (sub_use >= 1 && !mbar_wait_warp(out_free, (sub_use - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
             tc_fence_after();
             for (int j = 0; ok && j < ntiles; ++j, ++sb_use) {
               const int sb = sb_use & 1;
-              if (!mbar_wait(&sb_full[sb], (sb_use >> 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+              if (!mbar_wait_warp(&sb_full[sb], (sb_use >> 1) & 1, ab, kErrMomWait)) { ok = false; break; }
               tc_fence_after();
               const uint32_t bhi = smem_u32(sbuf + sb * L::kSbuf);
               const uint32_t dO = tmem + j * L::kTC;
               for (int kc = 0; kc < kRows / kChunk; ++kc, ++stg_use) {
                 const int b = stg_use % kNStg;
-                if (!mbar_wait(&stg_full[b], (stg_use / kNStg) & 1, ab, kErrMomWait)) { ok = false; break; }
+                if (!mbar_wait_warp(&stg_full[b], (stg_use / kNStg) & 1, ab, kErrMomWait)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t ahi = tmem + L::kStg + b * 2 * kChunk;
                 const uint32_t alo = ahi + kChunk;
@@ -418,27 +419,27 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
                 for (int kk = 0; kk < kChunk / 8; ++kk) {
                   const uint32_t off = (kc * kChunk + kk * 8) * 128;   // 8 feature rows of 128 B
                   const uint64_t db = sdesc_sw128_atom32(bhi + off, kRows * 128, 512);
-                  mma_tf32_ts(dO, ahi + kk * 8, db, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
-                  mma_tf32_ts(dO, alo + kk * 8, db, idesc, 1u);
+                  if (elect_one()) mma_tf32_ts(dO, ahi + kk * 8, db, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+                  if (elect_one()) mma_tf32_ts(dO, alo + kk * 8, db, idesc, 1u);
                 }
-                mma_commit(&stg_free[b]);
+                if (elect_one()) mma_commit(&stg_free[b]);
               }
-              mma_commit(&sb_free[sb]);
+              if (elect_one()) mma_commit(&sb_free[sb]);
             }
             // one commit per sub-tile: it completes once every tile's MMAs are done
             // (a waiter must never fall two phases behind an mbarrier)
-            if (ok) mma_commit(out_full);
+            if (ok && elect_one()) mma_commit(out_full);
           }
         }
         if (ok && c + 1 < nb) {
           for (int st = 0; ok && st < sub; ++st) {
             for (int tc = 0; ok && tc < kRows / kChunk; ++tc, ++v_use) {
               const int vs = v_use & 1;
-              if (!mbar_wait(&v_full[vs], (v_use >> 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+              if (!mbar_wait_warp(&v_full[vs], (v_use >> 1) & 1, ab, kErrMomWait)) { ok = false; break; }
               const uint32_t vhi = smem_u32(vst + vs * L::kVStage);
               for (int j = 0; ok && j < ntiles; ++j, ++stg_use) {
                 const int b = stg_use % kNStg;
-                if (!mbar_wait(&stg_full[b], (stg_use / kNStg) & 1, ab, kErrMomWait)) { ok = false; break; }
+                if (!mbar_wait_warp(&stg_full[b], (stg_use / kNStg) & 1, ab, kErrMomWait)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t ahi = tmem + L::kStg + b * 2 * kChunk;
                 const uint32_t alo = ahi + kChunk;
@@ -448,18 +449,18 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
                   const uint64_t db = sdesc_sw128(vhi + kk * 32, 16, 1024);
                   // dS_j starts from zero in every block
                   const uint32_t acc = (st > 0 || tc > 0 || kk > 0) ? 1u : 0u;
-                  mma_tf32_ts(dS, ahi + kk * 8, db, idesc_v, acc);
-                  mma_tf32_ts(dS, alo + kk * 8, db, idesc_v, 1u);
+                  if (elect_one()) mma_tf32_ts(dS, ahi + kk * 8, db, idesc_v, acc);
+                  if (elect_one()) mma_tf32_ts(dS, alo + kk * 8, db, idesc_v, 1u);
                 }
-                mma_commit(&stg_free[b]);
+                if (elect_one()) mma_commit(&stg_free[b]);
               }
-              mma_commit(&v_free[vs]);
+              if (elect_one()) mma_commit(&v_free[vs]);
             }
           }
-          if (ok) mma_commit(u_done);
+          if (ok && elect_one()) mma_commit(u_done);
         }
       }
-      mma_commit(drain);
+      if (elect_one()) mma_commit(drain);
       const uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(drain, 0)) {
         if (globaltimer_ns() - t0 > 2000000000ull) {
@@ -467,6 +468,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
           break;
         }
       }
+      __syncwarp();
     }
   } else {
     // -------------------------------------------------------------- generators

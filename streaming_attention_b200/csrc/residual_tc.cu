@@ -10,7 +10,8 @@
 // 64 rows: first the coreset reps of the blocks before the tile, then the keys
 // of the current block(s).  Roles:
 //   warp 0      TMA producer: K_hi, K_lo, V_hi, V_lo (+ rep weights) per stage
-//   warp 1      TMEM owner; lane 0 issues every tcgen05.mma and commit
+//   warp 1      TMEM owner and MMA issuer: the converged warp runs the loop, an
+//               elected lane issues every tcgen05.mma and commit
 //   warps 2..9  query rows: two warps per TMEM lane quarter, one row per
 //               thread, each warp of a pair owning 32 of a tile's 64 columns;
 //               they write the scaled query into TMEM, turn each S tile into
@@ -224,14 +225,15 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // the whole warp runs the loop; the elected lane issues MMAs and commits
+    {
       constexpr uint32_t idesc_qk = idesc_tf32(128, 2 * kTile, false, false);
       constexpr uint32_t idesc_pv = idesc_tf32(128, L::kPVStack ? 2 * DVP : DVP, false, false);
-      bool ok = mbar_wait(qready, 0, ab, kErrWaitQ);
+      bool ok = mbar_wait_warp(qready, 0, ab, kErrWaitQ);
       if (ok) tc_fence_after();
       auto issue_pv = [&](int tp) -> bool {
         const int sp = tp % kStages, bp = tp & 1;
-        if (!mbar_wait(&pfull[bp], (tp >> 1) & 1, ab, kErrWaitP)) return false;
+        if (!mbar_wait_warp(&pfull[bp], (tp >> 1) & 1, ab, kErrWaitP)) return false;
         tc_fence_after();
         const uint32_t vt = smem_u32(smem + sp * L::kStage + 2 * L::kKT);
         const uint32_t ph = tmem + L::kS0 + 128 * bp;
@@ -241,23 +243,23 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
           // 8 keys of 32-key chunk kk / 4: rows = value columns (hi rows, then lo rows)
           const uint32_t vc = vt + (kk >> 2) * (2 * DVP * 128) + (kk & 3) * 32;
           const uint64_t bh_ = sdesc_sw128(vc, 16, 1024);
-          mma_tf32_ts(tmem + L::kO, ph + kk * 8, bh_, idesc_pv, (tp > 0 || kk > 0) ? 1u : 0u);
+          if (elect_one()) mma_tf32_ts(tmem + L::kO, ph + kk * 8, bh_, idesc_pv, (tp > 0 || kk > 0) ? 1u : 0u);
           if (L::kPVStack) {
-            mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
+            if (elect_one()) mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
           } else {
             const uint64_t bl_ = sdesc_sw128(vc + DVP * 128, 16, 1024);
-            mma_tf32_ts(tmem + L::kO, ph + kk * 8, bl_, idesc_pv, 1u);
-            mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
+            if (elect_one()) mma_tf32_ts(tmem + L::kO, ph + kk * 8, bl_, idesc_pv, 1u);
+            if (elect_one()) mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
           }
         }
-        mma_commit(&empty[sp]);
-        mma_commit(&sfree[bp]);
+        if (elect_one()) mma_commit(&empty[sp]);
+        if (elect_one()) mma_commit(&sfree[bp]);
         return true;
       };
       for (int t = 0; ok && t < T; ++t) {
         const int s = t % kStages, b = t & 1;
-        if (!mbar_wait(&full[s], (t / kStages) & 1, ab, kErrWaitFull)) { ok = false; break; }
-        if (t >= 2 && !mbar_wait(&sfree[b], ((t >> 1) - 1) & 1, ab, kErrWaitSfree)) { ok = false; break; }
+        if (!mbar_wait_warp(&full[s], (t / kStages) & 1, ab, kErrWaitFull)) { ok = false; break; }
+        if (t >= 2 && !mbar_wait_warp(&sfree[b], ((t >> 1) - 1) & 1, ab, kErrWaitSfree)) { ok = false; break; }
         tc_fence_after();
         const uint32_t kh = smem_u32(smem + s * L::kStage);
         const uint32_t dS = tmem + L::kS0 + 128 * b;
@@ -266,16 +268,16 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
           // N = 128 rows: the chunk's 64 hi rows, then its 64 lo rows
           const uint32_t off = (kk >> 2) * (2 * kTile * 128) + (kk & 3) * 32;
           const uint64_t bk = sdesc_sw128(kh + off, 16, 1024);
-          mma_tf32_ts(dS, tmem + L::kQhi + kk * 8, bk, idesc_qk, kk > 0 ? 1u : 0u);
-          mma_tf32_ts(dS, tmem + L::kQlo + kk * 8, bk, idesc_qk, 1u);
+          if (elect_one()) mma_tf32_ts(dS, tmem + L::kQhi + kk * 8, bk, idesc_qk, kk > 0 ? 1u : 0u);
+          if (elect_one()) mma_tf32_ts(dS, tmem + L::kQlo + kk * 8, bk, idesc_qk, 1u);
         }
-        mma_commit(&sfull[b]);
+        if (elect_one()) mma_commit(&sfull[b]);
         if (t >= 1 && !issue_pv(t - 1)) { ok = false; break; }
       }
       if (ok && T > 0) ok = issue_pv(T - 1);
-      if (ok) mma_commit(ofull);
+      if (ok && elect_one()) mma_commit(ofull);
       // drain: nothing of ours may still write TMEM when it is freed
-      mma_commit(drain);
+      if (elect_one()) mma_commit(drain);
       const uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(drain, 0)) {
         if (globaltimer_ns() - t0 > 2000000000ull) {
@@ -283,6 +285,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
           break;
         }
       }
+      __syncwarp();
     }
   } else {
     // ------------------------------------------------------------ query rows

@@ -86,6 +86,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   }
 }
 
+// mbar_wait for all 32 lanes of a converged warp; the warp leaves together,
+// with one verdict.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, const Abort& ab, int code) {
+  const bool r = mbar_wait(bar, parity, ab, code);
+  return __all_sync(0xffffffffu, r);
+}
+
 // ---------------------------------------------------------------------------
 // TMA (no multicast anywhere in this library)
 // ---------------------------------------------------------------------------
@@ -228,6 +235,18 @@ __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
       ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
       : "memory");
+}
+
+// One elected lane of a converged warp (elect.sync over the full mask).  An MMA
+// issuer warp runs its loop with all 32 lanes, so that descriptor arithmetic
+// stays warp-uniform, and lets the elected lane issue each tcgen05.mma and each
+// tcgen05.commit; both must go through the same election so that a commit
+// tracks the MMAs before it.  Issuing from a single diverged lane instead costs
+// about 1.4x more time per MMA.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile("{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\t@P mov.u32 %0, 1;\n\t}" : "+r"(pred));
+  return pred != 0;
 }
 
 // Arrive once on `bar` when every tcgen05 operation this thread issued so far has completed.
