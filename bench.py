@@ -95,6 +95,10 @@ def algorithmic_work(c: dict) -> dict:
     R = 0 if c["compressor"] == "none" else nc * m_blk
     return {
         "residual_flops": pairs * (2 * d + 2 * dv + 2),
+        # phi_k^T [V, 1] over the keys of completed blocks plus phi_q . [S, s] for
+        # every query: 2 F (dv + 1) flops each.  (The intra-block product of a
+        # chunked scan, bs (F + dv + 1) per token, is not done here: the current
+        # block is exact and belongs to the residual kernel.)
         "moment_flops": 2 * F * (dv + 1) * n + 2 * F * (dv + 1) * nc * bs,
         "compress_bytes": (nc * bs * d * 4 + R * (d + dv) * 4 + R * (d + dv + 2) * 4
                            + nc * (d + bs // 2) * 4) if R else 0,
@@ -150,6 +154,45 @@ class ClockSampler:
         reasons = sorted({names[j] for r in rows for j in range(4) if r[6 + j].strip().lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(rows)}
+
+
+def tf32_gemm_peak_tflops(dev: torch.device) -> float:
+    """Dense TF32 tensor-core throughput of this GPU, measured as a cuBLAS TF32
+    GEMM (8192^3, best of 5): the denominator of the tensor-core kernels."""
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        n = 8192
+        a = torch.randn(n, n, device=dev)
+        b = torch.randn(n, n, device=dev)
+        c = a @ b
+        best = float("inf")
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.mm(a, b, out=c)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            best = min(best, e0.elapsed_time(e1) / 1e3)
+        del a, b, c
+        return 2.0 * n ** 3 / best / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old
+
+
+def profiled_traffic(cfg_id: int) -> dict:
+    """DRAM bytes per launch of each kernel, from the ncu summary committed for
+    this workload (profiles/traffic_config<N>.txt: `kernel bytes` lines)."""
+    path = os.path.join(ROOT, "profiles", f"traffic_config{cfg_id}.txt")
+    out = {}
+    try:
+        for line in open(path):
+            parts = line.split()
+            if len(parts) >= 2 and not line.startswith("#"):
+                out[parts[0]] = float(parts[1])
+    except OSError:
+        pass
+    return out
 
 
 def measured_peaks() -> dict:
@@ -366,14 +409,15 @@ def run_ours(args, rank, world, dev):
         grid = (c["B"], c["H"], c["N"])
 
         def e2e_step():
-            dq, dk, dvv = (x.to(dev, non_blocking=True) for x in (hq, hk, hv))
+            # the public entry point takes the pinned host tensors as they are and
+            # returns the output on the host (chunked, copies overlapping kernels)
             if per == bh_total:
-                o = sa.fast_article_causal_attention(dq.view(*grid, c["d"]), dk.view(*grid, c["d"]),
-                                                     dvv.view(*grid, c["dv"]), **kw)
+                o = sa.fast_article_causal_attention(hq.view(*grid, c["d"]), hk.view(*grid, c["d"]),
+                                                     hv.view(*grid, c["dv"]), **kw)
             else:
-                o = sa.fast.fast_article_causal_attention_shard(dq, dk, dvv, head_range=(h0, h1), batch=c["B"],
+                o = sa.fast.fast_article_causal_attention_shard(hq, hk, hv, head_range=(h0, h1), batch=c["B"],
                                                                 heads=c["H"], **kw)
-            hout.view(o.shape).copy_(o, non_blocking=True)
+            assert o.device.type == "cpu" and o.shape[-1] == c["dv"]
 
         for _ in range(max(1, args.warmup)):
             e2e_step()
@@ -401,25 +445,38 @@ def run_ours(args, rank, world, dev):
         except Exception as exc:  # the probe is a measurement aid only
             print(f"fp32 probe failed: {exc!r}", file=sys.stderr)
             fma_peak = float("nan")
-        if dominant == "compress":
-            achieved = work["compress_bytes"] * per / (avg["compress"] / 1e3) / 1e9
-            roof = {"bound": "hbm", "achieved": achieved, "peak": peaks.get("hbm_gbs", 6650.0), "unit": "GB/s"}
-        else:
-            flops = work["residual_flops" if dominant == "residual" else "moment_flops"] * per
-            achieved = flops / (avg[dominant] / 1e3) / 1e12
-            roof = {"bound": "fp32", "achieved": achieved, "peak": fma_peak, "unit": "TFLOP/s"}
-        roof["frac"] = roof["achieved"] / roof["peak"] if roof["peak"] else None
-        roof["kernel"] = dominant
-        roof["traffic"] = None
-        roof["peak_source"] = ("measured FP32 FMA pipe (NVRTC probe in bench.py)" if roof["bound"] == "fp32"
-                               else "MEASURED_PEAKS.json hbm_gbs")
+        tf32_peak = tf32_gemm_peak_tflops(dev)
+        hbm_peak = peaks.get("hbm_gbs", 6650.0)
+        # full-size bytes per launch at one GPU; a rank's launch covers per / bh_total of it
+        traffic = {k_: v_ * per / bh_total for k_, v_ in profiled_traffic(args.config).items()} if not args.bh else {}
+        # The contractions of both tensor-core kernels run on the TF32 tensor pipe
+        # with a 3xTF32 split (hi*hi + hi*lo + lo*hi per fp32 product), so their
+        # ceiling for fp32-accurate work is a third of the TF32 rate; both
+        # fractions are given.
         kernels = {}
         for name, t_ in avg.items():
             kernels[name] = {"ms": t_, "share": t_ / sum(avg.values())}
-        kernels["residual"]["tflops"] = work["residual_flops"] * per / (avg["residual"] / 1e3) / 1e12
-        kernels["moments"]["tflops"] = work["moment_flops"] * per / (avg["moments"] / 1e3) / 1e12
+        for name, key in (("moments", "moment_flops"), ("residual", "residual_flops")):
+            tfl = work[key] * per / (avg[name] / 1e3) / 1e12
+            kernels[name].update({"tflops": tfl, "frac_tf32": tfl / tf32_peak,
+                                  "frac_3xtf32": 3.0 * tfl / tf32_peak})
+        kernels["residual"]["frac_fp32_fma"] = kernels["residual"]["tflops"] / fma_peak
         if "compress" in avg and avg["compress"] > 0:
             kernels["compress"]["gbs"] = work["compress_bytes"] * per / (avg["compress"] / 1e3) / 1e9
+            kernels["compress"]["frac_hbm"] = kernels["compress"]["gbs"] / hbm_peak
+        if dominant == "compress":
+            roof = {"bound": "hbm", "achieved": kernels["compress"]["gbs"], "peak": hbm_peak, "unit": "GB/s",
+                    "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured copy)"}
+        else:
+            roof = {"bound": "tensor", "achieved": kernels[dominant]["tflops"], "peak": tf32_peak, "unit": "TFLOP/s",
+                    "peak_source": "measured cuBLAS TF32 GEMM (8192^3) in this run; bf16 of measured "
+                                   f"{peaks.get('bf16_tflops')} TFLOP/s for context",
+                    "frac_3xtf32": kernels[dominant]["frac_3xtf32"]}
+        roof["frac"] = roof["achieved"] / roof["peak"] if roof["peak"] else None
+        roof["kernel"] = dominant
+        roof["traffic"] = traffic.get(dominant)
+        roof["algorithmic_per_launch"] = (work["compress_bytes"] if dominant == "compress"
+                                          else work["moment_flops" if dominant == "moments" else "residual_flops"]) * per
         value = bh_total * c["N"] * args.steps / (ms_max / 1e3)
         out = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -431,7 +488,7 @@ def run_ours(args, rank, world, dev):
                        "l2": "inputs larger than L2 (no flush needed)"},
             "roofline": roof, "kernels": kernels,
             "e2e": e2e, "gpu_launches": st.launches * args.steps,
-            "clocks": clk.summary(), "fp32_fma_peak_tflops": fma_peak,
+            "clocks": clk.summary(), "fp32_fma_peak_tflops": fma_peak, "tf32_gemm_peak_tflops": tf32_peak,
         }
     return out, c
 

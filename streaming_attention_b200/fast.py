@@ -5,8 +5,11 @@ same names, keyword arguments, argument checks and messages, return types and
 ``FastArticleStats`` fields.  All arithmetic runs in the sm_100a kernels of
 libsa_b200.so (compressor, block-granular moment scan, residual + combine);
 this module only validates, lays tensors out contiguously, builds the
-compressor's draw tables and calls the C ABI.  There is no CPU path: CPU
-tensors are rejected, and a missing library raises.
+compressor's draw tables and calls the C ABI.  There is no CPU compute path:
+CUDA tensors run in place; host (CPU) tensors, as the reference takes them,
+are streamed through the GPU in chunks with the copies overlapping the
+kernels, and the result comes back on the host; without a CUDA device, or
+without the library, the call raises.
 """
 
 from __future__ import annotations
@@ -218,6 +221,86 @@ def _run(q3: Tensor, k3: Tensor, v3: Tensor, *, batch: int, heads: int, degree: 
 
 _CHECK_STATUS = os.environ.get("SA_CHECK_STATUS", "0") == "1"
 
+# bytes of q, k, v moved per chunk of the host path (about 4 chunks at config 3)
+_HOST_CHUNK_BYTES = int(os.environ.get("SA_HOST_CHUNK_BYTES", str(384 << 20)))
+
+
+def _run_host(q3: Tensor, k3: Tensor, v3: Tensor, *, batch: int, heads: int, degree: int, block_size: int,
+              scale: float, compressor: str, seed: int, eps: float, head_range: Optional[Tuple[int, int]] = None,
+              device: Optional[torch.device] = None) -> Tensor:
+    """Forward of host-resident sequences (contiguous float32 [bh, n, *] CPU
+    tensors) on the GPU.  The sequences go through in chunks: chunk i's
+    host->device copy, its kernels and its device->host copy run on three
+    streams, so the copies of one chunk overlap the kernels of its neighbours;
+    chunks alternate between two compute streams (each with its own device
+    slot), which lets one chunk's last wave of CTAs share the GPU with the
+    next chunk's first.  Pinned inputs give asynchronous copies; the output is
+    a pinned CPU tensor."""
+    bh, n, d = q3.shape
+    dv = v3.shape[-1]
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    out = torch.empty(bh, n, dv, dtype=torch.float32, pin_memory=True)
+    if bh == 0 or n == 0:
+        return out
+    g0 = head_range[0] if head_range is not None else 0
+    per_seq = n * (2 * d + dv) * 4
+    chunk = max(1, min(bh, _HOST_CHUNK_BYTES // max(per_seq, 1)))
+    bounds = [(s0, min(s0 + chunk, bh)) for s0 in range(0, bh, chunk)]
+    with torch.cuda.device(dev):
+        main = torch.cuda.current_stream(dev)
+        h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        comp = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+        for s_ in (h2d, d2h, *comp):
+            s_.wait_stream(main)
+        nslot = min(2, len(bounds))
+        dq = [torch.empty(chunk, n, d, device=dev) for _ in range(nslot)]
+        dk = [torch.empty(chunk, n, d, device=dev) for _ in range(nslot)]
+        dvv = [torch.empty(chunk, n, dv, device=dev) for _ in range(nslot)]
+        dout = [torch.empty(chunk, n, dv, device=dev) for _ in range(nslot)]
+        in_ready = [torch.cuda.Event() for _ in range(nslot)]
+        computed = [torch.cuda.Event() for _ in range(nslot)]
+        copied_out = [torch.cuda.Event() for _ in range(nslot)]
+        for i, (s0, s1) in enumerate(bounds):
+            slot, cnt = i % nslot, s1 - s0
+            if i >= nslot:   # the slot's inputs are free once chunk i - 2's kernels are done
+                h2d.wait_event(computed[slot])
+            with torch.cuda.stream(h2d):
+                dq[slot][:cnt].copy_(q3[s0:s1], non_blocking=True)
+                dk[slot][:cnt].copy_(k3[s0:s1], non_blocking=True)
+                dvv[slot][:cnt].copy_(v3[s0:s1], non_blocking=True)
+                in_ready[slot].record(h2d)
+            cs = comp[slot]
+            cs.wait_event(in_ready[slot])
+            if i >= nslot:   # and its output once chunk i - 2 has been copied back
+                cs.wait_event(copied_out[slot])
+            with torch.cuda.stream(cs):
+                _run(dq[slot][:cnt], dk[slot][:cnt], dvv[slot][:cnt], batch=batch, heads=heads, degree=degree,
+                     block_size=block_size, scale=scale, compressor=compressor, seed=seed, eps=eps,
+                     head_range=(g0 + s0, g0 + s1), out=dout[slot][:cnt])
+                computed[slot].record(cs)
+            d2h.wait_event(computed[slot])
+            with torch.cuda.stream(d2h):
+                out[s0:s1].copy_(dout[slot][:cnt], non_blocking=True)
+                copied_out[slot].record(d2h)
+        d2h.synchronize()
+        for s_ in (h2d, *comp):
+            s_.synchronize()
+    return out
+
+
+def _host_inputs(*ts: Tensor) -> bool:
+    """True when q, k, v all live on the host (the kernels still run on the
+    GPU: without a CUDA device this raises)."""
+    if not all(t.device.type == "cpu" for t in ts):
+        return False
+    if not torch.cuda.is_available():
+        raise ValueError("the B200 kernels need a CUDA device; none is available")
+    for t in ts:
+        if t.dtype == torch.float64 or not t.dtype.is_floating_point:
+            raise ValueError(f"unsupported dtype {t.dtype}: the kernels compute in float32 "
+                             "(float32, float16 and bfloat16 inputs are accepted)")
+    return True
+
 
 def check_device_status(workspace: Tensor) -> None:
     """Read the launch status word (the first 4 bytes of the workspace): the
@@ -244,10 +327,14 @@ def fast_article_causal_attention_single(
     _check_single(q, k, v, query_chunk_size, block_size)
     n, dim = q.shape
     _check_modes(n, block_size, degree, compressor, low_mode)
-    _check_device(q, k, v)
     s = _attention_scale(scale, dim)
-    out, _ = _run(_as_f32(q)[None], _as_f32(k)[None], _as_f32(v)[None], batch=1, heads=1, degree=degree,
-                  block_size=block_size, scale=s, compressor=compressor, seed=seed, eps=denominator_eps)
+    kw = dict(batch=1, heads=1, degree=degree, block_size=block_size, scale=s, compressor=compressor, seed=seed,
+              eps=denominator_eps)
+    if _host_inputs(q, k, v):
+        out = _run_host(_as_f32(q)[None], _as_f32(k)[None], _as_f32(v)[None], **kw)
+    else:
+        _check_device(q, k, v)
+        out, _ = _run(_as_f32(q)[None], _as_f32(k)[None], _as_f32(v)[None], **kw)
     out = out[0].to(q.dtype)
     if not return_stats:
         return out
@@ -286,12 +373,17 @@ def fast_article_causal_attention(
         if block_size <= 0:
             raise ValueError("block_size must be positive")
         _check_modes(n, block_size, degree, compressor, low_mode)
-    _check_device(q, k, v)
     bh = bsz * heads
     s = _attention_scale(scale, dim)
-    out3, _ = _run(_as_f32(q).reshape(bh, n, dim), _as_f32(k).reshape(bh, n, dim), _as_f32(v).reshape(bh, n, dv),
-                   batch=bsz, heads=heads, degree=degree, block_size=block_size, scale=s, compressor=compressor,
-                   seed=seed, eps=denominator_eps)
+    args3 = (_as_f32(q).reshape(bh, n, dim), _as_f32(k).reshape(bh, n, dim), _as_f32(v).reshape(bh, n, dv))
+    kw = dict(batch=bsz, heads=heads, degree=degree, block_size=block_size, scale=s, compressor=compressor,
+              seed=seed, eps=denominator_eps)
+    if _host_inputs(q, k, v):
+        # host tensors: streamed through the GPU in chunks, copies overlapping the kernels
+        out3 = _run_host(*args3, **kw)
+    else:
+        _check_device(q, k, v)
+        out3, _ = _run(*args3, **kw)
     out = out3.reshape(bsz, heads, n, dv).to(q.dtype)
     if not return_stats:
         return out
@@ -324,11 +416,15 @@ def fast_article_causal_attention_shard(
     if block_size <= 0:
         raise ValueError("block_size must be positive")
     _check_modes(n, block_size, degree, compressor, "auto")
-    _check_device(q, k, v)
     s = _attention_scale(scale, dim)
-    out3, _ = _run(_as_f32(q).reshape(cnt, n, dim), _as_f32(k).reshape(cnt, n, dim), _as_f32(v).reshape(cnt, n, dv),
-                   batch=batch, heads=heads, degree=degree, block_size=block_size, scale=s, compressor=compressor,
-                   seed=seed, eps=denominator_eps, head_range=head_range)
+    args3 = (_as_f32(q).reshape(cnt, n, dim), _as_f32(k).reshape(cnt, n, dim), _as_f32(v).reshape(cnt, n, dv))
+    kw = dict(batch=batch, heads=heads, degree=degree, block_size=block_size, scale=s, compressor=compressor,
+              seed=seed, eps=denominator_eps, head_range=head_range)
+    if _host_inputs(q, k, v):
+        out3 = _run_host(*args3, **kw)
+    else:
+        _check_device(q, k, v)
+        out3, _ = _run(*args3, **kw)
     return out3.reshape(q.shape[:-1] + (dv,)).to(q.dtype)
 
 

@@ -109,6 +109,25 @@ def test_deterministic(dev):
     assert torch.equal(a, b)
 
 
+def test_host_tensors_stream_through_the_gpu(dev, monkeypatch):
+    """CPU inputs (as the reference takes them) run on the GPU in chunks and come
+    back on the host; every sequence is computed exactly as in one device call."""
+    c = workloads.config(3, B=2, H=3, N=700)
+    q, k, v = workloads.make_inputs(c, seed=5)
+    kw = dict(degree=2, block_size=128, compressor="sorted_pair", seed=7)
+    ref = sa.fast_article_causal_attention(q.to(dev), k.to(dev), v.to(dev), **kw).cpu()
+    # small chunks: 6 sequences in 4 chunks over both device slots
+    monkeypatch.setattr(fast, "_HOST_CHUNK_BYTES", 700 * (2 * 64 + 64) * 4 * 2 - 1)
+    out = sa.fast_article_causal_attention(q.pin_memory(), k.pin_memory(), v.pin_memory(), **kw)
+    assert out.device.type == "cpu"
+    assert torch.equal(out, ref)
+    out2 = sa.fast_article_causal_attention(q, k, v, **kw)   # pageable inputs
+    assert torch.equal(out2, ref)
+    one = sa.fast_article_causal_attention(q[1, 2], k[1, 2], v[1, 2], seed=12)
+    assert torch.equal(one, sa.fast_article_causal_attention(q[1, 2].to(dev), k[1, 2].to(dev), v[1, 2].to(dev),
+                                                             seed=12).cpu())
+
+
 def test_stats_and_two_dim_entry(dev):
     g = load_golden("reftest_shapes_sorted_pair")
     q, k, v = (torch.from_numpy(g[x][0, 0]).to(dev) for x in "qkv")
