@@ -131,6 +131,43 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
                       float* out, int32_t* rep_idx, void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/* ---- streaming (decode) state: ArticleStreamingAttention -------------------
+ * The reference keeps, per attention stream, a Taylor moment sketch and a
+ * merge-and-reduce coreset (streaming_taylor_coreset_attention.py:229-616).
+ * Here that state lives in caller-owned device buffers: num [F, dv] and den [F]
+ * (fp32, F = sa_feature_count(d, degree)), a pending block of raw keys /
+ * values, and the level items (keys [m, d], values [m, dv], weights [m]).
+ * The caller keeps the level structure and draws the compressor's random
+ * numbers (as the streaming class in streaming_attention_b200/streaming.py does). */
+
+/* Replaces TaylorMomentSketch.update (streaming_taylor_coreset_attention.py:262-279):
+ * num[f, :] += (weight * phi_k(key)[f]) * value, den[f] += weight * phi_k(key)[f],
+ * product then add, each rounded to fp32, as the reference does. */
+int sa_stream_update(const float* key, const float* value, int d, int dv, int degree, float weight,
+                     float* num_state, float* den_state, void* stream);
+
+/* Replaces MergeReduceCoreset._compress (streaming_taylor_coreset_attention.py:414-470)
+ * for one block of n >= 2 weighted items: sorted_pair (direction [d], coins
+ * [n/2]; n <= 2 uses perm) or random (perm [ceil(n/2)] of the first draws of
+ * randperm(n)).  Writes ceil(n/2) items; outputs must not overlap inputs. */
+int sa_stream_compress(const float* keys, const float* values, const float* weights, int64_t n, int d,
+                       int dv, int compressor, const float* direction, const float* coins,
+                       const int32_t* perm, float* out_keys, float* out_values, float* out_weights,
+                       void* stream);
+
+/* Bytes of device workspace sa_stream_query needs. */
+int sa_stream_query_workspace_size(int d, int dv, int degree, size_t* bytes);
+
+/* Replaces ArticleStreamingAttention.query (streaming_taylor_coreset_attention.py:572-606):
+ * out [dv] = (phi_q(scale q).[num, den] + sum over the pending block (weight 1)
+ * and the level items of w (exp(x) - P_t(x)) [v, 1]) / max(den, eps), with
+ * x = scale * (k . q).  dens (nullable) receives {den, low den, tail den}. */
+int sa_stream_query(const float* query, int d, int dv, int degree, float scale, const float* num_state,
+                    const float* den_state, const float* buf_keys, const float* buf_values, int64_t n_buf,
+                    const float* lvl_keys, const float* lvl_values, const float* lvl_weights,
+                    int64_t n_lvl, float eps, float* out, float* dens, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
 /* Bytes of the library's built-in device scratch (per GPU). */
 #define SA_STATIC_SCRATCH_BYTES (64u * 1024u * 1024u)
 

@@ -3,7 +3,9 @@
 Drop-in for the fast path of PositiveLoss/streaming-attention
 (``fast_article_attention.py``): the same entry points and arguments, computed
 by hand-written CUDA kernels in ``libsa_b200.so`` through a C ABI
-(``include/streaming_attention.h``).  There is no CPU fallback.
+(``include/streaming_attention.h``), plus the streaming (decode) class
+``ArticleStreamingAttention`` of ``streaming_taylor_coreset_attention.py``.
+There is no CPU compute path.
 """
 
 from .fast import (  # noqa: F401
@@ -17,5 +19,7 @@ from .fast import (  # noqa: F401
     num_taylor_features,
     safe_relative_l2,
 )
+
+from .streaming import ArticleStreamingAttention, AttentionQueryStats  # noqa: F401
 
 __version__ = "0.1.0"

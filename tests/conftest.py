@@ -34,3 +34,8 @@ def load_golden(name):
 def golden_names():
     return sorted(f[:-4] for f in os.listdir(GOLDEN)
                   if f.endswith(".npz") and f not in ("misc.npz",) and not f.startswith("stream_"))
+
+
+def stream_golden_names():
+    """Fixtures of the streaming class (one update + query per token)."""
+    return sorted(f[:-4] for f in os.listdir(GOLDEN) if f.startswith("stream_") and f.endswith(".npz"))

@@ -287,7 +287,9 @@ def make_streaming(fa, st):
     out = {}
     for name, comp, n, d, dv, bs, t in [("stream_sorted_pair", "sorted_pair", 100, 4, 3, 8, 2),
                                         ("stream_random", "random", 90, 5, 4, 6, 2),
-                                        ("stream_deg3", "sorted_pair", 70, 3, 2, 4, 3)]:
+                                        ("stream_deg3", "sorted_pair", 70, 3, 2, 4, 3),
+                                        ("stream_odd_block", "sorted_pair", 75, 6, 5, 5, 2),
+                                        ("stream_none", "none", 40, 4, 3, 8, 1)]:
         g = torch.Generator().manual_seed(42)
         q = torch.randn(n, d, generator=g) * 0.5
         k = torch.randn(n, d, generator=g) * 0.5
@@ -302,9 +304,12 @@ def make_streaming(fa, st):
             items.append(s.coreset_items)
             sbytes.append(s.state_bytes)
             dens.append(s.denominator)
+        final = att.coreset.items()   # pending buffer, then levels 0, 1, ...
         out[name] = dict(q=q.numpy(), k=k.numpy(), v=v.numpy(), out=np.stack(outs),
                          items=np.asarray(items), state_bytes=np.asarray(sbytes),
-                         den=np.asarray(dens, np.float64),
+                         den=np.asarray(dens, np.float64), final_keys=final.keys.numpy(),
+                         final_values=final.values.numpy(), final_weights=final.weights.numpy(),
+                         compressions=np.asarray(att.coreset.num_compressions),
                          meta=np.frombuffer(json.dumps(dict(compressor=comp, n=n, d=d, dv=dv, bs=bs,
                                                             degree=t, seed=17)).encode(), dtype=np.uint8))
         np.savez_compressed(os.path.join(HERE, name + ".npz"), **out[name])
@@ -314,9 +319,14 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
     ap.add_argument("--only", default=None)
+    ap.add_argument("--streaming-only", action="store_true")
     args = ap.parse_args()
     torch.set_num_threads(1)
     fa, st = _load_reference(args.reference)
+    if args.streaming_only:
+        make_streaming(fa, st)
+        print("wrote streaming")
+        return
     for c in CASES:
         if args.only and c["name"] != args.only:
             continue

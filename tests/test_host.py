@@ -90,3 +90,21 @@ def test_argument_errors_match_reference_messages():
     # CPU tensors: no CPU fallback
     with pytest.raises(ValueError, match="CUDA"):
         f(q, q, q)
+
+
+def test_streaming_class_checks_arguments_like_the_reference():
+    """ArticleStreamingAttention's constructor errors (streaming_taylor_coreset_attention.py:
+    :137-161 feature map, :359-360 coreset), raised before any device work."""
+    from streaming_attention_b200 import ArticleStreamingAttention
+    with pytest.raises(ValueError, match="dim must be positive"):
+        ArticleStreamingAttention(0, 4)
+    with pytest.raises(ValueError, match="degree must be non-negative"):
+        ArticleStreamingAttention(4, 4, degree=-1)
+    with pytest.raises(ValueError, match="exceeding max_monomials=10"):
+        ArticleStreamingAttention(8, 4, degree=2, max_monomials=10)
+    with pytest.raises(ValueError, match="block_size must be at least 2"):
+        ArticleStreamingAttention(4, 4, block_size=1)
+    with pytest.raises(ValueError, match="Unsupported dtype"):
+        ArticleStreamingAttention(4, 4, dtype="int8")
+    with pytest.raises(NotImplementedError):
+        ArticleStreamingAttention(4, 4, degree=4)

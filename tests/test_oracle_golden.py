@@ -10,7 +10,7 @@ import json
 import numpy as np
 import pytest
 
-from conftest import golden_names, load_golden
+from conftest import golden_names, load_golden, stream_golden_names
 from oracle import oracle as O
 
 
@@ -108,3 +108,25 @@ def test_low_terms_before_block_plus_block_exp_is_the_output():
     p = np.where(cur, O.exp_taylor(x, 2), 0)
     np.testing.assert_allclose(ln + p @ v, full_ln, rtol=1e-9, atol=1e-9)
     np.testing.assert_allclose(ld + p.sum(-1), full_ld, rtol=1e-12)
+
+
+@pytest.mark.parametrize("name", stream_golden_names())
+def test_streaming_oracle_matches_reference_fixture(name):
+    """ArticleStreamingAttention restated: per-token outputs, coreset sizes, the
+    final merge-and-reduce items (bit-exact) and the number of compressions."""
+    g = load_golden(name)
+    m = g["meta"]
+    out, ld, td, items, final, comps = O.stream_attention(
+        g["q"], g["k"], g["v"], degree=m["degree"], block_size=m["bs"], compressor=m["compressor"], seed=m["seed"])
+    assert O.relative_l2(out, g["out"]) < 1e-5
+    np.testing.assert_array_equal(items, g["items"])
+    np.testing.assert_array_equal(final.keys, g["final_keys"])
+    np.testing.assert_array_equal(final.values, g["final_values"])
+    np.testing.assert_array_equal(final.weights, g["final_weights"])
+    assert comps == int(g["compressions"])
+    np.testing.assert_allclose(ld + td, g["den"], rtol=1e-5)
+
+
+def test_streaming_oracle_rejects_small_blocks():
+    with pytest.raises(ValueError, match="block_size must be at least 2"):
+        O.stream_attention(np.zeros((3, 2)), np.zeros((3, 2)), np.zeros((3, 1)), block_size=1)
