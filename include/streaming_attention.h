@@ -168,6 +168,44 @@ int sa_stream_query(const float* query, int d, int dv, int degree, float scale, 
                     int64_t n_lvl, float eps, float* out, float* dens, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* ---- one shard of a long sequence split along N over GPUs ------------------
+ * The reference has no multi-GPU path; these split one forward of
+ * fast_article_causal_attention (fast_article_attention.py:634-719) over P
+ * ranks that each hold a contiguous token range of every sequence (a whole
+ * number of blocks).  Rank r: sa_shard_begin (local compression with the
+ * global block ids, local moment scan, its moment state T_r), then the caller
+ * all-gathers the states and reps, then sa_shard_end (exclusive prefix of the
+ * earlier states, their contribution to the shard's queries, the residual
+ * over the reps of every earlier block).  Needs the tensor-core kernels. */
+
+/* Floats of one shard's moment state (the unit of the all-gather). */
+int sa_shard_state_floats(int64_t bh, int d, int dv, int degree, int64_t* floats);
+
+/* Bytes of workspace for both calls of a shard of n tokens whose residual reads
+ * rep_rows reps per sequence (the reps of the blocks before the shard's last). */
+int sa_shard_workspace_size(int64_t bh, int64_t n, int d, int dv, int degree, int block_size,
+                            int64_t rep_rows, size_t* bytes);
+
+/* Local part.  dirs/coins/perms hold the draws of the shard's n_compress
+ * blocks (global blocks c_off .. c_off+n_compress-1 of the sequence);
+ * rep_k/rep_v/rep_w [bh, n_compress*m, *] receive the raw reps, rep_idx
+ * (nullable) their global token indices; state_out receives T_r. */
+int sa_shard_begin(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d, int dv,
+                   int degree, int block_size, float scale, int compressor, const float* dirs,
+                   const float* coins, const int32_t* perms, int64_t n_compress, int64_t c_off,
+                   float* state_out, float* rep_k, float* rep_v, float* rep_w, int32_t* rep_idx,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Global part, after the exchange.  states_before: the n_before states of the
+ * earlier shards, contiguous in shard order; rep_k/rep_v/rep_w [bh, rep_rows,
+ * *]: the reps of global blocks 0.. in order (for compressor none: every
+ * earlier token, weight 1).  Same workspace as sa_shard_begin. */
+int sa_shard_end(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d, int dv,
+                 int degree, int block_size, float scale, int compressor, float eps,
+                 const float* states_before, int n_before, int64_t c_off, const float* rep_k,
+                 const float* rep_v, const float* rep_w, int64_t rep_rows, float* out, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
 /* Bytes of the library's built-in device scratch (per GPU). */
 #define SA_STATIC_SCRATCH_BYTES (64u * 1024u * 1024u)
 

@@ -45,6 +45,12 @@ SIGNATURES = {
                           _vp, _vp, _sz, _vp],
     "sa_fast_attention_static_scratch": [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _vp,
                                          _vp, _f32, _vp, _vp, _vp],
+    "sa_shard_state_floats": [_i64, _i32, _i32, _i32, ctypes.POINTER(_i64)],
+    "sa_shard_workspace_size": [_i64, _i64, _i32, _i32, _i32, _i32, _i64, ctypes.POINTER(_sz)],
+    "sa_shard_begin": [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _vp, _vp, _i64, _i64,
+                       _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp],
+    "sa_shard_end": [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _f32, _i32, _f32, _vp, _i32, _i64, _vp, _vp,
+                     _vp, _i64, _vp, _vp, _sz, _vp],
     "sa_stream_update": [_vp, _vp, _i32, _i32, _i32, _f32, _vp, _vp, _vp],
     "sa_stream_compress": [_vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "sa_stream_query_workspace_size": [_i32, _i32, _i32, ctypes.POINTER(_sz)],

@@ -24,7 +24,8 @@ namespace sa {
 
 int launch_compress(const float* k, const float* v, int64_t bh, int64_t n, int d, int dv, int bs, int compressor,
                     const float* dirs, const float* coins, const int32_t* perms, int32_t* rep_idx, float* rep_k,
-                    float* rep_v, float* rep_w, SplitOut sp, cudaStream_t stream);
+                    float* rep_v, float* rep_w, SplitOut sp, cudaStream_t stream,
+                    int64_t nc_force = -1, int64_t idx_offset = 0);
 int launch_split(const float* src, int64_t rows, int cols, int cols_pad, float* hi, float* lo, cudaStream_t stream);
 int launch_split_t(const float* src, int64_t bh, int64_t rows, int cols, int cols_pad, int64_t rows_pad, float* hi,
                    float* lo, cudaStream_t stream);
@@ -32,13 +33,16 @@ int residual_tc_dp(int d);
 int residual_tc_dvp(int dv);
 int launch_residual_tc(const CUtensorMap* maps, const float* q, const float* rep_w, int64_t r_pad, const float* low,
                        int groups, float* out, int* status, int64_t bh, int64_t n, int d, int dv, int degree, int bs,
-                       int64_t m_blk, float scale, float eps, cudaStream_t stream);
+                       int64_t m_blk, float scale, float eps, cudaStream_t stream, int64_t c_off = 0);
 int moments_tc_groups(int d, int dv, int degree);
 int64_t moments_tc_master_floats(int64_t bh, int d, int dv, int degree);
 int launch_moments_tc(const CUtensorMap* maps, const float* q, const float* k, float* part, float* master,
                       int* status, int64_t bh, int64_t n, int d, int dv, int degree, int bs, float scale,
-                      cudaStream_t stream);
+                      cudaStream_t stream, int mode = 0, float* den_io = nullptr);
 int launch_sum_groups(const float* part, int groups, int64_t stride, float* out, cudaStream_t stream);
+int64_t moments_tc_den_floats(int64_t bh, int d, int dv, int degree);
+int launch_state_prefix(const float* states, int nprev, int64_t n_master, int64_t n_den, float* master, float* den,
+                        cudaStream_t stream);
 int launch_low_moments(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d, int dv,
                        int degree, int bs, float scale, float* low, cudaStream_t stream);
 int launch_residual(const float* q, const float* k, const float* v, const float* rk, const float* rv,
@@ -107,6 +111,7 @@ struct Workspace {
   // (keys contiguous: the K-major layout of V for the tensor cores)
   size_t status = 0, low = 0, master = 0, khi = 0, klo = 0, vthi = 0, vtlo = 0;
   size_t rkhi = 0, rklo = 0, rvthi = 0, rvtlo = 0, rep_k = 0, rep_v = 0, rep_w = 0, rep_idx = 0, total = 0;
+  size_t den_io = 0;  // sharded forward: the feature sums of the moment state
 };
 
 enum class Plan { kFull, kResidualOnly, kMomentsOnly };
@@ -226,7 +231,7 @@ struct TCOperands {
 int residual_tc_from_split(const Workspace& w, const TCOperands& rep, const TCOperands& cur, const float* rep_w,
                            const float* q, const float* low, int groups, float* out, int* status, int64_t bh,
                            int64_t n, int d, int dv, int degree, int block_size, int compressor, float scale,
-                           float eps, cudaStream_t s) {
+                           float eps, cudaStream_t s, int64_t c_off = 0) {
   CUtensorMap maps[8];
   const TCOperands* ops[2] = {&rep, &cur};
   for (int j = 0; j < 2; ++j) {
@@ -239,21 +244,59 @@ int residual_tc_from_split(const Workspace& w, const TCOperands& rep, const TCOp
   }
   const int64_t m_blk = compressor == SA_COMPRESSOR_NONE ? block_size : (block_size + 1) / 2;
   return launch_residual_tc(maps, q, rep_w, w.r_pad, low, groups, out, status, bh, n, d, dv, degree, block_size,
-                            m_blk, scale, eps, s);
+                            m_blk, scale, eps, s, c_off);
 }
 
 // Tensor-core moments into `part` ([groups, bh, n, dv+1]) from the transposed
 // split v ([bh, dvp, n_pad]; K-major tiles of dvp value rows x 32 keys).
 int moments_tc_from_split(const Workspace& w, char* ws, const float* vthi, const float* vtlo, const float* q,
                           const float* k, float* part, int* status, int64_t bh, int64_t n, int d, int dv, int degree,
-                          int block_size, float scale, cudaStream_t s) {
+                          int block_size, float scale, cudaStream_t s, int mode = 0, float* den_io = nullptr) {
   CUtensorMap maps[2];
   int rc = encode_map(&maps[0], vthi, n, w.n_pad, w.dvp, bh, w.dvp, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = encode_map(&maps[1], vtlo, n, w.n_pad, w.dvp, bh, w.dvp, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   float* master = reinterpret_cast<float*>(ws + w.master);
-  return launch_moments_tc(maps, q, k, part, master, status, bh, n, d, dv, degree, block_size, scale, s);
+  return launch_moments_tc(maps, q, k, part, master, status, bh, n, d, dv, degree, block_size, scale, s, mode,
+                           den_io);
+}
+
+// Workspace of the sharded forward (one shard of a sequence split along N).
+// Buffers that do not depend on rep_rows come first, so begin (which does not
+// know rep_rows yet) and end see the same offsets.
+Workspace plan_shard(int64_t bh, int64_t n, int d, int dv, int degree, int bs, int64_t rep_rows) {
+  Workspace w{};
+  w.dp = residual_tc_dp(d);
+  w.dvp = residual_tc_dvp(dv);
+  w.tc = w.dp > 0 && w.dvp > 0 && bs % 4 == 0 && !force_simt();
+  w.groups = w.tc ? moments_tc_groups(d, dv, degree) : 0;
+  if (w.groups == 0) w.tc = false;
+  w.R = rep_rows;
+  w.r_pad = (rep_rows + 63) / 64 * 64;
+  w.n_pad = (n + 3) / 4 * 4;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align_up(off + bytes);
+    return at;
+  };
+  const size_t f = sizeof(float);
+  w.status = take(sizeof(int));
+  w.low = take((size_t)2 * (w.groups > 0 ? w.groups : 1) * bh * n * (dv + 1) * f);   // local + prefix slices
+  w.master = take((size_t)moments_tc_master_floats(bh, d, dv, degree) * f);
+  w.den_io = take((size_t)moments_tc_den_floats(bh, d, dv, degree) * f);
+  w.khi = take((size_t)bh * n * w.dp * f);
+  w.klo = take((size_t)bh * n * w.dp * f);
+  w.vthi = take((size_t)bh * w.dvp * w.n_pad * f);
+  w.vtlo = take((size_t)bh * w.dvp * w.n_pad * f);
+  w.rkhi = take((size_t)bh * w.R * w.dp * f);
+  w.rklo = take((size_t)bh * w.R * w.dp * f);
+  w.rvthi = take((size_t)bh * w.dvp * w.r_pad * f);
+  w.rvtlo = take((size_t)bh * w.dvp * w.r_pad * f);
+  w.rep_w = take((size_t)bh * w.r_pad * f);
+  w.total = off;
+  return w;
 }
 
 int check_workspace(const Workspace& w, const void* workspace, size_t workspace_bytes) {
@@ -518,6 +561,137 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
     if (rc) return rc;
   }
   return launch_residual(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, block_size, compressor, scale, eps, out, s);
+}
+
+
+/* ---- one shard of a sequence split along N (config 5 across GPUs) ---- */
+
+int sa_shard_state_floats(int64_t bh, int d, int dv, int degree, int64_t* floats) {
+  if (!floats) return set_error(SA_ERR_INVALID_ARG, "null output pointer");
+  int rc = check_common(nullptr, nullptr, nullptr, 0, 1, d, dv, degree, 4);
+  if (rc) return rc;
+  if (moments_tc_groups(d, dv, degree) <= 0)
+    return set_error(SA_ERR_UNSUPPORTED, "the sharded forward needs the tensor-core moment scan (dv <= 64)");
+  *floats = moments_tc_master_floats(bh, d, dv, degree) + moments_tc_den_floats(bh, d, dv, degree);
+  return SA_OK;
+}
+
+int sa_shard_workspace_size(int64_t bh, int64_t n, int d, int dv, int degree, int block_size, int64_t rep_rows,
+                            size_t* bytes) {
+  if (!bytes) return set_error(SA_ERR_INVALID_ARG, "null output pointer");
+  int rc = check_common(nullptr, nullptr, nullptr, 0, n, d, dv, degree, block_size);
+  if (rc) return rc;
+  if (bh < 0 || rep_rows < 0) return set_error(SA_ERR_INVALID_ARG, "bh and rep_rows must be non-negative");
+  const Workspace w = plan_shard(bh, n, d, dv, degree, block_size, rep_rows);
+  if (!w.tc)
+    return set_error(SA_ERR_UNSUPPORTED,
+                     "the sharded forward needs the tensor-core kernels (d <= 64, dv <= 64, block_size % 4 == 0)");
+  *bytes = w.total;
+  return SA_OK;
+}
+
+int sa_shard_begin(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d, int dv, int degree,
+                   int block_size, float scale, int compressor, const float* dirs, const float* coins,
+                   const int32_t* perms, int64_t n_compress, int64_t c_off, float* state_out, float* rep_k,
+                   float* rep_v, float* rep_w, int32_t* rep_idx, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  int rc = check_common(q, k, v, bh, n, d, dv, degree, block_size);
+  if (!rc) rc = check_compressor(compressor);
+  if (rc) return rc;
+  if (bh == 0 || n == 0) return SA_OK;
+  if (!state_out) return set_error(SA_ERR_INVALID_ARG, "null state pointer");
+  if (n_compress < 0 || n_compress * (int64_t)block_size > n || c_off < 0)
+    return set_error(SA_ERR_INVALID_ARG, "n_compress blocks must lie in the shard and c_off be non-negative");
+  const bool compress = compressor != SA_COMPRESSOR_NONE && n_compress > 0;
+  if (compress && (!rep_k || !rep_v || !rep_w)) return set_error(SA_ERR_INVALID_ARG, "null rep pointer");
+  const Workspace w = plan_shard(bh, n, d, dv, degree, block_size, 0);
+  if (!w.tc)
+    return set_error(SA_ERR_UNSUPPORTED,
+                     "the sharded forward needs the tensor-core kernels (d <= 64, dv <= 64, block_size % 4 == 0)");
+  rc = check_workspace(w, workspace, workspace_bytes);
+  if (rc) return rc;
+  char* ws = static_cast<char*>(workspace);
+  cudaStream_t s = (cudaStream_t)stream;
+  int* status = reinterpret_cast<int*>(ws + w.status);
+  rc = reset_status(status, s);
+  float* khi = reinterpret_cast<float*>(ws + w.khi);
+  float* klo = reinterpret_cast<float*>(ws + w.klo);
+  float* vthi = reinterpret_cast<float*>(ws + w.vthi);
+  float* vtlo = reinterpret_cast<float*>(ws + w.vtlo);
+  if (!rc) rc = launch_split(k, bh * n, d, w.dp, khi, klo, s);
+  if (!rc) rc = launch_split_t(v, bh, n, dv, w.dvp, w.n_pad, vthi, vtlo, s);
+  if (!rc && compress)
+    rc = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, rep_idx, rep_k, rep_v, rep_w,
+                         SplitOut{}, s, n_compress, c_off * (int64_t)block_size);
+  float* master = reinterpret_cast<float*>(ws + w.master);
+  float* den_io = reinterpret_cast<float*>(ws + w.den_io);
+  if (!rc)
+    rc = moments_tc_from_split(w, ws, vthi, vtlo, q, k, reinterpret_cast<float*>(ws + w.low), status, bh, n, d, dv,
+                               degree, block_size, scale, s, 1, den_io);
+  if (rc) return rc;
+  const int64_t nm = moments_tc_master_floats(bh, d, dv, degree), nd = moments_tc_den_floats(bh, d, dv, degree);
+  cudaError_t ce = cudaMemcpyAsync(state_out, master, (size_t)nm * sizeof(float), cudaMemcpyDeviceToDevice, s);
+  if (ce == cudaSuccess)
+    ce = cudaMemcpyAsync(state_out + nm, den_io, (size_t)nd * sizeof(float), cudaMemcpyDeviceToDevice, s);
+  if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "state copy: %s", cudaGetErrorString(ce));
+  return SA_OK;
+}
+
+int sa_shard_end(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d, int dv, int degree,
+                 int block_size, float scale, int compressor, float eps, const float* states_before, int n_before,
+                 int64_t c_off, const float* rep_k, const float* rep_v, const float* rep_w, int64_t rep_rows,
+                 float* out, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_common(q, k, v, bh, n, d, dv, degree, block_size);
+  if (!rc) rc = check_compressor(compressor);
+  if (rc) return rc;
+  if (bh == 0 || n == 0) return SA_OK;
+  if (!out) return set_error(SA_ERR_INVALID_ARG, "null output pointer");
+  if (n_before < 0 || (n_before > 0 && !states_before)) return set_error(SA_ERR_INVALID_ARG, "bad earlier states");
+  if (rep_rows > 0 && (!rep_k || !rep_v || !rep_w)) return set_error(SA_ERR_INVALID_ARG, "null rep pointer");
+  const Workspace w = plan_shard(bh, n, d, dv, degree, block_size, rep_rows);
+  if (!w.tc)
+    return set_error(SA_ERR_UNSUPPORTED,
+                     "the sharded forward needs the tensor-core kernels (d <= 64, dv <= 64, block_size % 4 == 0)");
+  rc = check_workspace(w, workspace, workspace_bytes);
+  if (rc) return rc;
+  char* ws = static_cast<char*>(workspace);
+  cudaStream_t s = (cudaStream_t)stream;
+  int* status = reinterpret_cast<int*>(ws + w.status);
+  float* master = reinterpret_cast<float*>(ws + w.master);
+  float* den_io = reinterpret_cast<float*>(ws + w.den_io);
+  const int64_t nm = moments_tc_master_floats(bh, d, dv, degree), nd = moments_tc_den_floats(bh, d, dv, degree);
+  // the state of every earlier shard, then its contribution to this shard's
+  // queries (a second set of partial slices; none for the first shard)
+  float* low = reinterpret_cast<float*>(ws + w.low);
+  float* vthi = reinterpret_cast<float*>(ws + w.vthi);
+  float* vtlo = reinterpret_cast<float*>(ws + w.vtlo);
+  const int64_t slice = bh * n * (dv + 1);
+  if (n_before > 0) {
+    rc = launch_state_prefix(states_before, n_before, nm, nd, master, den_io, s);
+    if (!rc)
+      rc = moments_tc_from_split(w, ws, vthi, vtlo, q, k, low + (int64_t)w.groups * slice, status, bh, n, d, dv,
+                                 degree, block_size, scale, s, 2, den_io);
+    if (rc) return rc;
+  }
+  const int groups = n_before > 0 ? 2 * w.groups : w.groups;
+  float* r[4] = {reinterpret_cast<float*>(ws + w.rkhi), reinterpret_cast<float*>(ws + w.rklo),
+                 reinterpret_cast<float*>(ws + w.rvthi), reinterpret_cast<float*>(ws + w.rvtlo)};
+  float* wpad = reinterpret_cast<float*>(ws + w.rep_w);
+  if (rep_rows > 0) {
+    rc = launch_split(rep_k, bh * rep_rows, d, w.dp, r[0], r[1], s);
+    if (!rc) rc = launch_split_t(rep_v, bh, rep_rows, dv, w.dvp, w.r_pad, r[2], r[3], s);
+    if (rc) return rc;
+    cudaError_t ce = cudaMemsetAsync(wpad, 0, (size_t)bh * w.r_pad * sizeof(float), s);
+    if (ce == cudaSuccess)
+      ce = cudaMemcpy2DAsync(wpad, (size_t)w.r_pad * sizeof(float), rep_w, (size_t)rep_rows * sizeof(float),
+                             (size_t)rep_rows * sizeof(float), (size_t)bh, cudaMemcpyDeviceToDevice, s);
+    if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "rep weight copy: %s", cudaGetErrorString(ce));
+  }
+  const TCOperands cur_ops{reinterpret_cast<float*>(ws + w.khi), reinterpret_cast<float*>(ws + w.klo), n, vthi, vtlo,
+                           n, w.n_pad};
+  const TCOperands rep_ops{r[0], r[1], rep_rows, r[2], r[3], rep_rows, w.r_pad};
+  return residual_tc_from_split(w, rep_ops, cur_ops, rep_rows > 0 ? wpad : nullptr, q, low, groups, out,
+                                status, bh, n, d, dv, degree, block_size, compressor, scale, eps, s, c_off);
 }
 
 }  // extern "C"

@@ -72,6 +72,14 @@ struct MomTCParams {
   int64_t n, bh;
   int d, dv, bs, degree, nseg, G;
   float scale;
+  // 0: the scan (state from zero, queries of block c read the blocks before it);
+  // 1 (total): also update and fold the last block, so that `master` ends as the
+  //    state of every block and den_io [G, bh, FT*128] receives the feature sums;
+  // 2 (frozen): `master` and den_io hold a given state; every block's queries
+  //    read it and nothing is updated (the contribution of keys before the
+  //    sequence, e.g. earlier shards of a split sequence).
+  int mode;
+  float* den_io;
 };
 
 template <int DVP>
@@ -321,6 +329,9 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
   const int ntiles = min(FT, (p.nseg - seg0 + 15) / 16);
   const int64_t nb = (p.n + p.bs - 1) / p.bs;
   const int sub = (p.bs + kRows - 1) / kRows;          // 128-token sub-tiles of a full block
+  // which phases block c has (see MomTCParams::mode)
+  auto has_update = [&](int64_t c) { return p.mode != 2 && (c + 1 < nb || p.mode == 1); };
+  auto has_query = [&](int64_t c) { return c > 0 || p.mode == 2; };
 
   if (threadIdx.x == 0) {
     for (int b = 0; b < kNStg; ++b) {
@@ -345,7 +356,8 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     seg_of(seg0 + s, p.d, p.degree, p1, p2, c0);
     segtab[s] = (uint32_t)p1 | ((uint32_t)p2 << 10) | ((uint32_t)c0 << 20);
   }
-  for (int f = threadIdx.x; f < FT * kRows; f += kThreads) sden[f] = 0.0f;
+  for (int f = threadIdx.x; f < FT * kRows; f += kThreads)
+    sden[f] = p.mode == 2 ? p.den_io[((int64_t)g * p.bh + h) * (FT * kRows) + f] : 0.0f;
   if (threadIdx.x >= 64) tmaps[threadIdx.x - 64] = tile_map_entries(p.d, (threadIdx.x >> 5) - 2, threadIdx.x & 31);
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -364,7 +376,8 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     if (lane == 0) {
       int use = 0;
       bool ok = true;
-      for (int64_t c = 0; ok && c + 1 < nb; ++c) {
+      for (int64_t c = 0; ok && c < nb; ++c) {
+        if (!has_update(c)) continue;
         for (int st = 0; ok && st < sub; ++st) {
           const int64_t t0 = c * p.bs + (int64_t)st * kRows;
           for (int tc = 0; tc < kRows / kChunk; ++tc, ++use) {
@@ -397,7 +410,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
       int stg_use = 0, sb_use = 0, v_use = 0, sub_use = 0;
       bool ok = true;
       for (int64_t c = 0; ok && c < nb; ++c) {
-        if (c > 0) {
+        if (has_query(c)) {
           const int64_t b1 = min((c + 1) * (int64_t)p.bs, p.n);
           const int nsq = (int)((b1 - c * (int64_t)p.bs + kRows - 1) / kRows);  // query sub-tiles of block c
           for (int st = 0; ok && st < nsq; ++st, ++sub_use) {
@@ -431,7 +444,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
             if (ok && elect_one()) mma_commit(out_full);
           }
         }
-        if (ok && c + 1 < nb) {
+        if (ok && has_update(c)) {
           for (int st = 0; ok && st < sub; ++st) {
             for (int tc = 0; ok && tc < kRows / kChunk; ++tc, ++v_use) {
               const int vs = v_use & 1;
@@ -500,14 +513,16 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
       if (uq) {
         const int64_t ub0 = uc * p.bs, ub1 = min(ub0 + p.bs, p.n);
         if ((int64_t)(ust + 1) * kRows < ub1 - ub0) issue_tile(uc, true, ust + 1);
-        else if (uc + 1 < nb) issue_tile(uc, false, 0);
+        else if (has_update(uc)) issue_tile(uc, false, 0);
+        else if (uc + 1 < nb && has_query(uc + 1)) issue_tile(uc + 1, true, 0);
       } else if (ust + 1 < sub) {
         issue_tile(uc, false, ust + 1);
-      } else {
+      } else if (uc + 1 < nb) {
         issue_tile(uc + 1, true, 0);
       }
     };
-    if (nb > 1) issue_tile(0, false, 0);
+    if (has_query(0)) issue_tile(0, true, 0);
+    else if (has_update(0)) issue_tile(0, false, 0);
     // Master state: only the thread that owns feature t of a tile (and its half of
     // the columns) ever touches those entries, so they are stored in the order
     // that makes a warp's accesses contiguous: float4 u4 of (tile j, half, lane
@@ -542,15 +557,18 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
       const int64_t b0 = c * p.bs;
       const int64_t b1 = min(b0 + (int64_t)p.bs, p.n);
       // ---------------- query phase: tokens of block c read S_{<c}
-      if (c == 0) {
+      if (!has_query(c)) {
         for (int64_t i = b0 + t + half * kRows; i < b1; i += 2 * kRows) {
           float* dst = part_h + i * col_stride;
           for (int col = 0; col <= p.dv; ++col) dst[col] = 0.0f;
         }
       } else {
-        if (c >= 2) mload(0);   // the state rows written by the previous query phase
-        if (!mbar_wait(u_done, (int)((c - 1) & 1), ab, kErrMomWait)) { ok = false; break; }
-        tc_fence_after();
+        const bool frozen = p.mode == 2;
+        if (c >= 2 || frozen) mload(0);   // the state rows written by the previous query phase
+        if (!frozen) {
+          if (!mbar_wait(u_done, (int)((c - 1) & 1), ab, kErrMomWait)) { ok = false; break; }
+          tc_fence_after();
+        }
         const int nsq = (int)((b1 - b0 + kRows - 1) / kRows);  // query sub-tiles of block c
         for (int st = 0; ok && st < nsq; ++st) {
           const int64_t i = b0 + (int64_t)st * kRows + t;
@@ -599,7 +617,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
 #pragma unroll
               for (int q = 0; q < HC / 16; ++q) {
                 float sv[16];
-                if (st == 0) {
+                if (st == 0 && !frozen) {
                   uint32_t a[16], b[16];
                   tmem_ld16(la + j * L::kTC + half * HC + 16 * q, a);
                   tmem_ld16(la + j * L::kTC + DVP + half * HC + 16 * q, b);
@@ -636,7 +654,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
             // prefetch the state row of the next tile to fold: tile j + 1, or tile 0 of
             // the next sub-tile (written by the fold of sub-tile 0 above)
             if (j + 1 < ntiles) {
-              if (st > 0 || c >= 2) mload(j + 1);
+              if (st > 0 || c >= 2 || frozen) mload(j + 1);
             } else if (st + 1 < nsq) {
               mload(0);
             }
@@ -713,7 +731,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
           }
         }
       }
-      if (!ok || c + 1 >= nb) continue;
+      if (!ok || !has_update(c)) continue;
       // ---------------- update phase: dS_j of block c
       float sd[FT];
 #pragma unroll
@@ -805,6 +823,43 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
           if (j < ntiles) sden[j * kRows + t] += sd[j] + sdx[j * kRows + t];
       }
     }
+    if (ok && p.mode == 1) {
+      // total: fold the last block's dS into the master (which then holds the
+      // state of every block) and hand out the feature sums
+      if (!mbar_wait(u_done, (int)((nb - 1) & 1), ab, kErrMomWait)) {
+        ok = false;
+      } else {
+        tc_fence_after();
+        for (int j = 0; j < ntiles; ++j) {
+          float4* mrow = mrow_of(j);
+#pragma unroll
+          for (int q = 0; q < HC / 16; ++q) {
+            uint32_t a[16], b[16];
+            tmem_ld16(la + j * L::kTC + half * HC + 16 * q, a);
+            tmem_ld16(la + j * L::kTC + DVP + half * HC + 16 * q, b);
+            tmem_wait_ld();
+#pragma unroll
+            for (int u4 = 0; u4 < 4; ++u4) {
+              float4 v4 = make_float4(__uint_as_float(a[4 * u4]) + __uint_as_float(b[4 * u4]),
+                                      __uint_as_float(a[4 * u4 + 1]) + __uint_as_float(b[4 * u4 + 1]),
+                                      __uint_as_float(a[4 * u4 + 2]) + __uint_as_float(b[4 * u4 + 2]),
+                                      __uint_as_float(a[4 * u4 + 3]) + __uint_as_float(b[4 * u4 + 3]));
+              if (nb >= 2) {
+                const float4 m4 = mrow[(4 * q + u4) * kRows];
+                v4.x += m4.x;
+                v4.y += m4.y;
+                v4.z += m4.z;
+                v4.w += m4.w;
+              }
+              mrow[(4 * q + u4) * kRows] = v4;
+            }
+          }
+        }
+        if (half == 0)
+          for (int j = 0; j < ntiles; ++j)
+            p.den_io[((int64_t)g * p.bh + h) * (FT * kRows) + j * kRows + t] = sden[j * kRows + t];
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -865,6 +920,44 @@ int64_t moments_tc_master_floats(int64_t bh, int d, int dv, int degree) {
   return (int64_t)G * bh * ft * kRows * dvp;
 }
 
+// Floats of the feature sums that go with the master state: [G, bh, FT*128].
+int64_t moments_tc_den_floats(int64_t bh, int d, int dv, int degree) {
+  const int G = moments_tc_groups(d, dv, degree);
+  if (G <= 0) return 0;
+  const int ft = (dv <= 32 ? 32 : 64) == 32 ? MomLayout<32>::kFT : MomLayout<64>::kFT;
+  return (int64_t)G * bh * ft * kRows;
+}
+
+namespace {
+
+// The exclusive prefix of per-shard moment states: for each entry e,
+// sum over r < nprev of states[r * stride + e], added in shard order; the
+// first n_master entries go to the master state, the rest to the feature sums.
+__global__ void state_prefix_kernel(const float* __restrict__ states, int nprev, int64_t stride,
+                                    float* __restrict__ master, int64_t n_master, float* __restrict__ den,
+                                    int64_t n_den) {
+  const int64_t total = n_master + n_den;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    float acc = 0.0f;
+    for (int r = 0; r < nprev; ++r) acc += __ldg(states + r * stride + e);
+    if (e < n_master) master[e] = acc;
+    else den[e - n_master] = acc;
+  }
+}
+
+}  // namespace
+
+int launch_state_prefix(const float* states, int nprev, int64_t n_master, int64_t n_den, float* master, float* den,
+                        cudaStream_t stream) {
+  const int64_t total = n_master + n_den;
+  if (total == 0) return SA_OK;
+  if (nprev > 0 && !states) return set_error(SA_ERR_INVALID_ARG, "null state pointer");
+  const int threads = 256;
+  const int64_t blocks = min((total + threads - 1) / threads, (int64_t)148 * 8);
+  state_prefix_kernel<<<(unsigned)blocks, threads, 0, stream>>>(states, nprev, total, master, n_master, den, n_den);
+  return check_launch("state_prefix_kernel");
+}
+
 // out[e] = sum_g part[g * stride + e]: the low sums from the per-group partials.
 int launch_sum_groups(const float* part, int groups, int64_t stride, float* out, cudaStream_t stream) {
   if (stride == 0) return SA_OK;
@@ -877,12 +970,14 @@ int launch_sum_groups(const float* part, int groups, int64_t stride, float* out,
 // maps: split v hi / lo ([bh, n, dvp], box {32, 32, 1}, 128-byte swizzle with 32-byte atoms).
 int launch_moments_tc(const CUtensorMap* maps, const float* q, const float* k, float* part, float* master,
                       int* status, int64_t bh, int64_t n, int d, int dv, int degree, int bs, float scale,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, int mode, float* den_io) {
   if (bh == 0 || n == 0) return SA_OK;
   const int G = moments_tc_groups(d, dv, degree);
   if (G <= 0) return set_error(SA_ERR_UNSUPPORTED, "tensor-core moments: shape not supported");
   if (bh > 65535) return set_error(SA_ERR_UNSUPPORTED, "too many sequences for one launch");
-  MomTCParams prm{q, k, part, master, status, n, bh, d, dv, bs, degree, (int)mom_seg_count(d, degree), G, scale};
+  if (mode != 0 && !den_io) return set_error(SA_ERR_INVALID_ARG, "moment state modes need the feature-sum buffer");
+  MomTCParams prm{q, k, part, master, status, n, bh, d, dv, bs, degree, (int)mom_seg_count(d, degree), G, scale,
+                  mode, den_io};
   if (degree == 3) return dv <= 32 ? launch_mom_tc<32, true>(maps, prm, stream) : launch_mom_tc<64, true>(maps, prm, stream);
   return dv <= 32 ? launch_mom_tc<32, false>(maps, prm, stream) : launch_mom_tc<64, false>(maps, prm, stream);
 }

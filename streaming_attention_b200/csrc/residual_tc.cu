@@ -65,6 +65,8 @@ struct ResTCParams {
   float scale, eps;
   int groups;            // partial slices in `low`
   int64_t group_stride;  // floats between slices (bh * n * (dv+1))
+  int64_t c_off;         // global index of the sequence's first block (a shard of a longer sequence:
+                         // rep rows and each query's active reps count from global block 0)
 };
 
 template <int DP, int DVP>
@@ -148,7 +150,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
   const int64_t q0 = qt * kRowsQ;
   const int64_t q_last = min(q0 + kRowsQ, p.n) - 1;
   const int64_t c_first = q0 / p.bs, c_last = q_last / p.bs;
-  const int64_t r_end = c_last * p.m_blk;
+  const int64_t r_end = (p.c_off + c_last) * p.m_blk;
   const int n_rep = (int)((r_end + kTile - 1) / kTile);
   const int64_t kb0 = c_first * p.bs;
   const int n_cur = (int)((q_last + 1 - kb0 + kTile - 1) / kTile);
@@ -319,7 +321,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
       mbar_arrive(qready);
     }
     const int64_t ci = valid ? i / p.bs : 0;
-    const int64_t lim = valid ? ci * p.m_blk : 0;    // reps r < lim are active for this query
+    const int64_t lim = valid ? (p.c_off + ci) * p.m_blk : 0;    // reps r < lim are active for this query
     const int64_t bst = valid ? ci * p.bs : p.n;      // first key of this query's block
     float den = 0.0f;
     bool ok = true;
@@ -473,11 +475,12 @@ int residual_tc_dvp(int dv) { return dv <= 32 ? 32 : (dv <= 64 ? 64 : (dv <= 128
 // maps: rep_k_hi, rep_k_lo, rep_v_hi, rep_v_lo, k_hi, k_lo, v_hi, v_lo (3-D, box {32, 64, 1}).
 int launch_residual_tc(const CUtensorMap* maps, const float* q, const float* rep_w, int64_t r_pad, const float* low,
                        int groups, float* out, int* status, int64_t bh, int64_t n, int d, int dv, int degree, int bs,
-                       int64_t m_blk, float scale, float eps, cudaStream_t stream) {
+                       int64_t m_blk, float scale, float eps, cudaStream_t stream, int64_t c_off) {
   if (bh == 0 || n == 0) return SA_OK;
   if (bh > 65535 || (n + kRowsQ - 1) / kRowsQ > 2147483647LL)
     return set_error(SA_ERR_UNSUPPORTED, "grid too large for the tensor-core residual");
-  ResTCParams prm{q, rep_w, low, out, status, n, m_blk, r_pad, d, dv, bs, scale, eps, groups, bh * n * (dv + 1)};
+  ResTCParams prm{q, rep_w, low, out, status, n, m_blk, r_pad, d, dv, bs, scale, eps, groups, bh * n * (dv + 1),
+                  c_off};
   const int dp = residual_tc_dp(d), dvp = residual_tc_dvp(dv);
   if (dp == 32 && dvp == 32) return launch_deg<32, 32>(degree, maps, prm, bh, stream);
   if (dp == 32 && dvp == 64) return launch_deg<32, 64>(degree, maps, prm, bh, stream);

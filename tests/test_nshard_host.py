@@ -1,0 +1,67 @@
+"""Host logic of the N-sharded forward on CPU: the shard plan, and the
+exchange over a world-size-2 gloo group (two processes on this host)."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from streaming_attention_b200 import nshard
+
+
+def test_shard_plan_splits_blocks_and_reps():
+    p = [nshard.shard_plan(4096, 4, r, 256, "sorted_pair") for r in range(4)]
+    assert [x.t0 for x in p] == [0, 1024, 2048, 3072]
+    assert [x.c_off for x in p] == [0, 4, 8, 12]
+    # 15 completed blocks in all: the last shard's last block completes nothing later
+    assert [x.n_compress for x in p] == [4, 4, 4, 3]
+    assert all(x.reps_per_rank == 4 * 128 for x in p)
+    none = nshard.shard_plan(1024, 2, 1, 64, "none")
+    assert (none.n_compress, none.reps_per_rank, none.m_blk) == (0, 512, 64)
+    with pytest.raises(ValueError, match="equal shards"):
+        nshard.shard_plan(1000, 3, 0, 8, "sorted_pair")
+    with pytest.raises(ValueError, match="whole number of blocks"):
+        nshard.shard_plan(1024, 2, 0, 100, "sorted_pair")
+    with pytest.raises(ValueError, match="rank"):
+        nshard.shard_plan(1024, 2, 2, 64, "sorted_pair")
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _exchange_rank(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        bh, rb, d = 2, 3, 4
+        state = torch.full((5,), float(rank + 1))
+        rk = torch.arange(bh * rb * d, dtype=torch.float32).reshape(bh, rb, d) + 100 * rank
+        rv = rk[..., :2] * 2
+        rw = torch.full((bh, rb), float(rank))
+        before, ka, va, wa = nshard.exchange(state, rk, rv, rw, rank, world)
+        results[rank] = (before.clone(), ka.clone(), va.clone(), wa.clone())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_exchange_over_a_two_rank_gloo_group():
+    world = 2
+    with mp.Manager() as mgr:
+        results = mgr.dict()
+        mp.spawn(_exchange_rank, args=(world, _free_port(), results), nprocs=world, join=True)
+        r0, r1 = results[0], results[1]
+    # rank 0 sees no earlier state and only its own reps
+    assert r0[0].shape == (0, 5)
+    assert r0[1].shape == (2, 3, 4) and torch.equal(r0[3], torch.zeros(2, 3))
+    # rank 1: the state of rank 0, the reps of ranks 0 then 1 per sequence
+    assert torch.equal(r1[0], torch.ones(1, 5))
+    base = torch.arange(24, dtype=torch.float32).reshape(2, 3, 4)
+    assert torch.equal(r1[1], torch.cat([base, base + 100], dim=1))
+    assert torch.equal(r1[3], torch.cat([torch.zeros(2, 3), torch.ones(2, 3)], dim=1))
