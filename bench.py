@@ -353,6 +353,68 @@ class Staged:
             self.times["residual"].append(ev[2].elapsed_time(ev[3]))
 
 
+def run_nshard(args, rank, world, dev):
+    """Config 5 over several GPUs: every sequence split along N (rank r holds
+    tokens [r N/P, (r+1) N/P) of all sequences); each step is one collective
+    sharded forward (local scan, NCCL all-gather of states and reps, device
+    prefix scan, residual)."""
+    from streaming_attention_b200 import nshard, workloads
+
+    c = bench_config(args)
+    N, P = c["N"], world
+    chunks = nshard.owned_chunks(rank, world, "zigzag")
+    L = N // (P * len(chunks))
+    q, k, v = workloads.make_inputs(c, seed=0, device=dev, generator_device="cuda")
+    q, k, v = (torch.cat([x[:, :, j * L:(j + 1) * L] for j in chunks], dim=2).contiguous() for x in (q, k, v))
+    torch.cuda.empty_cache()
+    kw = dict(degree=c["degree"], block_size=c["block_size"], scale=c["scale"], compressor=c["compressor"], seed=0)
+
+    def step():
+        return nshard.fast_article_causal_attention_nshard(q, k, v, rank=rank, world=world, **kw)
+
+    def barrier():
+        torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    with ClockSampler(dev.index) as clk:
+        barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            step()
+        t1.record()
+        barrier()
+    ms_max = reduce_max(t0.elapsed_time(t1), world, dev)
+    out = None
+    if rank == 0:
+        work = algorithmic_work(c)
+        flops = (work["moment_flops"] + work["residual_flops"]) * c["B"] * c["H"]
+        tf32_peak = tf32_gemm_peak_tflops(dev)
+        achieved = flops * args.steps / (ms_max / 1e3) / 1e12 / world
+        out = {
+            "metric": METRIC, "value": c["B"] * c["H"] * N * args.steps / (ms_max / 1e3), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded, CUDA generator)",
+            "config": {"workload": workload_name(c, args.config), "B": c["B"], "H": c["H"], "N": N, "d": c["d"],
+                       "dv": c["dv"], "degree": c["degree"], "block_size": c["block_size"],
+                       "compressor": c["compressor"],
+                       "parallelism": f"N sharded over {world} GPU(s) in zig-zag chunk pairs: NCCL all-gather "
+                                      "of moment states and reps",
+                       "l2": "inputs larger than L2 (no flush needed)"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
+                         "frac": achieved / tf32_peak, "frac_3xtf32": 3 * achieved / tf32_peak,
+                         "kernel": "whole sharded forward, per GPU", "traffic": None,
+                         "peak_source": "measured cuBLAS TF32 GEMM (8192^3) in this run"},
+            "e2e": None, "gpu_launches": None, "clocks": clk.summary(),
+        }
+    return out, c
+
+
 def run_ours(args, rank, world, dev):
     import streaming_attention_b200 as sa
     from streaming_attention_b200 import _lib, workloads
@@ -578,7 +640,10 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=dev)
     try:
-        line, c = run_ours(args, rank, world, dev)
+        if args.config == 5 and world > 1:
+            line, c = run_nshard(args, rank, world, dev)
+        else:
+            line, c = run_ours(args, rank, world, dev)
         if rank == 0:
             if world == 1 and not args.no_cpu_baseline:
                 heads = args.cpu_sample_heads or auto_sample_heads(c, 10.0)

@@ -18,6 +18,11 @@ number of blocks, and the forward runs in three steps:
    local query; the residual runs over the reps of all earlier blocks (global
    block offset) and the exact current block, and divides.
 
+With ``layout="zigzag"`` (the default) the sequence is cut into 2P chunks and
+rank r holds chunks r and 2P - 1 - r: the residual work of a chunk grows with
+the reps before it, so pairing an early with a late chunk evens the ranks out.
+Each chunk is a shard of the 2P-way split; the exchange gathers all chunks.
+
 The moment sums are linear in the state, so the local and the earlier-shard
 parts are two sets of partial slices that the residual epilogue adds.  The
 result equals the single-GPU forward up to the association of the fp32
@@ -38,7 +43,8 @@ from .fast import _attention_scale, _as_f32, _check_device, _check_modes, _ptr
 
 Tensor = torch.Tensor
 
-__all__ = ["ShardPlan", "shard_plan", "fast_article_causal_attention_nshard", "nshard_emulate"]
+__all__ = ["ShardPlan", "shard_plan", "owned_chunks", "exchange", "fast_article_causal_attention_nshard",
+           "nshard_emulate"]
 
 
 @dataclass(frozen=True)
@@ -171,6 +177,18 @@ def exchange(state: Tensor, rk: Tensor, rv: Tensor, rw: Tensor, rank: int, world
     return before.contiguous(), _assemble(ks[:rank + 1]), _assemble(vs[:rank + 1]), _assemble(ws[:rank + 1])
 
 
+def owned_chunks(rank: int, world: int, layout: str = "zigzag") -> List[int]:
+    """Chunk indices a rank holds.  "contiguous": chunk r of a world-way split.
+    "zigzag": chunks r and 2 world - 1 - r of a 2 world-way split, so that every
+    rank gets one early and one late chunk (the residual work of a chunk grows
+    with the number of reps before it) and the ranks finish together."""
+    if layout == "contiguous":
+        return [rank]
+    if layout == "zigzag":
+        return [rank, 2 * world - 1 - rank]
+    raise ValueError("layout must be 'contiguous' or 'zigzag'")
+
+
 def _prep(q: Tensor, k: Tensor, v: Tensor):
     if q.ndim != 4 or k.shape != q.shape or v.shape[:3] != q.shape[:3]:
         raise ValueError("q/k/v must be [B,H,L,D], [B,H,L,D], [B,H,L,Dv] shards")
@@ -180,28 +198,56 @@ def _prep(q: Tensor, k: Tensor, v: Tensor):
 
 @torch.no_grad()
 def fast_article_causal_attention_nshard(
-    q: Tensor, k: Tensor, v: Tensor, *, rank: int, world: int, group=None, degree: int = 2, block_size: int = 128,
-    scale: Optional[float] = None, compressor: str = "sorted_pair", seed: int = 0, denominator_eps: float = 1e-12,
+    q: Tensor, k: Tensor, v: Tensor, *, rank: int, world: int, group=None, layout: str = "zigzag", degree: int = 2,
+    block_size: int = 128, scale: Optional[float] = None, compressor: str = "sorted_pair", seed: int = 0,
+    denominator_eps: float = 1e-12,
 ) -> Tensor:
-    """This rank's [B, H, L, Dv] slice of fast_article_causal_attention over
-    sequences of world * L tokens, of which q, k, v hold tokens
-    [rank L, (rank + 1) L).  Every rank of ``group`` calls it collectively."""
-    B, H, L, d, dv = _prep(q, k, v)
+    """This rank's part of fast_article_causal_attention over [B, H, N, *]
+    sequences split along N.  q, k, v hold the rank's chunks (see
+    ``owned_chunks``) concatenated along N in that order; the result is the
+    matching [B, H, len, Dv] slice of the output.  Every rank of ``group``
+    calls it collectively."""
+    B, H, Lr, d, dv = _prep(q, k, v)
     _check_device(q, k, v)
-    _check_modes(L * world, block_size, degree, compressor, "auto")
+    chunks = owned_chunks(rank, world, layout)
+    nv = world * len(chunks)                     # chunks of the whole sequence
+    if Lr % len(chunks):
+        raise ValueError("the rank's tokens do not split into its chunks")
+    L = Lr // len(chunks)
+    _check_modes(L * nv, block_size, degree, compressor, "auto")
     if compressor not in _lib.COMPRESSORS:
         raise ValueError("compressor must be one of {'sorted_pair', 'random', 'none'}")
-    plan = shard_plan(L * world, world, rank, block_size, compressor)
     bh = B * H
     s = _attention_scale(scale, d)
-    sh = _Shard(_as_f32(q).reshape(bh, L, d), _as_f32(k).reshape(bh, L, d), _as_f32(v).reshape(bh, L, dv), plan,
-                batch=B, heads=H, degree=degree, block_size=block_size, scale=s, compressor=compressor, seed=seed,
-                eps=denominator_eps)
-    state, rk, rv, rw, _ = sh.begin()
-    before, rk_all, rv_all, rw_all = exchange(state, rk, rv, rw, rank, world, group)
-    out = torch.empty(bh, L, dv, device=q.device, dtype=torch.float32)
-    sh.end(before, rk_all, rv_all, rw_all, out)
-    return out.reshape(B, H, L, dv).to(q.dtype)
+    shards = []
+    for i, j in enumerate(chunks):
+        sl = slice(i * L, (i + 1) * L)
+        f = lambda x: _as_f32(x[:, :, sl]).reshape(bh, L, -1)  # noqa: E731
+        shards.append(_Shard(f(q), f(k), f(v), shard_plan(L * nv, nv, j, block_size, compressor), batch=B,
+                             heads=H, degree=degree, block_size=block_size, scale=s, compressor=compressor,
+                             seed=seed, eps=denominator_eps))
+    begun = [sh.begin() for sh in shards]
+    # all-gather every rank's chunks, then index them by chunk
+    import torch.distributed as dist
+
+    def gather(t: Tensor) -> List[Tensor]:
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t.contiguous(), group=group)
+        return parts
+
+    per = [gather(torch.stack([b[x] for b in begun])) for x in range(4)]   # state, rep_k, rep_v, rep_w
+    owner = {}
+    for r in range(world):
+        for slot, j in enumerate(owned_chunks(r, world, layout)):
+            owner[j] = (r, slot)
+    by_chunk = [[per[x][owner[j][0]][owner[j][1]] for j in range(nv)] for x in range(4)]
+    outs = []
+    for sh, j in zip(shards, chunks):
+        before = (torch.stack(by_chunk[0][:j]) if j > 0 else by_chunk[0][0].new_empty(0, sh.state_floats))
+        out = torch.empty(bh, L, dv, device=q.device, dtype=torch.float32)
+        outs.append(sh.end(before.contiguous(), _assemble(by_chunk[1][:j + 1]), _assemble(by_chunk[2][:j + 1]),
+                           _assemble(by_chunk[3][:j + 1]), out))
+    return torch.cat(outs, dim=1).reshape(B, H, Lr, dv).to(q.dtype)
 
 
 @torch.no_grad()

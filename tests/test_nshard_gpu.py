@@ -68,12 +68,14 @@ def _nccl_rank(rank, world, port, q, k, v, kw, results):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
     try:
-        L = q.shape[2] // world
-        sl = slice(rank * L, (rank + 1) * L)
         d = torch.device("cuda", rank)
-        out = nshard.fast_article_causal_attention_nshard(q[:, :, sl].to(d), k[:, :, sl].to(d), v[:, :, sl].to(d),
-                                                          rank=rank, world=world, **kw)
-        results[rank] = out.cpu()
+        for layout in ("contiguous", "zigzag"):
+            chunks = nshard.owned_chunks(rank, world, layout)
+            L = q.shape[2] // (world * len(chunks))
+            pick = lambda x: torch.cat([x[:, :, j * L:(j + 1) * L] for j in chunks], dim=2).to(d)  # noqa: E731
+            out = nshard.fast_article_causal_attention_nshard(pick(q), pick(k), pick(v), rank=rank, world=world,
+                                                              layout=layout, **kw)
+            results[(rank, layout)] = (chunks, out.cpu())
     finally:
         dist.destroy_process_group()
 
@@ -88,5 +90,12 @@ def test_sharded_forward_over_nccl(dev):
     with mp.Manager() as mgr:
         results = mgr.dict()
         mp.spawn(_nccl_rank, args=(2, _free_port(), q, k, v, kw, results), nprocs=2, join=True)
-        out = torch.cat([results[0], results[1]], dim=2)
-    assert O.relative_l2(out.numpy(), ref.numpy()) < TOL
+        for layout in ("contiguous", "zigzag"):
+            parts = {}
+            for r in range(2):
+                chunks, out = results[(r, layout)]
+                L = out.shape[2] // len(chunks)
+                for i, j in enumerate(chunks):
+                    parts[j] = out[:, :, i * L:(i + 1) * L]
+            full = torch.cat([parts[j] for j in sorted(parts)], dim=2)
+            assert O.relative_l2(full.numpy(), ref.numpy()) < TOL, layout

@@ -65,3 +65,12 @@ def test_exchange_over_a_two_rank_gloo_group():
     base = torch.arange(24, dtype=torch.float32).reshape(2, 3, 4)
     assert torch.equal(r1[1], torch.cat([base, base + 100], dim=1))
     assert torch.equal(r1[3], torch.cat([torch.zeros(2, 3), torch.ones(2, 3)], dim=1))
+
+
+def test_zigzag_ownership_covers_every_chunk_once():
+    for world in (1, 2, 4, 8):
+        owned = [j for r in range(world) for j in nshard.owned_chunks(r, world, "zigzag")]
+        assert sorted(owned) == list(range(2 * world))
+        assert nshard.owned_chunks(1, 4, "contiguous") == [1]
+    with pytest.raises(ValueError, match="layout"):
+        nshard.owned_chunks(0, 2, "striped")
