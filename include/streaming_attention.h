@@ -226,6 +226,39 @@ int sa_fast_attention_static_scratch(const float* q, const float* k, const float
                                      const float* coins, const int32_t* perms, float eps,
                                      float* out, int32_t* rep_idx, void* stream);
 
+/* ---- the segment-mean variant (deterministic reps) -------------------------
+ * Replaces triton_article_causal_attention (triton_article_attention.py:448-578)
+ * and its kernel _article_direct_kernel (:266-370): the same low-degree
+ * moments and exact current-block residual as sa_fast_attention, but each
+ * completed block is represented by the means of its block_size/compress_stride
+ * runs of compress_stride adjacent tokens, each of weight compress_stride, and
+ * the exp of a score is taken of min(score, 80) (:331-333, :359).  degree 0, 1
+ * or 2 (else SA_ERR_UNSUPPORTED); block_size % compress_stride != 0 is
+ * SA_ERR_INVALID_ARG.  d <= 128 and dv <= 128.  key_dtype / value_dtype say
+ * how the reference's reps were stored (the dtypes of its k and v, SA_REP_*):
+ * the key and value means are rounded to them. */
+#define SA_REP_FLOAT32 0
+#define SA_REP_FLOAT16 1
+#define SA_REP_BFLOAT16 2
+
+/* Replaces build_segment_mean_coreset (triton_article_attention.py:190-245):
+ * rep_k [bh, R, d], rep_v [bh, R, dv], R = (n-1)/block_size *
+ * (block_size/compress_stride) (0 rows when n <= block_size). */
+int sa_segment_mean_reps(const float* k, const float* v, int64_t bh, int64_t n, int d, int dv,
+                         int block_size, int compress_stride, int key_dtype, int value_dtype,
+                         float* rep_k, float* rep_v, void* stream);
+
+/* Bytes of device workspace sa_article_segment_mean needs. */
+int sa_article_segment_mean_workspace_size(int64_t bh, int64_t n, int d, int dv, int degree,
+                                           int block_size, int compress_stride, size_t* bytes);
+
+/* The whole forward of the segment-mean variant for bh sequences. */
+int sa_article_segment_mean(const float* q, const float* k, const float* v, int64_t bh, int64_t n,
+                            int d, int dv, int degree, int block_size, int compress_stride,
+                            float scale, int key_dtype, int value_dtype, float eps, float* out,
+                            void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,6 +21,8 @@ SA_ERR_TIMEOUT = -4
 SA_ERR_WORKSPACE = -5
 
 COMPRESSORS = {"none": 0, "sorted_pair": 1, "random": 2}
+# storage dtype of the segment-mean reps (SA_REP_*)
+REP_DTYPES = {"float32": 0, "float16": 1, "bfloat16": 2}
 MAX_DEGREE = 3
 
 _i64 = ctypes.c_int64
@@ -54,6 +56,10 @@ SIGNATURES = {
     "sa_stream_update": [_vp, _vp, _i32, _i32, _i32, _f32, _vp, _vp, _vp],
     "sa_stream_compress": [_vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "sa_stream_query_workspace_size": [_i32, _i32, _i32, ctypes.POINTER(_sz)],
+    "sa_segment_mean_reps": [_vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp],
+    "sa_article_segment_mean_workspace_size": [_i64, _i64, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(_sz)],
+    "sa_article_segment_mean": [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _f32,
+                                _vp, _vp, _sz, _vp],
     "sa_stream_query": [_vp, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _i64, _f32, _vp, _vp,
                         _vp, _sz, _vp],
 }

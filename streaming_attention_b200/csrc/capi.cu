@@ -33,7 +33,8 @@ int residual_tc_dp(int d);
 int residual_tc_dvp(int dv);
 int launch_residual_tc(const CUtensorMap* maps, const float* q, const float* rep_w, int64_t r_pad, const float* low,
                        int groups, float* out, int* status, int64_t bh, int64_t n, int d, int dv, int degree, int bs,
-                       int64_t m_blk, float scale, float eps, cudaStream_t stream, int64_t c_off = 0);
+                       int64_t m_blk, float scale, float eps, cudaStream_t stream, int64_t c_off = 0,
+                       bool clamp_exp = false);
 int moments_tc_groups(int d, int dv, int degree);
 int64_t moments_tc_master_floats(int64_t bh, int d, int dv, int degree);
 int launch_moments_tc(const CUtensorMap* maps, const float* q, const float* k, float* part, float* master,
@@ -48,6 +49,12 @@ int launch_low_moments(const float* q, const float* k, const float* v, int64_t b
 int launch_residual(const float* q, const float* k, const float* v, const float* rk, const float* rv,
                     const float* rw, const float* low, int64_t bh, int64_t n, int d, int dv, int degree, int bs,
                     int compressor, float scale, float eps, float* out, cudaStream_t s);
+int launch_residual_reps(const float* q, const float* k, const float* v, const float* rk, const float* rv,
+                         const float* rw, const float* low, int64_t bh, int64_t n, int d, int dv, int degree, int bs,
+                         int64_t m_blk, int64_t rph, float scale, float eps, bool clamp, float* out, cudaStream_t s);
+int launch_segment_mean(const float* k, const float* v, int64_t bh, int64_t n, int d, int dv, int bs, int stride,
+                        int key_dtype, int value_dtype, float* rep_k, float* rep_v, cudaStream_t s);
+int launch_fill(float* dst, int64_t count, float value, cudaStream_t s);
 
 namespace {
 thread_local char g_err[512] = {0};
@@ -88,6 +95,12 @@ int check_compressor(int c) {
   return SA_OK;
 }
 
+// Reps per completed block of the merge-reduce compressors; compressor none
+// reads every key of a block as its own rep.
+inline int64_t reps_per_block(int compressor, int bs) {
+  return compressor == SA_COMPRESSOR_NONE ? bs : (bs + 1) / 2;
+}
+
 constexpr size_t kAlign = 256;
 inline size_t align_up(size_t x) { return (x + kAlign - 1) & ~(kAlign - 1); }
 
@@ -114,9 +127,11 @@ struct Workspace {
   size_t den_io = 0;  // sharded forward: the feature sums of the moment state
 };
 
-enum class Plan { kFull, kResidualOnly, kMomentsOnly };
+// kSegment: the segment-mean variant (reps made by the segment-mean kernel as
+// plain rows, then split; `stride` adjacent tokens per rep, 1 = the keys).
+enum class Plan { kFull, kResidualOnly, kMomentsOnly, kSegment };
 
-Workspace plan(int64_t bh, int64_t n, int d, int dv, int degree, int bs, int compressor, Plan what) {
+Workspace plan(int64_t bh, int64_t n, int d, int dv, int degree, int bs, int compressor, Plan what, int stride = 0) {
   Workspace w{};
   const bool simt = force_simt();
   w.dp = residual_tc_dp(d);
@@ -128,7 +143,10 @@ Workspace plan(int64_t bh, int64_t n, int d, int dv, int degree, int bs, int com
   w.groups = (!simt && aligned_blocks && what != Plan::kResidualOnly) ? moments_tc_groups(d, dv, degree) : 0;
   if (w.groups > 0 && w.dvp == 0) w.dvp = dv <= 32 ? 32 : 64;
   const int64_t nc = n > 0 ? (n - 1) / bs : 0;
-  w.R = (compressor == SA_COMPRESSOR_NONE) ? 0 : nc * ((bs + 1) / 2);
+  if (what == Plan::kSegment)
+    w.R = stride > 1 ? nc * (bs / stride) : 0;
+  else
+    w.R = (compressor == SA_COMPRESSOR_NONE) ? 0 : nc * ((bs + 1) / 2);
   w.r_pad = (w.R + 63) / 64 * 64;
   w.n_pad = (n + 3) / 4 * 4;
   size_t off = 0;
@@ -151,14 +169,16 @@ Workspace plan(int64_t bh, int64_t n, int d, int dv, int degree, int bs, int com
     w.vtlo = take((size_t)bh * w.dvp * w.n_pad * f);
   }
   if (what != Plan::kMomentsOnly) {
+    const bool seg = what == Plan::kSegment;
     if (w.tc) {
       w.rkhi = take((size_t)bh * w.R * w.dp * f);
       w.rklo = take((size_t)bh * w.R * w.dp * f);
       w.rvthi = take((size_t)bh * w.dvp * w.r_pad * f);
       w.rvtlo = take((size_t)bh * w.dvp * w.r_pad * f);
       w.rep_w = take((size_t)bh * w.r_pad * f);
-      if (what == Plan::kFull) w.rep_v = take((size_t)bh * w.R * dv * f);   // gathered rows, then transposed
-    } else if (what == Plan::kFull) {
+      if (seg) w.rep_k = take((size_t)bh * w.R * d * f);   // segment means, then split
+      if (what == Plan::kFull || seg) w.rep_v = take((size_t)bh * w.R * dv * f);   // rep rows, then transposed
+    } else if (what == Plan::kFull || seg) {
       w.rep_k = take((size_t)bh * w.R * d * f);
       w.rep_v = take((size_t)bh * w.R * dv * f);
       w.rep_w = take((size_t)bh * w.R * f);
@@ -230,8 +250,8 @@ struct TCOperands {
 // 32-column chunk; V^T tiles are dvp value rows of a 32-key chunk.
 int residual_tc_from_split(const Workspace& w, const TCOperands& rep, const TCOperands& cur, const float* rep_w,
                            const float* q, const float* low, int groups, float* out, int* status, int64_t bh,
-                           int64_t n, int d, int dv, int degree, int block_size, int compressor, float scale,
-                           float eps, cudaStream_t s, int64_t c_off = 0) {
+                           int64_t n, int d, int dv, int degree, int block_size, int64_t m_blk, float scale,
+                           float eps, cudaStream_t s, int64_t c_off = 0, bool clamp_exp = false) {
   CUtensorMap maps[8];
   const TCOperands* ops[2] = {&rep, &cur};
   for (int j = 0; j < 2; ++j) {
@@ -242,9 +262,8 @@ int residual_tc_from_split(const Workspace& w, const TCOperands& rep, const TCOp
     if (!rc) rc = encode_map(&maps[4 * j + 3], o.vtlo, o.vrows, o.vpitch, w.dvp, bh, w.dvp, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
-  const int64_t m_blk = compressor == SA_COMPRESSOR_NONE ? block_size : (block_size + 1) / 2;
   return launch_residual_tc(maps, q, rep_w, w.r_pad, low, groups, out, status, bh, n, d, dv, degree, block_size,
-                            m_blk, scale, eps, s, c_off);
+                            m_blk, scale, eps, s, c_off, clamp_exp);
 }
 
 // Tensor-core moments into `part` ([groups, bh, n, dv+1]) from the transposed
@@ -297,6 +316,26 @@ Workspace plan_shard(int64_t bh, int64_t n, int d, int dv, int degree, int bs, i
   w.rep_w = take((size_t)bh * w.r_pad * f);
   w.total = off;
   return w;
+}
+
+// Argument checks of the segment-mean variant, in the reference's order
+// (triton_article_attention.py:487-501); the width limits belong to the
+// forward only (the rep builder, :216-223, takes any width).
+int check_segment(const void* q, const void* k, const void* v, int64_t bh, int64_t n, int d, int dv, int degree,
+                  int bs, int stride, int key_dtype, int value_dtype, bool forward = true) {
+  if (degree < 0 || degree > 2)
+    return set_error(SA_ERR_UNSUPPORTED, "the segment-mean variant supports degree 0, 1, or 2");
+  if (bs <= 0 || stride <= 0) return set_error(SA_ERR_INVALID_ARG, "block_size and compress_stride must be positive");
+  if (bs % stride != 0) return set_error(SA_ERR_INVALID_ARG, "block_size must be divisible by compress_stride");
+  int rc = check_common(q, k, v, bh, n, d, dv, degree, bs);
+  if (rc) return rc;
+  if (forward && d > 128) return set_error(SA_ERR_INVALID_ARG, "this compact kernel supports D <= 128");
+  if (forward && dv > 256) return set_error(SA_ERR_INVALID_ARG, "this compact kernel supports Dv <= 256");
+  if (forward && dv > 128) return set_error(SA_ERR_UNSUPPORTED, "value_dim above 128: split the value columns");
+  for (const int t : {key_dtype, value_dtype})
+    if (t < SA_REP_FLOAT32 || t > SA_REP_BFLOAT16)
+      return set_error(SA_ERR_INVALID_ARG, "rep dtypes must be SA_REP_FLOAT32, SA_REP_FLOAT16 or SA_REP_BFLOAT16");
+  return SA_OK;
 }
 
 int check_workspace(const Workspace& w, const void* workspace, size_t workspace_bytes) {
@@ -455,7 +494,7 @@ int sa_residual_combine(const float* q, const float* k, const float* v, const fl
     rep_ops = TCOperands{r[0], r[1], w.R, r[2], r[3], w.R, w.r_pad};
   }
   return residual_tc_from_split(w, rep_ops, cur_ops, wpad, q, low, 1, out, status, bh, n, d, dv, degree, block_size,
-                                compressor, scale, eps, s);
+                                reps_per_block(compressor, block_size), scale, eps, s);
 }
 
 int sa_fast_attention_workspace_size(int64_t bh, int64_t n, int d, int dv, int degree, int block_size, int compressor,
@@ -555,7 +594,7 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
   // R: residual + combine
   if (w.tc)
     return residual_tc_from_split(w, rep_ops, cur_ops, rw, q, low, groups, out, status, bh, n, d, dv, degree,
-                                  block_size, compressor, scale, eps, s);
+                                  block_size, reps_per_block(compressor, block_size), scale, eps, s);
   if (groups > 1) {  // the CUDA-core residual reads one summed slice
     rc = launch_sum_groups(low, groups, bh * n * (dv + 1), low, s);
     if (rc) return rc;
@@ -691,7 +730,111 @@ int sa_shard_end(const float* q, const float* k, const float* v, int64_t bh, int
                            n, w.n_pad};
   const TCOperands rep_ops{r[0], r[1], rep_rows, r[2], r[3], rep_rows, w.r_pad};
   return residual_tc_from_split(w, rep_ops, cur_ops, rep_rows > 0 ? wpad : nullptr, q, low, groups, out,
-                                status, bh, n, d, dv, degree, block_size, compressor, scale, eps, s, c_off);
+                                status, bh, n, d, dv, degree, block_size, reps_per_block(compressor, block_size),
+                                scale, eps, s, c_off);
+}
+
+
+/* ---- the segment-mean variant (triton_article_attention.py:190-578) ---- */
+
+int sa_segment_mean_reps(const float* k, const float* v, int64_t bh, int64_t n, int d, int dv, int block_size,
+                         int compress_stride, int key_dtype, int value_dtype, float* rep_k, float* rep_v,
+                         void* stream) {
+  int rc = check_segment(k, k, v, bh, n, d, dv, 0, block_size, compress_stride, key_dtype, value_dtype, false);
+  if (rc) return rc;
+  const int64_t R = n > 0 ? (n - 1) / block_size * (block_size / compress_stride) : 0;
+  if (bh == 0 || R == 0) return SA_OK;
+  if (!rep_k || !rep_v) return set_error(SA_ERR_INVALID_ARG, "null rep pointer");
+  return launch_segment_mean(k, v, bh, n, d, dv, block_size, compress_stride, key_dtype, value_dtype, rep_k, rep_v,
+                             (cudaStream_t)stream);
+}
+
+int sa_article_segment_mean_workspace_size(int64_t bh, int64_t n, int d, int dv, int degree, int block_size,
+                                           int compress_stride, size_t* bytes) {
+  if (!bytes) return set_error(SA_ERR_INVALID_ARG, "null output pointer");
+  int rc = check_segment(nullptr, nullptr, nullptr, 0, n, d, dv, degree, block_size, compress_stride, 0, 0);
+  if (rc) return rc;
+  if (bh < 0) return set_error(SA_ERR_INVALID_ARG, "bh must be non-negative");
+  *bytes = plan(bh, n, d, dv, degree, block_size, SA_COMPRESSOR_NONE, Plan::kSegment, compress_stride).total;
+  return SA_OK;
+}
+
+// Same pipeline as sa_fast_attention with the segment-mean kernel in place of
+// the compressor: reps of weight compress_stride, bs/compress_stride per block
+// (compress_stride 1: every earlier key, weight 1, read in place), and the
+// exp argument capped at 80 in the residual.
+int sa_article_segment_mean(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d, int dv,
+                            int degree, int block_size, int compress_stride, float scale, int key_dtype,
+                            int value_dtype, float eps, float* out, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  int rc = check_segment(q, k, v, bh, n, d, dv, degree, block_size, compress_stride, key_dtype, value_dtype);
+  if (rc) return rc;
+  if (bh == 0 || n == 0) return SA_OK;
+  if (!out) return set_error(SA_ERR_INVALID_ARG, "null output pointer");
+  const Workspace w = plan(bh, n, d, dv, degree, block_size, SA_COMPRESSOR_NONE, Plan::kSegment, compress_stride);
+  rc = check_workspace(w, workspace, workspace_bytes);
+  if (rc) return rc;
+  char* ws = static_cast<char*>(workspace);
+  float* low = reinterpret_cast<float*>(ws + w.low);
+  int* status = reinterpret_cast<int*>(ws + w.status);
+  cudaStream_t s = (cudaStream_t)stream;
+  rc = reset_status(status, s);
+  if (rc) return rc;
+  const bool reps = w.R > 0;
+  const int64_t m_blk = compress_stride > 1 ? block_size / compress_stride : block_size;
+
+  float* khi = reinterpret_cast<float*>(ws + w.khi);
+  float* klo = reinterpret_cast<float*>(ws + w.klo);
+  float* vthi = reinterpret_cast<float*>(ws + w.vthi);
+  float* vtlo = reinterpret_cast<float*>(ws + w.vtlo);
+  if (w.tc) {
+    rc = launch_split(k, bh * n, d, w.dp, khi, klo, s);
+    if (rc) return rc;
+  }
+  if (w.tc || w.groups > 0) {
+    rc = launch_split_t(v, bh, n, dv, w.dvp, w.n_pad, vthi, vtlo, s);
+    if (rc) return rc;
+  }
+
+  // reps: the segment means of the completed blocks, weight compress_stride
+  float* rep_k = reinterpret_cast<float*>(ws + w.rep_k);
+  float* rep_v = reinterpret_cast<float*>(ws + w.rep_v);
+  float* rw = reinterpret_cast<float*>(ws + w.rep_w);
+  const TCOperands cur_ops{khi, klo, n, vthi, vtlo, n, w.n_pad};
+  TCOperands rep_ops = cur_ops;
+  if (reps) {
+    rc = launch_segment_mean(k, v, bh, n, d, dv, block_size, compress_stride, key_dtype, value_dtype, rep_k, rep_v,
+                             s);
+    if (!rc) rc = launch_fill(rw, bh * (w.tc ? w.r_pad : w.R), (float)compress_stride, s);
+    if (rc) return rc;
+    if (w.tc) {
+      float* r[4] = {reinterpret_cast<float*>(ws + w.rkhi), reinterpret_cast<float*>(ws + w.rklo),
+                     reinterpret_cast<float*>(ws + w.rvthi), reinterpret_cast<float*>(ws + w.rvtlo)};
+      rc = launch_split(rep_k, bh * w.R, d, w.dp, r[0], r[1], s);
+      if (!rc) rc = launch_split_t(rep_v, bh, w.R, dv, w.dvp, w.r_pad, r[2], r[3], s);
+      if (rc) return rc;
+      rep_ops = TCOperands{r[0], r[1], w.R, r[2], r[3], w.R, w.r_pad};
+    }
+  }
+
+  // low-degree moments
+  if (w.groups > 0)
+    rc = moments_tc_from_split(w, ws, vthi, vtlo, q, k, low, status, bh, n, d, dv, degree, block_size, scale, s);
+  else
+    rc = launch_low_moments(q, k, v, bh, n, d, dv, degree, block_size, scale, low, s);
+  if (rc) return rc;
+  const int groups = w.groups > 0 ? w.groups : 1;
+
+  // residual + combine
+  if (w.tc)
+    return residual_tc_from_split(w, rep_ops, cur_ops, reps ? rw : nullptr, q, low, groups, out, status, bh, n, d,
+                                  dv, degree, block_size, m_blk, scale, eps, s, 0, true);
+  if (groups > 1) {
+    rc = launch_sum_groups(low, groups, bh * n * (dv + 1), low, s);
+    if (rc) return rc;
+  }
+  return launch_residual_reps(q, k, v, reps ? rep_k : k, reps ? rep_v : v, reps ? rw : nullptr, low, bh, n, d, dv,
+                              degree, block_size, m_blk, reps ? w.R : n, scale, eps, true, out, s);
 }
 
 }  // extern "C"

@@ -30,7 +30,7 @@ __global__ void __launch_bounds__(kResThreads)
 residual_kernel(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
                 const float* __restrict__ rk, const float* __restrict__ rv, const float* __restrict__ rw,
                 const float* __restrict__ low, int64_t n, int d, int dv, int degree, int bs, int64_t m_blk,
-                int64_t reps_per_head, float scale, float eps, float* __restrict__ out) {
+                int64_t reps_per_head, float scale, float eps, bool clamp, float* __restrict__ out) {
   constexpr int CPT = DVP / 4;
   extern __shared__ float4 res_smem4[];
   // layout: Kt [DP][kTK+4] | Vs [kTK][DVP] | Qs [kTQ][DP+1] | E [kTQ][kTK+1] | Ws [kTK]
@@ -103,7 +103,7 @@ residual_kernel(const float* __restrict__ q, const float* __restrict__ k, const 
       float e = 0.0f;
       if (valid && rl < tk && r < lim) {
         const float xs = x[rr] * scale;
-        e = Ws[rl] * (expf(xs) - taylor_poly(xs, degree));
+        e = Ws[rl] * (expf(clamp ? fminf(xs, 80.0f) : xs) - taylor_poly(xs, degree));
       }
       E[qi][rl] = e;
     }
@@ -161,7 +161,10 @@ residual_kernel(const float* __restrict__ q, const float* __restrict__ k, const 
       const int rl = cg * 8 + rr;
       const int64_t j = j0 + rl;
       float e = 0.0f;
-      if (valid && rl < tk && j <= i && j >= my_b0) e = expf(x[rr] * scale);
+      if (valid && rl < tk && j <= i && j >= my_b0) {
+        const float xs = x[rr] * scale;
+        e = expf(clamp ? fminf(xs, 80.0f) : xs);
+      }
       E[qi][rl] = e;
     }
     __syncthreads();
@@ -197,42 +200,52 @@ residual_kernel(const float* __restrict__ q, const float* __restrict__ k, const 
 template <int DP, int DVP>
 int launch_dp(const float* q, const float* k, const float* v, const float* rk, const float* rv, const float* rw,
               const float* low, int64_t bh, int64_t n, int d, int dv, int degree, int bs, int64_t m_blk,
-              int64_t reps_per_head, float scale, float eps, float* out, cudaStream_t stream) {
+              int64_t reps_per_head, float scale, float eps, bool clamp, float* out, cudaStream_t stream) {
   dim3 grid((unsigned)ceil_div(n, kTQ), (unsigned)bh);
   const size_t smem = sizeof(float) * ((size_t)DP * (kTK + 4) + (size_t)kTK * DVP + (size_t)kTQ * (DP + 1) +
                                        (size_t)kTQ * (kTK + 1) + kTK);
   cudaFuncSetAttribute(residual_kernel<DP, DVP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   residual_kernel<DP, DVP><<<grid, kResThreads, smem, stream>>>(q, k, v, rk, rv, rw, low, n, d, dv, degree, bs, m_blk,
-                                                             reps_per_head, scale, eps, out);
+                                                             reps_per_head, scale, eps, clamp, out);
   return check_launch("residual_kernel");
 }
 
 template <int DP>
 int launch_dv(const float* q, const float* k, const float* v, const float* rk, const float* rv, const float* rw,
               const float* low, int64_t bh, int64_t n, int d, int dv, int degree, int bs, int64_t m_blk,
-              int64_t rph, float scale, float eps, float* out, cudaStream_t s) {
-  if (dv <= 16) return launch_dp<DP, 16>(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, out, s);
-  if (dv <= 32) return launch_dp<DP, 32>(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, out, s);
-  if (dv <= 64) return launch_dp<DP, 64>(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, out, s);
-  return launch_dp<DP, 128>(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, out, s);
+              int64_t rph, float scale, float eps, bool clamp, float* out, cudaStream_t s) {
+  if (dv <= 16) return launch_dp<DP, 16>(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, clamp, out, s);
+  if (dv <= 32) return launch_dp<DP, 32>(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, clamp, out, s);
+  if (dv <= 64) return launch_dp<DP, 64>(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, clamp, out, s);
+  return launch_dp<DP, 128>(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, clamp, out, s);
 }
 
 }  // namespace
 
-int launch_residual(const float* q, const float* k, const float* v, const float* rk, const float* rv,
-                    const float* rw, const float* low, int64_t bh, int64_t n, int d, int dv, int degree, int bs,
-                    int compressor, float scale, float eps, float* out, cudaStream_t s) {
+// Reps of m_blk per completed block (rows r of head h at rk + (h * rph + r) * d;
+// rph = rows per head); clamp caps the exp argument at 80 (the segment-mean
+// variant, triton_article_attention.py:331-333).
+int launch_residual_reps(const float* q, const float* k, const float* v, const float* rk, const float* rv,
+                         const float* rw, const float* low, int64_t bh, int64_t n, int d, int dv, int degree, int bs,
+                         int64_t m_blk, int64_t rph, float scale, float eps, bool clamp, float* out, cudaStream_t s) {
   if (bh == 0 || n == 0) return SA_OK;
   if (d > 128 || dv > 128) return set_error(SA_ERR_UNSUPPORTED, "dim and value_dim above 128 are not supported");
   if (bh > 65535) return set_error(SA_ERR_UNSUPPORTED, "more than 65535 heads in one launch");
-  const int64_t nc = (n - 1) / bs;
+  if (d <= 16) return launch_dv<16>(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, clamp, out, s);
+  if (d <= 32) return launch_dv<32>(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, clamp, out, s);
+  if (d <= 64) return launch_dv<64>(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, clamp, out, s);
+  return launch_dv<128>(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, clamp, out, s);
+}
+
+int launch_residual(const float* q, const float* k, const float* v, const float* rk, const float* rv,
+                    const float* rw, const float* low, int64_t bh, int64_t n, int d, int dv, int degree, int bs,
+                    int compressor, float scale, float eps, float* out, cudaStream_t s) {
+  const int64_t nc = n > 0 ? (n - 1) / bs : 0;
   const int64_t m_blk = (compressor == SA_COMPRESSOR_NONE) ? bs : (bs + 1) / 2;
   // compressor none reads the keys themselves: n rows per head
   const int64_t rph = (compressor == SA_COMPRESSOR_NONE) ? n : nc * m_blk;
-  if (d <= 16) return launch_dv<16>(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, out, s);
-  if (d <= 32) return launch_dv<32>(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, out, s);
-  if (d <= 64) return launch_dv<64>(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, out, s);
-  return launch_dv<128>(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, out, s);
+  return launch_residual_reps(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, bs, m_blk, rph, scale, eps, false, out,
+                              s);
 }
 
 }  // namespace sa

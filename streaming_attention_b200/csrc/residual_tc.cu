@@ -117,7 +117,14 @@ __device__ __forceinline__ float taylor_fma(float x) {
   return fmaf(fmaf(fmaf(x, 1.0f / 6.0f, 0.5f), x, 1.0f), x, 1.0f);
 }
 
-template <int DP, int DVP, int DEG>
+// exp of a score; CLAMP caps its argument at 80 (the segment-mean variant,
+// triton_article_attention.py:331-333 and :359, keeps e^x finite in fp32 there)
+template <bool CLAMP>
+__device__ __forceinline__ float exp_score(float x) {
+  return __expf(CLAMP ? fminf(x, 80.0f) : x);
+}
+
+template <int DP, int DVP, int DEG, bool CLAMP>
 __global__ void __launch_bounds__(kThreads, 1)
 residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_constant__ CUtensorMap tm_rkl,
                    const __grid_constant__ CUtensorMap tm_rvh, const __grid_constant__ CUtensorMap tm_rvl,
@@ -358,7 +365,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
             for (int u = 0; u < 4; ++u) {
               const int j = 4 * j4 + u;
               const float x = sv[j];
-              float e = (__expf(x) - taylor_fma<DEG>(x)) * ww[u];
+              float e = (exp_score<CLAMP>(x) - taylor_fma<DEG>(x)) * ww[u];
               if (!all_on && col0 + j >= lim) e = 0.0f;
               den += e;
               hi[j] = to_tf32(e);
@@ -369,7 +376,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const float x = sv[j];
-            float e = __expf(x) - taylor_fma<DEG>(x);
+            float e = exp_score<CLAMP>(x) - taylor_fma<DEG>(x);
             if (!all_on && col0 + j >= lim) e = 0.0f;
             den += e;
             hi[j] = to_tf32(e);
@@ -381,7 +388,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const int64_t key = col0 + j;
-          float e = __expf(sv[j]);
+          float e = exp_score<CLAMP>(sv[j]);
           if (!all_on && (key > i || key < bst)) e = 0.0f;
           den += e;
           hi[j] = to_tf32(e);
@@ -444,10 +451,10 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
   }
 }
 
-template <int DP, int DVP, int DEG>
+template <int DP, int DVP, int DEG, bool CLAMP = false>
 int launch_tc(const CUtensorMap* maps, const ResTCParams& prm, int64_t bh, cudaStream_t stream) {
   using L = Layout<DP, DVP>;
-  auto kern = residual_tc_kernel<DP, DVP, DEG>;
+  auto kern = residual_tc_kernel<DP, DVP, DEG, CLAMP>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kSmemBytes);
   if (e != cudaSuccess) return set_error(SA_ERR_CUDA, "residual_tc smem attribute: %s", cudaGetErrorString(e));
   dim3 grid((unsigned)((prm.n + kRowsQ - 1) / kRowsQ), (unsigned)bh);
@@ -457,7 +464,16 @@ int launch_tc(const CUtensorMap* maps, const ResTCParams& prm, int64_t bh, cudaS
 }
 
 template <int DP, int DVP>
-int launch_deg(int degree, const CUtensorMap* maps, const ResTCParams& prm, int64_t bh, cudaStream_t s) {
+int launch_deg(int degree, const CUtensorMap* maps, const ResTCParams& prm, int64_t bh, cudaStream_t s,
+               bool clamp_exp) {
+  if (clamp_exp) {  // the segment-mean variant: degree 0, 1 or 2
+    switch (degree) {
+      case 0: return launch_tc<DP, DVP, 0, true>(maps, prm, bh, s);
+      case 1: return launch_tc<DP, DVP, 1, true>(maps, prm, bh, s);
+      case 2: return launch_tc<DP, DVP, 2, true>(maps, prm, bh, s);
+      default: return set_error(SA_ERR_UNSUPPORTED, "the clamped residual supports degree 0, 1 or 2");
+    }
+  }
   switch (degree) {
     case 0: return launch_tc<DP, DVP, 0>(maps, prm, bh, s);
     case 1: return launch_tc<DP, DVP, 1>(maps, prm, bh, s);
@@ -475,19 +491,20 @@ int residual_tc_dvp(int dv) { return dv <= 32 ? 32 : (dv <= 64 ? 64 : (dv <= 128
 // maps: rep_k_hi, rep_k_lo, rep_v_hi, rep_v_lo, k_hi, k_lo, v_hi, v_lo (3-D, box {32, 64, 1}).
 int launch_residual_tc(const CUtensorMap* maps, const float* q, const float* rep_w, int64_t r_pad, const float* low,
                        int groups, float* out, int* status, int64_t bh, int64_t n, int d, int dv, int degree, int bs,
-                       int64_t m_blk, float scale, float eps, cudaStream_t stream, int64_t c_off) {
+                       int64_t m_blk, float scale, float eps, cudaStream_t stream, int64_t c_off,
+                       bool clamp_exp) {
   if (bh == 0 || n == 0) return SA_OK;
   if (bh > 65535 || (n + kRowsQ - 1) / kRowsQ > 2147483647LL)
     return set_error(SA_ERR_UNSUPPORTED, "grid too large for the tensor-core residual");
   ResTCParams prm{q, rep_w, low, out, status, n, m_blk, r_pad, d, dv, bs, scale, eps, groups, bh * n * (dv + 1),
                   c_off};
   const int dp = residual_tc_dp(d), dvp = residual_tc_dvp(dv);
-  if (dp == 32 && dvp == 32) return launch_deg<32, 32>(degree, maps, prm, bh, stream);
-  if (dp == 32 && dvp == 64) return launch_deg<32, 64>(degree, maps, prm, bh, stream);
-  if (dp == 32 && dvp == 128) return launch_deg<32, 128>(degree, maps, prm, bh, stream);
-  if (dp == 64 && dvp == 32) return launch_deg<64, 32>(degree, maps, prm, bh, stream);
-  if (dp == 64 && dvp == 64) return launch_deg<64, 64>(degree, maps, prm, bh, stream);
-  if (dp == 64 && dvp == 128) return launch_deg<64, 128>(degree, maps, prm, bh, stream);
+  if (dp == 32 && dvp == 32) return launch_deg<32, 32>(degree, maps, prm, bh, stream, clamp_exp);
+  if (dp == 32 && dvp == 64) return launch_deg<32, 64>(degree, maps, prm, bh, stream, clamp_exp);
+  if (dp == 32 && dvp == 128) return launch_deg<32, 128>(degree, maps, prm, bh, stream, clamp_exp);
+  if (dp == 64 && dvp == 32) return launch_deg<64, 32>(degree, maps, prm, bh, stream, clamp_exp);
+  if (dp == 64 && dvp == 64) return launch_deg<64, 64>(degree, maps, prm, bh, stream, clamp_exp);
+  if (dp == 64 && dvp == 128) return launch_deg<64, 128>(degree, maps, prm, bh, stream, clamp_exp);
   return set_error(SA_ERR_UNSUPPORTED, "tensor-core residual: d=%d dv=%d not supported", d, dv);
 }
 

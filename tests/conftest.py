@@ -33,7 +33,12 @@ def load_golden(name):
 
 def golden_names():
     return sorted(f[:-4] for f in os.listdir(GOLDEN)
-                  if f.endswith(".npz") and f not in ("misc.npz",) and not f.startswith("stream_"))
+                  if f.endswith(".npz") and f not in ("misc.npz",) and not f.startswith(("stream_", "segment_")))
+
+
+def segment_golden_names():
+    """Fixtures of the segment-mean variant (reference reps, exact attention at stride 1)."""
+    return sorted(f[:-4] for f in os.listdir(GOLDEN) if f.startswith("segment_") and f.endswith(".npz"))
 
 
 def stream_golden_names():

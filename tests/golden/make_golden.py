@@ -12,7 +12,10 @@ reference's outputs:
   ``_build_completed_block_reps`` (fast_article_attention.py:365-434) against
   the block's own key rows (keys are continuous random draws, so an exact row
   match is unambiguous),
-* the representative weights, and the ``FastArticleStats`` fields.
+* the representative weights, and the ``FastArticleStats`` fields;
+* for the segment-mean variant (triton_article_attention.py), the reps of
+  ``build_segment_mean_coreset`` and, at compress_stride 1, the exact
+  attention it reduces to (``segment_*.npz``).
 
 Degree 3 is outside the reference fast path (``num_taylor_features`` raises at
 fast_article_attention.py:141-142).  For degree 3 the fixture is composed from
@@ -315,13 +318,59 @@ def make_streaming(fa, st):
         np.savez_compressed(os.path.join(HERE, name + ".npz"), **out[name])
 
 
+SEGMENT_CASES = [
+    # name, (B, H) or None for 2-D, n, d, dv, block_size, compress_stride, key/value dtype
+    ("segment_stride2", (1, 2), 300, 16, 8, 32, 2, "float32"),
+    ("segment_stride4_ragged", None, 257, 24, 12, 16, 4, "float32"),
+    ("segment_stride1_exact", (2, 1), 200, 8, 5, 32, 1, "float32"),
+    ("segment_stride3", None, 200, 12, 6, 48, 3, "float32"),
+    ("segment_one_rep_per_block", None, 129, 8, 4, 16, 16, "float32"),
+    ("segment_no_completed_block", None, 64, 8, 4, 64, 8, "float32"),
+    ("segment_float16", (1, 2), 160, 16, 8, 32, 2, "float16"),
+    ("segment_bfloat16", None, 140, 16, 16, 16, 4, "bfloat16"),
+]
+
+
+def make_segment(path: str):
+    """The segment-mean variant (triton_article_attention.py): the reps of
+    ``build_segment_mean_coreset`` (:190-245, plain torch, run here on the CPU)
+    and, for compress_stride 1, the exact attention of
+    ``torch_classical_causal_attention`` (:123-143), which the variant matches
+    up to roundoff (its docstring, :472-474).  The Triton kernel itself needs
+    a GPU and Triton; its arithmetic is restated in the oracle."""
+    sys.path.insert(0, path)
+    tr = importlib.import_module("triton_article_attention")
+    for name, bhs, n, d, dv, bs, stride, dt in SEGMENT_CASES:
+        g = torch.Generator().manual_seed(1234 + n)
+        shape = (bhs[0], bhs[1]) if bhs else ()
+        q = torch.randn(*shape, n, d, generator=g) * 0.6
+        k = torch.randn(*shape, n, d, generator=g) * 0.6
+        v = torch.randn(*shape, n, dv, generator=g)
+        dtype = getattr(torch, dt)
+        q, k, v = q.to(dtype), k.to(dtype), v.to(dtype)
+        k3, v3 = (k.reshape(-1, n, d), v.reshape(-1, n, dv))
+        rk, rv, m = tr.build_segment_mean_coreset(k3, v3, block_size=bs, compress_stride=stride)
+        rec = dict(q=q.float().numpy(), k=k.float().numpy(), v=v.float().numpy(), rep_k=rk.float().numpy(),
+                   rep_v=rv.float().numpy(), reps_per_block=np.asarray(m))
+        if stride == 1:
+            rec["exact"] = tr.torch_classical_causal_attention(q.double(), k.double(), v.double()).numpy()
+        rec["meta"] = np.frombuffer(json.dumps(dict(n=n, d=d, dv=dv, bs=bs, stride=stride, dtype=dt,
+                                                    batched=bhs is not None)).encode(), dtype=np.uint8)
+        np.savez_compressed(os.path.join(HERE, name + ".npz"), **rec)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
     ap.add_argument("--only", default=None)
     ap.add_argument("--streaming-only", action="store_true")
+    ap.add_argument("--segment-only", action="store_true")
     args = ap.parse_args()
     torch.set_num_threads(1)
+    if args.segment_only:
+        make_segment(args.reference)
+        print("wrote segment")
+        return
     fa, st = _load_reference(args.reference)
     if args.streaming_only:
         make_streaming(fa, st)
@@ -335,7 +384,8 @@ def main() -> None:
     if not args.only:
         make_misc(fa, st)
         make_streaming(fa, st)
-        print("wrote misc, streaming")
+        make_segment(args.reference)
+        print("wrote misc, streaming, segment")
 
 
 if __name__ == "__main__":

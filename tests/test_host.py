@@ -108,3 +108,17 @@ def test_streaming_class_checks_arguments_like_the_reference():
         ArticleStreamingAttention(4, 4, dtype="int8")
     with pytest.raises(NotImplementedError):
         ArticleStreamingAttention(4, 4, degree=4)
+
+
+def test_bench_csv_columns_and_inputs_match_the_reference_benchmark():
+    """benchmark_attention.py's CSV header (:205-229) and make_data (:70-101)."""
+    from streaming_attention_b200 import bench_csv
+    header = ("n,d,dv,degree,block_size,compressor,data,radius,scale,device,dtype,rel_l2,max_abs,mean_abs,"
+              "classical_median_ms,classical_best_ms,article_median_ms,article_best_ms,article_final_state_bytes,"
+              "article_max_state_bytes,article_max_coreset_items,classical_kv_bytes,classical_naive_scores_bytes")
+    assert ",".join(bench_csv.COLUMNS) == header
+    # the config 1 fixture was drawn by the reference's make-data with the same generator calls
+    g = load_golden("cfg1_full")
+    q, k, v = bench_csv.make_data(1024, 32, 32, radius=1.0, data="unit_ball", seed=0)
+    np.testing.assert_array_equal(q.numpy(), g["q"].reshape(1024, 32))
+    np.testing.assert_array_equal(v.numpy(), g["v"].reshape(1024, 32))

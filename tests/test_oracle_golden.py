@@ -10,7 +10,7 @@ import json
 import numpy as np
 import pytest
 
-from conftest import golden_names, load_golden, stream_golden_names
+from conftest import golden_names, load_golden, segment_golden_names, stream_golden_names
 from oracle import oracle as O
 
 
@@ -130,3 +130,73 @@ def test_streaming_oracle_matches_reference_fixture(name):
 def test_streaming_oracle_rejects_small_blocks():
     with pytest.raises(ValueError, match="block_size must be at least 2"):
         O.stream_attention(np.zeros((3, 2)), np.zeros((3, 2)), np.zeros((3, 1)), block_size=1)
+
+
+# ---- the segment-mean variant (triton_article_attention.py) ----
+
+def _as_dtype(x, name):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(x)).to(getattr(torch, name)).float().numpy()
+
+
+def _rep_tolerance(x, dtype_name, stride):
+    """The rounding bound of a float32 sum of `stride` terms (stride - 1 units
+    in the last place of the largest |x|: the reference's mean sums in torch's
+    order, the kernel in token order), plus one unit of the storage dtype for
+    float16 / bfloat16 (the mean is rounded once more)."""
+    big = float(np.abs(x).max()) if x.size else 1.0
+    e = np.floor(np.log2(max(big, 1e-30)))
+    tol = max(1, stride - 1) * 2.0 ** (e - 23)
+    if dtype_name != "float32":
+        tol += 2.0 ** (e - {"float16": 10, "bfloat16": 7}[dtype_name])
+    return tol
+
+
+@pytest.mark.parametrize("name", segment_golden_names())
+def test_segment_oracle_reps_match_reference_fixture(name):
+    g = load_golden(name)
+    m = g["meta"]
+    k = g["k"].reshape(-1, m["n"], m["d"])
+    v = g["v"].reshape(-1, m["n"], m["dv"])
+    for h in range(k.shape[0]):
+        rk, rv, mm = O.segment_mean_reps(k[h], v[h], m["bs"], m["stride"])
+        assert mm == int(g["reps_per_block"])
+        rk, rv = _as_dtype(rk, m["dtype"]), _as_dtype(rv, m["dtype"])
+        assert rk.shape == g["rep_k"][h].shape and rv.shape == g["rep_v"][h].shape
+        for got, want in ((rk, g["rep_k"][h]), (rv, g["rep_v"][h])):
+            np.testing.assert_allclose(got, want, rtol=0, atol=_rep_tolerance(want, m["dtype"], m["stride"]))
+
+
+def test_segment_oracle_stride1_is_the_reference_exact_attention():
+    g = load_golden("segment_stride1_exact")
+    m = g["meta"]
+    q, k, v = (g[x].reshape(-1, m["n"], g[x].shape[-1]) for x in "qkv")
+    exact = g["exact"].reshape(-1, m["n"], m["dv"])
+    for h in range(q.shape[0]):
+        for degree in (0, 1, 2):
+            out = O.segment_mean_attention(q[h], k[h], v[h], degree=degree, block_size=m["bs"], compress_stride=1)
+            assert O.relative_l2(out, exact[h]) < 1e-12
+
+
+def test_segment_oracle_rejects_what_the_reference_rejects():
+    x = np.zeros((8, 2), np.float32)
+    with pytest.raises(ValueError, match="divisible by compress_stride"):
+        O.segment_mean_reps(x, x, 6, 4)
+    with pytest.raises(ValueError, match="must be positive"):
+        O.segment_mean_reps(x, x, 4, 0)
+    with pytest.raises(NotImplementedError):
+        O.segment_mean_attention(x, x, x, degree=3, block_size=4, compress_stride=2)
+
+
+def test_segment_oracle_caps_the_exp_argument_at_80():
+    """Scores above 80 count as exactly e^80 in both residual parts."""
+    q = np.array([[10.0], [10.0], [10.0]], np.float32)
+    k = np.array([[9.0], [9.5], [1.0]], np.float32)
+    v = np.array([[1.0], [2.0], [3.0]], np.float32)
+    out = O.segment_mean_attention(q, k, v, degree=0, block_size=2, compress_stride=2, scale=1.0)
+    # query 2 sees the mean rep of tokens 0, 1 (key 9.25, score 92.5 -> e^80,
+    # weight 2) and its own key (score 10)
+    w_rep, w_own = 2 * np.exp(80.0), np.exp(10.0)
+    assert np.isclose(out[2, 0], (w_rep * 1.5 + w_own * 3.0) / (w_rep + w_own), rtol=1e-12)
+    # query 1: two scores of 90 and 95 in its own block, both capped
+    assert np.isclose(out[1, 0], 1.5, rtol=1e-12)
