@@ -259,6 +259,19 @@ int sa_article_segment_mean(const float* q, const float* k, const float* v, int6
                             void* workspace,
                             size_t workspace_bytes, void* stream);
 
+/* ---- exact causal softmax attention ----------------------------------------
+ * Replaces triton_flash_causal_attention (triton_article_attention.py:580-637)
+ * and its kernel _flash_causal_kernel (:372-435): out = softmax(scale q k^T,
+ * causal) v with the running-maximum (online) softmax and
+ * out = acc / max(l, 1e-20).  d <= 128, dv <= 256 (else SA_ERR_INVALID_ARG).
+ * Tensor cores (3xTF32) for d <= 64 and dv <= 128 with a workspace of
+ * sa_flash_causal_attention_workspace_size bytes (256-byte aligned); CUDA
+ * cores otherwise (workspace size 0, may be NULL). */
+int sa_flash_causal_attention_workspace_size(int64_t bh, int64_t n, int d, int dv, size_t* bytes);
+int sa_flash_causal_attention(const float* q, const float* k, const float* v, int64_t bh, int64_t n,
+                              int d, int dv, float scale, float* out, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -27,6 +27,7 @@ from .segment import (  # noqa: F401
     build_segment_mean_coreset,
     torch_classical_causal_attention,
     triton_article_causal_attention,
+    triton_flash_causal_attention,
 )
 
 __version__ = "0.1.0"

@@ -58,6 +58,8 @@ SIGNATURES = {
     "sa_stream_query_workspace_size": [_i32, _i32, _i32, ctypes.POINTER(_sz)],
     "sa_segment_mean_reps": [_vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp],
     "sa_article_segment_mean_workspace_size": [_i64, _i64, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(_sz)],
+    "sa_flash_causal_attention_workspace_size": [_i64, _i64, _i32, _i32, ctypes.POINTER(_sz)],
+    "sa_flash_causal_attention": [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _f32, _vp, _vp, _sz, _vp],
     "sa_article_segment_mean": [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _f32,
                                 _vp, _vp, _sz, _vp],
     "sa_stream_query": [_vp, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _i64, _f32, _vp, _vp,

@@ -55,6 +55,10 @@ int launch_residual_reps(const float* q, const float* k, const float* v, const f
 int launch_segment_mean(const float* k, const float* v, int64_t bh, int64_t n, int d, int dv, int bs, int stride,
                         int key_dtype, int value_dtype, float* rep_k, float* rep_v, cudaStream_t s);
 int launch_fill(float* dst, int64_t count, float value, cudaStream_t s);
+int launch_flash_tc(const CUtensorMap* maps, const float* q, float* out, int* status, int64_t bh, int64_t n, int d,
+                    int dv, float scale, cudaStream_t stream);
+int launch_flash_simt(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d, int dv,
+                      float scale, float* out, cudaStream_t s);
 
 namespace {
 thread_local char g_err[512] = {0};
@@ -335,6 +339,42 @@ int check_segment(const void* q, const void* k, const void* v, int64_t bh, int64
   for (const int t : {key_dtype, value_dtype})
     if (t < SA_REP_FLOAT32 || t > SA_REP_BFLOAT16)
       return set_error(SA_ERR_INVALID_ARG, "rep dtypes must be SA_REP_FLOAT32, SA_REP_FLOAT16 or SA_REP_BFLOAT16");
+  return SA_OK;
+}
+
+// Workspace of the exact flash kernel: the status word and the tf32 splits of
+// k ([bh, n, dp]) and of v transposed ([bh, dvp, n_pad]); empty on the
+// CUDA-core path (d > 64, dv > 128, or SA_FORCE_SIMT=1).
+Workspace plan_flash(int64_t bh, int64_t n, int d, int dv) {
+  Workspace w{};
+  w.dp = residual_tc_dp(d);
+  w.dvp = residual_tc_dvp(dv);
+  w.tc = w.dp > 0 && w.dvp > 0 && !force_simt();
+  if (!w.tc) return w;
+  w.n_pad = (n + 3) / 4 * 4;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align_up(off + bytes);
+    return at;
+  };
+  const size_t f = sizeof(float);
+  w.status = take(sizeof(int));
+  w.khi = take((size_t)bh * n * w.dp * f);
+  w.klo = take((size_t)bh * n * w.dp * f);
+  w.vthi = take((size_t)bh * w.dvp * w.n_pad * f);
+  w.vtlo = take((size_t)bh * w.dvp * w.n_pad * f);
+  w.total = off;
+  return w;
+}
+
+int check_flash(const void* q, const void* k, const void* v, int64_t bh, int64_t n, int d, int dv) {
+  if (bh < 0 || n < 0) return set_error(SA_ERR_INVALID_ARG, "bh and n must be non-negative");
+  if (d <= 0 || dv <= 0) return set_error(SA_ERR_INVALID_ARG, "dim and value_dim must be positive");
+  if (d > 128) return set_error(SA_ERR_INVALID_ARG, "this compact kernel supports D <= 128");
+  if (dv > 256) return set_error(SA_ERR_INVALID_ARG, "this compact kernel supports Dv <= 256");
+  if (bh > 0 && n > 0 && (!q || !k || !v)) return set_error(SA_ERR_INVALID_ARG, "null input pointer");
+  if (n > ((int64_t)1 << 31)) return set_error(SA_ERR_UNSUPPORTED, "sequence length above 2^31");
   return SA_OK;
 }
 
@@ -835,6 +875,48 @@ int sa_article_segment_mean(const float* q, const float* k, const float* v, int6
   }
   return launch_residual_reps(q, k, v, reps ? rep_k : k, reps ? rep_v : v, reps ? rw : nullptr, low, bh, n, d, dv,
                               degree, block_size, m_blk, reps ? w.R : n, scale, eps, true, out, s);
+}
+
+/* ---- exact causal attention (triton_article_attention.py:372-435, :580-637) ---- */
+
+int sa_flash_causal_attention_workspace_size(int64_t bh, int64_t n, int d, int dv, size_t* bytes) {
+  if (!bytes) return set_error(SA_ERR_INVALID_ARG, "null output pointer");
+  const int rc = check_flash(nullptr, nullptr, nullptr, 0, n, d, dv);
+  if (rc) return rc;
+  if (bh < 0) return set_error(SA_ERR_INVALID_ARG, "bh must be non-negative");
+  *bytes = plan_flash(bh, n, d, dv).total;
+  return SA_OK;
+}
+
+int sa_flash_causal_attention(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d, int dv,
+                              float scale, float* out, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_flash(q, k, v, bh, n, d, dv);
+  if (rc) return rc;
+  if (bh == 0 || n == 0) return SA_OK;
+  if (!out) return set_error(SA_ERR_INVALID_ARG, "null output pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  const Workspace w = plan_flash(bh, n, d, dv);
+  if (!w.tc) return launch_flash_simt(q, k, v, bh, n, d, dv, scale, out, s);
+  rc = check_workspace(w, workspace, workspace_bytes);
+  if (rc) return rc;
+  char* ws = static_cast<char*>(workspace);
+  int* status = reinterpret_cast<int*>(ws + w.status);
+  rc = reset_status(status, s);
+  if (rc) return rc;
+  float* khi = reinterpret_cast<float*>(ws + w.khi);
+  float* klo = reinterpret_cast<float*>(ws + w.klo);
+  float* vthi = reinterpret_cast<float*>(ws + w.vthi);
+  float* vtlo = reinterpret_cast<float*>(ws + w.vtlo);
+  rc = launch_split(k, bh * n, d, w.dp, khi, klo, s);
+  if (!rc) rc = launch_split_t(v, bh, n, dv, w.dvp, w.n_pad, vthi, vtlo, s);
+  if (rc) return rc;
+  CUtensorMap maps[4];
+  rc = encode_map_3d(&maps[0], khi, w.dp, n, bh, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = encode_map_3d(&maps[1], klo, w.dp, n, bh, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = encode_map(&maps[2], vthi, n, w.n_pad, w.dvp, bh, w.dvp, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = encode_map(&maps[3], vtlo, n, w.n_pad, w.dvp, bh, w.dvp, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  return launch_flash_tc(maps, q, out, status, bh, n, d, dv, scale, s);
 }
 
 }  // extern "C"

@@ -2,7 +2,8 @@
 
 Mirrors ``triton_article_attention.py`` of PositiveLoss/streaming-attention:
 ``triton_article_causal_attention``, ``build_segment_mean_coreset``,
-``TritonArticleStats`` and ``torch_classical_causal_attention`` keep the
+``TritonArticleStats``, ``triton_flash_causal_attention`` (exact causal
+attention, the comparator) and ``torch_classical_causal_attention`` keep the
 reference's names, keyword arguments, argument checks (order and messages),
 return types and stats fields.  The arithmetic runs in libsa_b200.so: the
 segment-mean kernel, then the same block-granular moment scan and tensor-core
@@ -29,7 +30,7 @@ from . import fast as _fast
 Tensor = torch.Tensor
 
 __all__ = ["TritonArticleStats", "build_segment_mean_coreset", "triton_article_causal_attention",
-           "torch_classical_causal_attention"]
+           "triton_flash_causal_attention", "torch_classical_causal_attention"]
 
 _MAX_VALUE_SLICE = 128
 
@@ -214,6 +215,42 @@ def triton_article_causal_attention(
         kv_bytes_per_sequence=int(n * (dim + dv) * elem_kv), score_matrix_bytes_per_sequence=int(n * n * elem_kv),
         output_bytes_per_sequence=int(n * dv * elem_out))
     return out, stats
+
+
+@torch.no_grad()
+def triton_flash_causal_attention(
+    q: Tensor, k: Tensor, v: Tensor, *, scale: Optional[float] = None, block_m: int = 16, block_n: int = 64,
+    value_block: Optional[int] = None, output_dtype: Optional[torch.dtype] = torch.float32,
+) -> Tensor:
+    """Exact causal softmax attention for [N,D] or [B,H,N,D] tensors on a CUDA
+    device (triton_article_attention.py:580-637): online softmax, fp32
+    accumulation, out = acc / max(l, 1e-20).  Runs on the tensor cores (3xTF32)
+    for D <= 64 and Dv <= 128, on the CUDA cores otherwise."""
+    _require_cuda(q, k, v)
+    q3, k3, v3, original_shape, had_bh = _flatten_bh_qkv(q, k, v)
+    bh, n, dim = q3.shape
+    dv = v3.shape[-1]
+    if dim > 128:
+        raise ValueError("this compact kernel supports D <= 128")
+    if dv > 256:
+        raise ValueError("this compact kernel supports Dv <= 256")
+    s = _attention_scale(scale, dim)
+    qf, kf, vf = (t.to(torch.float32).contiguous() for t in (q3, k3, v3))
+    dev = qf.device
+    out3 = torch.empty(bh, n, dv, device=dev, dtype=torch.float32)
+    if bh > 0 and n > 0:
+        lib = _lib.load()
+        nbytes = _lib.ctypes.c_size_t(0)
+        _lib.check(lib.sa_flash_causal_attention_workspace_size(bh, n, dim, dv, _lib.ctypes.byref(nbytes)),
+                   "sa_flash_causal_attention_workspace_size")
+        ws = torch.empty(max(int(nbytes.value), 256), device=dev, dtype=torch.uint8)
+        with torch.cuda.device(dev):
+            _lib.check(lib.sa_flash_causal_attention(
+                qf.data_ptr(), kf.data_ptr(), vf.data_ptr(), bh, n, dim, dv, float(s), out3.data_ptr(),
+                ws.data_ptr(), ws.numel(), torch.cuda.current_stream(dev).cuda_stream), "sa_flash_causal_attention")
+            if _fast._CHECK_STATUS and nbytes.value:
+                _fast.check_device_status(ws)
+    return _unflatten_output(out3.to(output_dtype or torch.float32), original_shape, had_bh)
 
 
 @torch.no_grad()
