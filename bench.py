@@ -54,6 +54,8 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-exact", action="store_true",
+                    help="skip the accuracy check against exact attention and the exact kernel's timing")
     ap.add_argument("--cpu-sample-heads", type=int, default=0, help="heads in the CPU sample (0 = auto)")
     ap.add_argument("--bh", type=int, default=0,
                     help="profiling only: replace B*H by this many sequences (B=1) to make a small case")
@@ -496,6 +498,37 @@ def run_ours(args, rank, world, dev):
                "h2d_bytes_per_step": int((hq.numel() + hk.numel() + hv.numel()) * 4 * world),
                "d2h_bytes_per_step": int(hout.numel() * 4 * world), "ms_per_step": e2e_ms / args.steps}
 
+    # the metric's accuracy part: the timed output against exact causal
+    # attention (this library's fp32-accurate flash kernel) on the same inputs,
+    # over every rank's heads; and that exact kernel timed on them as a comparator
+    accuracy = exact = None
+    if not args.no_exact:
+        st.fused(stream)
+        exact_out = sa.triton_flash_causal_attention(q3[None], k3[None], v3[None], scale=st.scale)[0]
+        sums = torch.stack([(st.out - exact_out).double().pow(2).sum(), exact_out.double().pow(2).sum(),
+                            (st.out - exact_out).abs().max().double()])
+        if world > 1:
+            torch.distributed.all_reduce(sums[:2])
+            torch.distributed.all_reduce(sums[2:], op=torch.distributed.ReduceOp.MAX)
+        accuracy = {"rel_l2_vs_exact": math.sqrt(float(sums[0]) / max(float(sums[1]), 1e-300)),
+                    "max_abs_vs_exact": float(sums[2]),
+                    "exact": "causal softmax attention, triton_flash_causal_attention (3xTF32 tensor cores)"}
+        del exact_out
+        for _ in range(2):
+            sa.triton_flash_causal_attention(q3[None], k3[None], v3[None], scale=st.scale)
+        barrier()
+        x0 = torch.cuda.Event(enable_timing=True)
+        x1 = torch.cuda.Event(enable_timing=True)
+        x_steps = max(1, min(args.steps, 5))
+        x0.record()
+        for _ in range(x_steps):
+            sa.triton_flash_causal_attention(q3[None], k3[None], v3[None], scale=st.scale)
+        x1.record()
+        barrier()
+        x_ms = reduce_max(x0.elapsed_time(x1), world, dev) / x_steps
+        exact = {"value": bh_total * c["N"] / (x_ms / 1e3), "unit": UNIT, "ms_per_step": x_ms, "steps": x_steps,
+                 "what": "exact causal attention on the same inputs (the comparator, not the headline)"}
+
     out = None
     if rank == 0:
         work = algorithmic_work(c)
@@ -549,7 +582,7 @@ def run_ours(args, rank, world, dev):
                        "compressor": c["compressor"], "parallelism": f"heads sharded over {world} GPU(s)",
                        "l2": "inputs larger than L2 (no flush needed)"},
             "roofline": roof, "kernels": kernels,
-            "e2e": e2e, "gpu_launches": st.launches * args.steps,
+            "e2e": e2e, "gpu_launches": st.launches * args.steps, "accuracy": accuracy, "exact_attention": exact,
             "clocks": clk.summary(), "fp32_fma_peak_tflops": fma_peak, "tf32_gemm_peak_tflops": tf32_peak,
         }
     return out, c

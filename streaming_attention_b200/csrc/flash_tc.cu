@@ -15,11 +15,19 @@
 // Online softmax with a lazily moved reference maximum.  Each row keeps m, the
 // maximum it subtracts; the pair of warps sharing a row agrees on the tile's
 // row maximum through shared memory.  m moves only when the tile maximum
-// exceeds it by more than kRescale (so every p = exp(x - m) <= e^kRescale):
-// then the row's O accumulator in TMEM (all products of earlier tiles, which
-// the warp first waits for) and its running sum are multiplied by
-// exp(m_old - m_new).  After the first tile that is rare, so the tensor-core
-// pipeline almost never waits on it.
+// exceeds it by more than kRescale (so every p <= 2^kRescale): then the row's
+// O accumulator in TMEM (all products of earlier tiles, which the warp first
+// waits for) and its running sum are multiplied by the factor of the move.
+// After the first tile that is rare, so the tensor-core pipeline almost never
+// waits on it.
+//
+// The tensor cores' fp32 accumulation in TMEM is not round-to-nearest, so O
+// is not carried in TMEM over the whole sequence: every kFold tiles the query
+// rows fold it (after its last product has landed) into an fp32 master in
+// registers (the row's columns of this half) with round-to-nearest adds, and
+// the next product restarts the TMEM chain.  The running sum l adds each tile's 32
+// values pairwise before the running add.  Scores are kept in base-2 units (the query is scaled by
+// scale * log2(e), as FlashAttention-2 does), so p = 2^(s - m) is one ex2.
 #include <math.h>
 
 #include "sa_common.cuh"
@@ -34,10 +42,18 @@ using namespace tc;
 constexpr int kRowsQ = 128;
 constexpr int kTile = 64;
 constexpr int kThreads = 320;
-constexpr float kRescale = 8.0f;
+constexpr float kRescale = 12.0f;   // base-2 units: p <= 4096
+constexpr int kFold = 16;           // key tiles per TMEM accumulation chain
 
 constexpr int kErrWaitQ = 301, kErrWaitFull = 302, kErrWaitSfree = 303, kErrWaitP = 304, kErrWaitS = 305,
               kErrWaitEmpty = 306, kErrWaitO = 307, kErrDrain = 308, kErrWaitPV = 309;
+
+// 2^x with the SFU's ex2 (relative error about 2^-22; 2^-inf = 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 struct FlashParams {
   const float* q;   // [bh, n, d]
@@ -177,7 +193,8 @@ flash_tc_kernel(const __grid_constant__ CUtensorMap tm_kh, const __grid_constant
       for (int kk = 0; kk < kTile / 8; ++kk) {
         const uint32_t vc = vt + (kk >> 2) * (2 * DVP * 128) + (kk & 3) * 32;
         const uint64_t bh_ = sdesc_sw128(vc, 16, 1024);
-        if (elect_one()) mma_tf32_ts(tmem + L::kO, ph + kk * 8, bh_, idesc_pv, (tp > 0 || kk > 0) ? 1u : 0u);
+        // the accumulator restarts after every fold (tiles tp % kFold == 0)
+        if (elect_one()) mma_tf32_ts(tmem + L::kO, ph + kk * 8, bh_, idesc_pv, (tp % kFold || kk > 0) ? 1u : 0u);
         if (L::kPVStack) {
           if (elect_one()) mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
         } else {
@@ -226,6 +243,7 @@ flash_tc_kernel(const __grid_constant__ CUtensorMap tm_kh, const __grid_constant
     const int64_t i = q0 + row;
     const bool valid = i < p.n;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    const float qscale = p.scale * 1.4426950408889634f;   // log2(e): scores in base 2
     {
       const float* qr = p.q + (h * p.n + (valid ? i : 0)) * p.d;
 #pragma unroll
@@ -235,7 +253,7 @@ flash_tc_kernel(const __grid_constant__ CUtensorMap tm_kh, const __grid_constant
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const int a = cchunk * 32 + j;
-          const float x = (valid && a < p.d) ? __ldg(qr + a) * p.scale : 0.0f;
+          const float x = (valid && a < p.d) ? __ldg(qr + a) * qscale : 0.0f;
           hi[j] = to_tf32(x);
           lo[j] = __float_as_uint(x - __uint_as_float(hi[j]));
         }
@@ -250,6 +268,13 @@ flash_tc_kernel(const __grid_constant__ CUtensorMap tm_kh, const __grid_constant
     // (for DVP = 32 the single chunk belongs to half 0)
     float m = -INFINITY;   // the maximum this row subtracts
     float l = 0.0f;        // this half's running sum of exp(x - m)
+    // the master: this half's 32-column chunks of the row (tiles before the last fold)
+    constexpr int kMine = DVP == 32 ? 1 : DVP / 64;
+    float master[kMine][32];
+#pragma unroll
+    for (int c = 0; c < kMine; ++c)
+#pragma unroll
+      for (int j = 0; j < 32; ++j) master[c][j] = 0.0f;
     bool ok = true;
     const uint32_t bar_id = 2 + quarter;   // named barrier of the warp pair
     // Waits are warp-uniform and a failed wait does not leave the loop: both
@@ -260,8 +285,10 @@ flash_tc_kernel(const __grid_constant__ CUtensorMap tm_kh, const __grid_constant
       if (ok && !mbar_wait_warp(&sfull[b], (t >> 1) & 1, ab, kErrWaitS)) ok = false;
       const uint32_t tS = lane_addr + L::kS0 + 128 * b + half * 32;
       const int64_t col0 = (int64_t)t * kTile + half * 32;
-      // causal mask: key col0 + j is visible to row i when col0 + j <= i
-      const bool all_on = valid && col0 + 31 <= i;
+      // causal mask: key col0 + j is visible to row i when j <= lim
+      const int64_t rel = i - col0;
+      const int lim = !valid || rel < 0 ? -1 : (rel > 31 ? 31 : (int)rel);
+      const bool all_on = lim >= 31;
       float sv[32];
       float pm = -INFINITY;
       if (ok) {
@@ -270,10 +297,18 @@ flash_tc_kernel(const __grid_constant__ CUtensorMap tm_kh, const __grid_constant
         tmem_ld32(tS, sv);
         tmem_ld32(tS + 64, s2);
         tmem_wait_ld();
+        if (all_on) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          sv[j] += s2[j];
-          if (all_on || (valid && col0 + j <= i)) pm = fmaxf(pm, sv[j]);
+          for (int j = 0; j < 32; ++j) {
+            sv[j] += s2[j];
+            pm = fmaxf(pm, sv[j]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            sv[j] = j <= lim ? sv[j] + s2[j] : -INFINITY;
+            pm = fmaxf(pm, sv[j]);
+          }
         }
       }
       // the pair's row maximum of this tile
@@ -286,12 +321,14 @@ flash_tc_kernel(const __grid_constant__ CUtensorMap tm_kh, const __grid_constant
       const bool move = tmax > m + kRescale;
       float alpha = 1.0f;
       if (move) {
-        alpha = (m == -INFINITY) ? 0.0f : __expf(m - tmax);
+        alpha = (m == -INFINITY) ? 0.0f : ex2_approx(m - tmax);
         m = tmax;
         l *= alpha;
       }
-      // rescale O (the products of tiles < t) where a row of this warp moved its m
-      if (t > 0 && __any_sync(0xffffffffu, move)) {
+      // fold O into the master (every kFold tiles), or rescale it where a row
+      // of this warp moved its m; both first wait for the products of tile t-1
+      const bool fold = t > 0 && t % kFold == 0;
+      if (t > 0 && (fold || __any_sync(0xffffffffu, move))) {
         const int tp = t - 1;
         if (!mbar_wait_warp(&sfree[tp & 1], (tp >> 1) & 1, ab, kErrWaitPV)) {
           ok = false;
@@ -302,28 +339,57 @@ flash_tc_kernel(const __grid_constant__ CUtensorMap tm_kh, const __grid_constant
         for (int cchunk = 0; cchunk < DVP / 32; ++cchunk) {
           if (DVP > 32 && (cchunk & 1) != half) continue;
           if (DVP == 32 && half != 0) continue;
-#pragma unroll
-          for (int part = 0; part < (L::kPVStack ? 2 : 1); ++part) {
-            const uint32_t oa = lane_addr + L::kO + part * DVP + cchunk * 32;
+          float (&g)[32] = master[DVP == 32 ? 0 : cchunk >> 1];
+          if (fold) {
+            // master = (master + O) * alpha; the TMEM chain restarts at tile t
             float ov[32];
-            tmem_ld32(oa, ov);
-            tmem_wait_ld();
-            uint32_t os[32];
+            tmem_ld32(lane_addr + L::kO + cchunk * 32, ov);
+            if (L::kPVStack) {
+              float o2[32];
+              tmem_ld32(lane_addr + L::kO + DVP + cchunk * 32, o2);
+              tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) os[j] = __float_as_uint(ov[j] * alpha);
-            tmem_st32(oa, os);
+              for (int j = 0; j < 32; ++j) ov[j] += o2[j];
+            }
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) g[j] = (g[j] + ov[j]) * alpha;
+          } else {
+            // O *= alpha in TMEM, and the master with it
+#pragma unroll
+            for (int part = 0; part < (L::kPVStack ? 2 : 1); ++part) {
+              const uint32_t oa = lane_addr + L::kO + part * DVP + cchunk * 32;
+              float ov[32];
+              tmem_ld32(oa, ov);
+              tmem_wait_ld();
+              uint32_t os[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) os[j] = __float_as_uint(ov[j] * alpha);
+              tmem_st32(oa, os);
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) g[j] *= alpha;
           }
         }
       }
+      // masked scores are -inf: ex2 gives exactly 0 there (m is finite for a
+      // valid row; an invalid row has every p = 0 below)
+      const float mm = valid ? m : 0.0f;
       uint32_t hi[32], lo[32];
+      float ps[16];
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const bool on = all_on || (valid && col0 + j <= i);
-        const float e = on ? __expf(sv[j] - m) : 0.0f;
-        l += e;
+        const float e = ex2_approx(sv[j] - mm);
+        if (j & 1) ps[j >> 1] += e; else ps[j >> 1] = e;
         hi[j] = to_tf32(e);
         lo[j] = __float_as_uint(e - __uint_as_float(hi[j]));
       }
+#pragma unroll
+      for (int w = 8; w >= 1; w >>= 1) {
+#pragma unroll
+        for (int j = 0; j < w; ++j) ps[j] += ps[j + w];
+      }
+      l += ps[0];
       tmem_st32(tS, hi);
       tmem_st32(tS + 64, lo);
       tmem_wait_st();
@@ -356,7 +422,7 @@ flash_tc_kernel(const __grid_constant__ CUtensorMap tm_kh, const __grid_constant
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int col = cchunk * 32 + j;
-            if (col < p.dv) orow[col] = __fdiv_rn(ov[j], dmax);
+            if (col < p.dv) orow[col] = __fdiv_rn(master[DVP == 32 ? 0 : cchunk >> 1][j] + ov[j], dmax);
           }
         }
       }

@@ -124,6 +124,46 @@ __device__ __forceinline__ float exp_score(float x) {
   return __expf(CLAMP ? fminf(x, 80.0f) : x);
 }
 
+// P = w (e^x - P_t(x)) over 32 rep scores, split hi / lo; MASK zeroes j > jhi;
+// w = nullptr for unit weights.
+template <bool MASK, int DEG, bool CLAMP>
+__device__ __forceinline__ void rep_to_p(const float (&sv)[32], const float* w, int jhi, float& den,
+                                         uint32_t (&hi)[32], uint32_t (&lo)[32]) {
+#pragma unroll
+  for (int j4 = 0; j4 < 8; ++j4) {
+    float ww[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+    if (w) {
+      const float4 w4 = reinterpret_cast<const float4*>(w)[j4];
+      ww[0] = w4.x; ww[1] = w4.y; ww[2] = w4.z; ww[3] = w4.w;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = 4 * j4 + u;
+      const float x = sv[j];
+      float e = exp_score<CLAMP>(x) - taylor_fma<DEG>(x);
+      if (w) e *= ww[u];
+      if (MASK && j > jhi) e = 0.0f;
+      den += e;
+      hi[j] = to_tf32(e);
+      lo[j] = __float_as_uint(e - __uint_as_float(hi[j]));
+    }
+  }
+}
+
+// P = e^x over 32 current-block scores; MASK keeps jlo <= j <= jhi only.
+template <bool MASK, bool CLAMP>
+__device__ __forceinline__ void cur_to_p(const float (&sv)[32], int jlo, int jhi, float& den, uint32_t (&hi)[32],
+                                         uint32_t (&lo)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float e = exp_score<CLAMP>(sv[j]);
+    if (MASK && (j < jlo || j > jhi)) e = 0.0f;
+    den += e;
+    hi[j] = to_tf32(e);
+    lo[j] = __float_as_uint(e - __uint_as_float(hi[j]));
+  }
+}
+
 template <int DP, int DVP, int DEG, bool CLAMP>
 __global__ void __launch_bounds__(kThreads, 1)
 residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_constant__ CUtensorMap tm_rkl,
@@ -354,46 +394,23 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
       }
       uint32_t hi[32], lo[32];
       if (rep) {
-        const bool all_on = col0 + 32 <= lim;
-        if (with_w) {
-          const float4* w4 = reinterpret_cast<const float4*>(wbuf + s * kTile + half * 32);
-#pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {
-            const float4 w = w4[j4];
-            const float ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int j = 4 * j4 + u;
-              const float x = sv[j];
-              float e = (exp_score<CLAMP>(x) - taylor_fma<DEG>(x)) * ww[u];
-              if (!all_on && col0 + j >= lim) e = 0.0f;
-              den += e;
-              hi[j] = to_tf32(e);
-              lo[j] = __float_as_uint(e - __uint_as_float(hi[j]));
-            }
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float x = sv[j];
-            float e = exp_score<CLAMP>(x) - taylor_fma<DEG>(x);
-            if (!all_on && col0 + j >= lim) e = 0.0f;
-            den += e;
-            hi[j] = to_tf32(e);
-            lo[j] = __float_as_uint(e - __uint_as_float(hi[j]));
-          }
-        }
+        // reps col0 + j with j <= jhi are active (r < lim)
+        const int64_t rel = lim - 1 - col0;
+        const int jhi = rel < 0 ? -1 : (rel > 31 ? 31 : (int)rel);
+        const float* w = with_w ? wbuf + s * kTile + half * 32 : nullptr;
+        if (jhi == 31)
+          rep_to_p<false, DEG, CLAMP>(sv, w, jhi, den, hi, lo);
+        else
+          rep_to_p<true, DEG, CLAMP>(sv, w, jhi, den, hi, lo);
       } else {
-        const bool all_on = col0 >= bst && col0 + 31 <= i;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int64_t key = col0 + j;
-          float e = exp_score<CLAMP>(sv[j]);
-          if (!all_on && (key > i || key < bst)) e = 0.0f;
-          den += e;
-          hi[j] = to_tf32(e);
-          lo[j] = __float_as_uint(e - __uint_as_float(hi[j]));
-        }
+        // keys col0 + j of the query's own block up to the query: jlo <= j <= jhi
+        const int64_t rlo = bst - col0, rhi = i - col0;
+        const int jlo = rlo < 0 ? 0 : (rlo > 32 ? 32 : (int)rlo);
+        const int jhi = !valid || rhi < 0 ? -1 : (rhi > 31 ? 31 : (int)rhi);
+        if (jlo == 0 && jhi == 31)
+          cur_to_p<false, CLAMP>(sv, jlo, jhi, den, hi, lo);
+        else
+          cur_to_p<true, CLAMP>(sv, jlo, jhi, den, hi, lo);
       }
       tmem_st32(tS, hi);
       tmem_st32(tS + 64, lo);
