@@ -30,18 +30,19 @@
 // remainder copies made by the transposing split pass) arrive by TMA, K-major
 // with the 128-byte swizzle: dv hi rows, then dv lo rows, of 32 tokens.
 //
-// Each 8-wide K step takes two MMAs of N = 2*DVP: A_hi and A_lo times
-// B = [B_hi | B_lo] (the hi and remainder copies of V or of the state sit one
-// chunk stride apart in shared memory).  A tf32 MMA costs about the same time
-// for any N up to 256, so this beats three N = DVP products; the two column
-// halves of the result are added on the CUDA cores.
+// Each 8-wide K step takes the three products of 3xTF32 as three MMAs of
+// N = DVP into one accumulator: A_hi B_hi, A_hi B_lo, A_lo B_hi (the hi and
+// remainder copies of V or of the state sit one fixed stride apart in shared
+// memory).  A tf32 MMA's time grows with N (M = 128: 32 cycles at N = 64,
+// 64 at N = 128, measured back to back), so this costs 3/4 of the two
+// doubled-width MMAs that would also form the unneeded A_lo B_lo.
 //
 // Accumulation: tensor-core accumulation into TMEM does not round to nearest,
-// so no long sum stays there.  dS_j covers one block (<= 64 MMA steps) and is
+// so no long sum stays there.  dS_j covers one block (3 MMAs per 8 keys) and is
 // folded into an fp32 master state in global memory (L2-resident, RN adds on
 // the CUDA cores) at the start of the next query phase, where the same thread
 // also writes the state's hi/lo split (MN-major, 32-byte-atom swizzle) that is
-// the B operand of the query product.  Out_j covers one tile (32 MMA steps)
+// the B operand of the query product.  Out_j covers one tile (48 MMA steps)
 // and lands in tile j's own TMEM columns (free after the fold); the tiles are
 // summed in registers.  The denominator column is a dot product with the same
 // features on the CUDA cores.  Each CTA writes its partial sums; the residual
@@ -58,7 +59,7 @@ using namespace tc;
 constexpr int kRows = 128;      // tokens per sub-tile = features per tile = TMEM lanes
 constexpr int kChunk = 32;      // K columns per staged feature chunk
 constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 generators
-constexpr int kNStg = 2;        // TMEM staging buffers (32 hi + 32 lo columns each)
+constexpr int kNStg = 4;        // TMEM staging buffers (32 hi + 32 lo columns each)
 constexpr int kXtStride = kRows + 4;   // transposed key tile row (floats)
 
 constexpr int kErrMomWait = 201, kErrMomDrain = 202;
@@ -84,9 +85,10 @@ struct MomTCParams {
 
 template <int DVP>
 struct MomLayout {
-  // TMEM columns of a tile: the product with [hi | lo] of the B operand, 2*DVP columns
-  static constexpr int kTC = 2 * DVP;
-  static constexpr int kFT = (512 - kNStg * 2 * kChunk) / kTC;      // state tiles per CTA
+  // TMEM columns of a tile: one DVP-wide accumulator
+  static constexpr int kTC = DVP;
+  static constexpr int kFT = (512 - kNStg * 2 * kChunk) / kTC > 4 ? 4 : (512 - kNStg * 2 * kChunk) / kTC;
+                                                                       // state tiles per CTA
   // TMEM columns: tile j at j*kTC (dS_j, then Out_j); staging after the tiles
   static constexpr uint32_t kStg = kFT * kTC;
   static_assert(kStg + kNStg * 2 * kChunk <= 512, "TMEM columns");
@@ -201,8 +203,7 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[HC]) {
   tmem_wait_ld();
 }
 
-// v[u] = TMEM column u + column u + off of this thread's lane, u < HC: the two
-// halves of a [hi | lo] product (A times the hi copy, A times the remainder).
+// 16 consecutive 32-bit columns of this thread's TMEM lane (no wait).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
@@ -210,19 +211,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
-}
-
-template <int HC>
-__device__ __forceinline__ void tmem_ld_sum(uint32_t taddr, uint32_t off, float (&v)[HC]) {
-#pragma unroll
-  for (int q = 0; q < HC / 16; ++q) {
-    uint32_t a[16], b[16];
-    tmem_ld16(taddr + 16 * q, a);
-    tmem_ld16(taddr + off + 16 * q, b);
-    tmem_wait_ld();
-#pragma unroll
-    for (int u = 0; u < 16; ++u) v[16 * q + u] = __uint_as_float(a[u]) + __uint_as_float(b[u]);
-  }
 }
 
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
@@ -308,7 +296,8 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
   float* sdx = xch + 2 * kRows;                                          // [FT*128]
   uint4* tmaps = reinterpret_cast<uint4*>(
       (reinterpret_cast<uintptr_t>(sdx + FT * kRows) + 15) & ~uintptr_t(15));   // [256] tile load maps
-  uint64_t* bars = reinterpret_cast<uint64_t*>(tmaps + 256);
+  uint2* fco = reinterpret_cast<uint2*>(tmaps + 256);                    // [FT][256] update-phase feature of a thread
+  uint64_t* bars = reinterpret_cast<uint64_t*>(fco + FT * 256);
   uint64_t* stg_full = bars;                // [kNStg] 256 arrivals
   uint64_t* stg_free = bars + kNStg;        // [kNStg] commit
   uint64_t* sb_full = bars + 2 * kNStg;     // [2] 256 arrivals
@@ -402,11 +391,10 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     // -------------------------------------------------------------- MMA issuer
     // the whole warp runs the loop; the elected lane issues MMAs and commits
     {
-      // B = [hi | lo] of V or of the state: both copies sit at one chunk / row
-      // stride, so a single MMA of N = 2*DVP multiplies A by both.  The state is
-      // MN-major (written by the generators); V is K-major (transposed split).
-      constexpr uint32_t idesc = idesc_tf32(128, 2 * DVP, false, true);
-      constexpr uint32_t idesc_v = idesc_tf32(128, 2 * DVP, false, false);
+      // B = the hi or the lo copy of V or of the state (N = DVP each).  The state
+      // is MN-major (written by the generators); V is K-major (transposed split).
+      constexpr uint32_t idesc = idesc_tf32(128, DVP, false, true);
+      constexpr uint32_t idesc_v = idesc_tf32(128, DVP, false, false);
       int stg_use = 0, sb_use = 0, v_use = 0, sub_use = 0;
       bool ok = true;
       for (int64_t c = 0; ok && c < nb; ++c) {
@@ -431,9 +419,11 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
 #pragma unroll
                 for (int kk = 0; kk < kChunk / 8; ++kk) {
                   const uint32_t off = (kc * kChunk + kk * 8) * 128;   // 8 feature rows of 128 B
-                  const uint64_t db = sdesc_sw128_atom32(bhi + off, kRows * 128, 512);
-                  if (elect_one()) mma_tf32_ts(dO, ahi + kk * 8, db, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
-                  if (elect_one()) mma_tf32_ts(dO, alo + kk * 8, db, idesc, 1u);
+                  const uint64_t dbh = sdesc_sw128_atom32(bhi + off, kRows * 128, 512);
+                  const uint64_t dbl = sdesc_sw128_atom32(bhi + L::kSbufHalf + off, kRows * 128, 512);
+                  if (elect_one()) mma_tf32_ts(dO, ahi + kk * 8, dbh, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+                  if (elect_one()) mma_tf32_ts(dO, ahi + kk * 8, dbl, idesc, 1u);
+                  if (elect_one()) mma_tf32_ts(dO, alo + kk * 8, dbh, idesc, 1u);
                 }
                 if (elect_one()) mma_commit(&stg_free[b]);
               }
@@ -459,11 +449,13 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
                 const uint32_t dS = tmem + j * L::kTC;
 #pragma unroll
                 for (int kk = 0; kk < kChunk / 8; ++kk) {
-                  const uint64_t db = sdesc_sw128(vhi + kk * 32, 16, 1024);
+                  const uint64_t dbh = sdesc_sw128(vhi + kk * 32, 16, 1024);
+                  const uint64_t dbl = sdesc_sw128(vhi + DVP * 128 + kk * 32, 16, 1024);
                   // dS_j starts from zero in every block
                   const uint32_t acc = (st > 0 || tc > 0 || kk > 0) ? 1u : 0u;
-                  if (elect_one()) mma_tf32_ts(dS, ahi + kk * 8, db, idesc_v, acc);
-                  if (elect_one()) mma_tf32_ts(dS, alo + kk * 8, db, idesc_v, 1u);
+                  if (elect_one()) mma_tf32_ts(dS, ahi + kk * 8, dbh, idesc_v, acc);
+                  if (elect_one()) mma_tf32_ts(dS, ahi + kk * 8, dbl, idesc_v, 1u);
+                  if (elect_one()) mma_tf32_ts(dS, alo + kk * 8, dbh, idesc_v, 1u);
                 }
                 if (elect_one()) mma_commit(&stg_free[b]);
               }
@@ -544,14 +536,14 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
       }
     };
     // this thread's feature of every tile in the update phase: indices and key factor
-    uint32_t fidx[FT];
-    float fcoef[FT];
+    // (kept in shared memory, [tile][generator thread], to spare registers)
+    const int gi = threadIdx.x - 64;
 #pragma unroll
     for (int j = 0; j < FT; ++j) {
       const uint32_t sg = segtab[j * 16 + (t >> 3)];
       const int p1 = sg & 1023, p2 = (sg >> 10) & 1023, c = (int)(sg >> 20) + (t & 7);
-      fidx[j] = (uint32_t)p1 | ((uint32_t)p2 << 10) | ((uint32_t)c << 20);
-      fcoef[j] = j < ntiles ? seg_key_coef(p1, p2, c, p.d, p.degree) : 0.0f;
+      const float cf = j < ntiles ? seg_key_coef(p1, p2, c, p.d, p.degree) : 0.0f;
+      fco[j * 256 + gi] = make_uint2((uint32_t)p1 | ((uint32_t)p2 << 10) | ((uint32_t)c << 20), __float_as_uint(cf));
     }
     for (int64_t c = 0; ok && c < nb; ++c) {
       const int64_t b0 = c * p.bs;
@@ -618,12 +610,11 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
               for (int q = 0; q < HC / 16; ++q) {
                 float sv[16];
                 if (st == 0 && !frozen) {
-                  uint32_t a[16], b[16];
+                  uint32_t a[16];
                   tmem_ld16(la + j * L::kTC + half * HC + 16 * q, a);
-                  tmem_ld16(la + j * L::kTC + DVP + half * HC + 16 * q, b);
                   tmem_wait_ld();
 #pragma unroll
-                  for (int u = 0; u < 16; ++u) sv[u] = __uint_as_float(a[u]) + __uint_as_float(b[u]);
+                  for (int u = 0; u < 16; ++u) sv[u] = __uint_as_float(a[u]);
                   if (c >= 2) {
 #pragma unroll
                     for (int u = 0; u < 16; ++u) sv[u] += mp[16 * q + u];
@@ -703,7 +694,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
           for (int u = 0; u < HC; ++u) acc[u] = 0.0f;
           for (int j = 0; j < ntiles; ++j) {
             float ov[HC];
-            tmem_ld_sum<HC>(la + j * L::kTC + half * HC, DVP, ov);
+            tmem_ld_cols<HC>(la + j * L::kTC + half * HC, ov);
 #pragma unroll
             for (int u = 0; u < HC; ++u) acc[u] += ov[u];
           }
@@ -776,8 +767,9 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
             const int b = stg_use % kNStg;
             if (stg_use >= kNStg && !mbar_wait(&stg_free[b], ((stg_use / kNStg) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
             ++stg_use;
-            const uint32_t fi = fidx[j];
-            const float cf = fcoef[j];
+            const uint2 fc = fco[j * 256 + gi];
+            const uint32_t fi = fc.x;
+            const float cf = __uint_as_float(fc.y);
             const float* r1 = X + (fi & 1023) * kXtStride + tok0;
             const float* rc = X + (fi >> 20) * kXtStride + tok0;
             uint32_t hi[16], lo[16];
@@ -834,16 +826,13 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
           float4* mrow = mrow_of(j);
 #pragma unroll
           for (int q = 0; q < HC / 16; ++q) {
-            uint32_t a[16], b[16];
+            uint32_t a[16];
             tmem_ld16(la + j * L::kTC + half * HC + 16 * q, a);
-            tmem_ld16(la + j * L::kTC + DVP + half * HC + 16 * q, b);
             tmem_wait_ld();
 #pragma unroll
             for (int u4 = 0; u4 < 4; ++u4) {
-              float4 v4 = make_float4(__uint_as_float(a[4 * u4]) + __uint_as_float(b[4 * u4]),
-                                      __uint_as_float(a[4 * u4 + 1]) + __uint_as_float(b[4 * u4 + 1]),
-                                      __uint_as_float(a[4 * u4 + 2]) + __uint_as_float(b[4 * u4 + 2]),
-                                      __uint_as_float(a[4 * u4 + 3]) + __uint_as_float(b[4 * u4 + 3]));
+              float4 v4 = make_float4(__uint_as_float(a[4 * u4]), __uint_as_float(a[4 * u4 + 1]),
+                                      __uint_as_float(a[4 * u4 + 2]), __uint_as_float(a[4 * u4 + 3]));
               if (nb >= 2) {
                 const float4 m4 = mrow[(4 * q + u4) * kRows];
                 v4.x += m4.x;
@@ -875,7 +864,8 @@ size_t mom_smem(int d) {
   const int dp = dpad8(d), DX = dp + 8, XS = DX + 4;
   const size_t xwords = (size_t)max(max(kRows * XS, DX * kXtStride), kRows * (DVP + 1));
   return 1024 + 2 * L::kSbuf + L::kVStages * L::kVStage + xwords * 4 + (size_t)L::kFT * 16 * 4 +
-         (size_t)L::kFT * kRows * 8 + 2 * kRows * 4 + 16 + 256 * 16 + (2 * kNStg + 12) * 8 + 16;
+         (size_t)L::kFT * kRows * 8 + 2 * kRows * 4 + 16 + 256 * 16 + (size_t)L::kFT * 256 * 8 +
+         (2 * kNStg + 12) * 8 + 16;
 }
 
 template <int DVP, bool DEG3>

@@ -308,7 +308,9 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
       for (int t = 0; ok && t < T; ++t) {
         const int s = t % kStages, b = t & 1;
         if (!mbar_wait_warp(&full[s], (t / kStages) & 1, ab, kErrWaitFull)) { ok = false; break; }
-        if (t >= 2 && !mbar_wait_warp(&sfree[b], ((t >> 1) - 1) & 1, ab, kErrWaitSfree)) { ok = false; break; }
+        // S(t) reuses the TMEM columns that PV(t-2) reads as its A operand.  No wait:
+        // tcgen05.mma operations issued by one thread execute in issue order (mma
+        // after mma is an implicitly pipelined pair), and PV(t-2) was issued first.
         tc_fence_after();
         const uint32_t kh = smem_u32(smem + s * L::kStage);
         const uint32_t dS = tmem + L::kS0 + 128 * b;
