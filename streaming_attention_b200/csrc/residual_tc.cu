@@ -25,9 +25,11 @@
 // row-major k split, V tiles from the transposed v split (an MN-major tf32
 // operand runs markedly slower on the tensor cores).
 //
-// A tf32 MMA costs about the same for N = 64 as for N = 128, so both products
-// put the hi and remainder copies of their B operand side by side and take two
-// MMAs of twice the width per 8-wide K step instead of three:
+// Both products put the hi and remainder copies of their B operand side by
+// side and take two MMAs of twice the width per 8-wide K step instead of three
+// N-wide ones.  That also forms the unneeded lo*lo product (a tf32 MMA's time
+// grows with N), but measured on the same GPU the three-MMA form ran this
+// kernel 10 % slower, so the doubled width stays:
 //   S' = Q_hi [K_hi; K_lo]^T + Q_lo [K_hi; K_lo]^T   (N = 128: each 32-column
 //        K chunk holds the 64 hi rows, then the 64 lo rows), S = S'[:, :64] + S'[:, 64:]
 //   O' = P_hi [V_hi | V_lo] + P_lo [V_hi | V_lo]     (N = 2 dv: each 32-key chunk of
