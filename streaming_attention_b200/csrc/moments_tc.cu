@@ -486,7 +486,21 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     int stg_use = 0, sb_use = 0, out_use = 0;
     bool ok = true;
     const int64_t col_stride = p.dv + 1;
+
     float* part_h = p.part + ((int64_t)g * p.bh + h) * p.n * col_stride;
+    // staged query sums of one sub-tile ([rows, dv + 1] in the state buffer)
+    // and where they go; copy_out writes them once every thread has staged its row
+    float* ostg = reinterpret_cast<float*>(sbuf);
+    int64_t out_i0 = 0;
+    int out_rows = 0;
+    auto copy_out = [&]() {
+      if (out_rows > 0) {
+        const int total = out_rows * (int)col_stride;
+        float* dst = part_h + out_i0 * col_stride;
+        for (int e = threadIdx.x - 64; e < total; e += 256) dst[e] = ostg[e];
+        out_rows = 0;
+      }
+    };
     float* master_h = p.master + ((int64_t)g * p.bh + h) * (int64_t)(FT * kRows) * DVP;
     const bool vec = (p.d & 3) == 0 &&
                      ((reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.k)) & 15) == 0;
@@ -557,10 +571,6 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
       } else {
         const bool frozen = p.mode == 2;
         if (c >= 2 || frozen) mload(0);   // the state rows written by the previous query phase
-        if (!frozen) {
-          if (!mbar_wait(u_done, (int)((c - 1) & 1), ab, kErrMomWait)) { ok = false; break; }
-          tc_fence_after();
-        }
         const int nsq = (int)((b1 - b0 + kRows - 1) / kRows);  // query sub-tiles of block c
         for (int st = 0; ok && st < nsq; ++st) {
           const int64_t i = b0 + (int64_t)st * kRows + t;
@@ -593,6 +603,12 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
           }
           issue_next(c, true, st);
           gen_sync();
+          // the fold below reads the update products of block c - 1: wait for them
+          // only now, so that staging the query tile overlaps their tail
+          if (st == 0 && !frozen) {
+            if (!mbar_wait(u_done, (int)((c - 1) & 1), ab, kErrMomWait)) { ok = false; break; }
+            tc_fence_after();
+          }
           float den_acc = 0.0f;
           for (int j = 0; ok && j < ntiles; ++j, ++sb_use) {
             const int sb = sb_use & 1;
@@ -704,21 +720,23 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
           xch[half * kRows + t] = den_acc;
           gen_sync();
           {
-            // X is free: stage the sub-tile's [rows, dv + 1] sums (row stride dv + 1
-            // is odd, so the column writes are conflict-free), then copy the
-            // contiguous block out with consecutive threads on consecutive words
+            // Stage the sub-tile's [rows, dv + 1] sums in the state buffer (every
+            // product that reads it is done; row stride dv + 1 is odd, so the
+            // column writes are conflict-free).  The coalesced copy to global
+            // memory (consecutive threads on consecutive words) waits until after
+            // the update phase, where it overlaps the tail of the update products,
+            // unless another query sub-tile's fold needs the buffer first.
             const int cs = (int)col_stride;
 #pragma unroll
             for (int u = 0; u < HC; ++u)
-              if (half * HC + u < p.dv) X[t * cs + half * HC + u] = acc[u];
-            if (half == 0) X[t * cs + p.dv] = xch[t] + xch[kRows + t];
+              if (half * HC + u < p.dv) ostg[t * cs + half * HC + u] = acc[u];
+            if (half == 0) ostg[t * cs + p.dv] = xch[t] + xch[kRows + t];
+            out_i0 = b0 + (int64_t)st * kRows;
+            out_rows = (int)min((int64_t)kRows, b1 - out_i0);
           }
-          gen_sync();
-          {
-            const int64_t i0 = b0 + (int64_t)st * kRows;
-            const int total = (int)min((int64_t)kRows, b1 - i0) * (int)col_stride;
-            float* dst = part_h + i0 * col_stride;
-            for (int e = threadIdx.x - 64; e < total; e += 256) dst[e] = X[e];
+          if (st + 1 < nsq || !has_update(c)) {
+            gen_sync();
+            copy_out();
           }
         }
       }
@@ -814,6 +832,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
         for (int j = 0; j < FT; ++j)
           if (j < ntiles) sden[j * kRows + t] += sd[j] + sdx[j * kRows + t];
       }
+      copy_out();   // the query sums of this block, staged before the update phase
     }
     if (ok && p.mode == 1) {
       // total: fold the last block's dS into the master (which then holds the
