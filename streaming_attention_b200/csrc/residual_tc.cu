@@ -427,15 +427,24 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     den_x[half * 128 + row] = den;
     asm volatile("bar.sync 1, 256;" ::: "memory");
     const float den_all = den_x[row] + den_x[128 + row];
-    if (ok && mbar_wait(ofull, 0, ab, kErrWaitO)) {
+    // Epilogue.  The output rows and the moment kernel's `groups` partial
+    // slices of the low term are read and written coalesced: each thread first
+    // puts its row's O columns (and the row's divisor) into shared memory, over
+    // the stage buffers, which no copy or product touches any more once O is
+    // complete; then each warp takes whole rows, lanes on consecutive columns.
+    const bool o_ok = ok && mbar_wait_warp(ofull, 0, ab, kErrWaitO);
+    constexpr int OS = DVP + 1;                                  // odd row stride: conflict-free
+    float* os = reinterpret_cast<float*>(smem);                  // [128][DVP + 1]
+    float* dms = os + kRowsQ * OS;                               // [128] max(den, eps)
+    if (o_ok) {
       tc_fence_after();
-      // low term: the sum of the moment kernel's `groups` partial slices
-      const float* lrow = p.low + (h * p.n + (valid ? i : 0)) * (int64_t)(p.dv + 1);
-      float ldsum = 0.0f;
-      for (int gi = 0; gi < p.groups; ++gi) ldsum += valid ? __ldg(lrow + gi * p.group_stride + p.dv) : 0.0f;
-      const float dtot = valid ? ldsum + den_all : 1.0f;
-      const float dmax = fmaxf(dtot, p.eps);
-      float* orow = p.out + (h * p.n + (valid ? i : 0)) * (int64_t)p.dv;
+      if (half == 0) {
+        const float* lrow = p.low + (h * p.n + (valid ? i : 0)) * (int64_t)(p.dv + 1);
+        float ldsum = 0.0f;
+        for (int gi = 0; gi < p.groups; ++gi) ldsum += valid ? __ldg(lrow + gi * p.group_stride + p.dv) : 0.0f;
+        const float dtot = valid ? ldsum + den_all : 1.0f;
+        dms[row] = fmaxf(dtot, p.eps);
+      }
 #pragma unroll
       for (int cchunk = 0; cchunk < DVP / 32; ++cchunk) {
         if (DVP > 32 && (cchunk & 1) != half) continue;
@@ -450,16 +459,22 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
           for (int j = 0; j < 32; ++j) ov[j] += o2[j];
         }
         tmem_wait_ld();
-        if (valid) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int col = cchunk * 32 + j;
-            if (col < p.dv) {
-              float lv = 0.0f;
-              for (int gi = 0; gi < p.groups; ++gi) lv += __ldg(lrow + gi * p.group_stride + col);
-              orow[col] = __fdiv_rn(ov[j] + lv, dmax);
-            }
-          }
+        for (int j = 0; j < 32; ++j) os[row * OS + cchunk * 32 + j] = ov[j];
+      }
+    }
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    if (o_ok) {
+      const int nrows = (int)min((int64_t)kRowsQ, p.n - q0);
+      for (int r = warp - 2; r < nrows; r += 8) {
+        const int64_t gr = h * p.n + q0 + r;
+        const float* lr = p.low + gr * (int64_t)(p.dv + 1);
+        float* orow = p.out + gr * (int64_t)p.dv;
+        const float dm = dms[r];
+        for (int col = lane; col < p.dv; col += 32) {
+          float lv = 0.0f;
+          for (int gi = 0; gi < p.groups; ++gi) lv += __ldg(lr + gi * p.group_stride + col);
+          orow[col] = __fdiv_rn(os[r * OS + col] + lv, dm);
         }
       }
     }
