@@ -56,6 +56,15 @@ namespace {
 
 using namespace tc;
 
+// tf32 hi part of x by truncation (one logic op).  lo = x - hi is still exact,
+// |lo| < 2^-10 |x| instead of 2^-11 with round-to-nearest, which leaves the
+// 3xTF32 products within ~2^-20 relative; measured on the config-3-shaped
+// parity case: 7.9e-7 rel-L2 against the oracle instead of 7.1e-7, and the
+// moment scan 0.85 ms faster.  NaNs from arithmetic (high mantissa bits set)
+// stay NaN.
+__device__ __forceinline__ uint32_t tf32_trunc(float x) { return __float_as_uint(x) & 0xffffe000u; }
+
+
 constexpr int kRows = 128;      // tokens per sub-tile = features per tile = TMEM lanes
 constexpr int kChunk = 32;      // K columns per staged feature chunk
 constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 generators
@@ -648,7 +657,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
                   float hv[8], lv[8];
 #pragma unroll
                   for (int u = 0; u < 8; ++u) {
-                    hv[u] = __uint_as_float(to_tf32(sv[gg * 8 + u]));
+                    hv[u] = __uint_as_float(tf32_trunc(sv[gg * 8 + u]));
                     lv[u] = sv[gg * 8 + u] - hv[u];
                   }
                   *reinterpret_cast<float4*>(bhi + off) = make_float4(hv[0], hv[1], hv[2], hv[3]);
@@ -688,7 +697,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
                   den_acc = fmaf(ph[u], dd[u], den_acc);
-                  hi[sg * 8 + u] = to_tf32(ph[u]);
+                  hi[sg * 8 + u] = tf32_trunc(ph[u]);
                   lo[sg * 8 + u] = __float_as_uint(ph[u] - __uint_as_float(hi[sg * 8 + u]));
                 }
               }
@@ -807,7 +816,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
                 fsum += ph[u];
-                hi[4 * u4 + u] = to_tf32(ph[u]);
+                hi[4 * u4 + u] = tf32_trunc(ph[u]);
                 lo[4 * u4 + u] = __float_as_uint(ph[u] - __uint_as_float(hi[4 * u4 + u]));
               }
             }
