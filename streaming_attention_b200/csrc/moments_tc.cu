@@ -68,7 +68,8 @@ __device__ __forceinline__ uint32_t tf32_trunc(float x) { return __float_as_uint
 constexpr int kRows = 128;      // tokens per sub-tile = features per tile = TMEM lanes
 constexpr int kChunk = 32;      // K columns per staged feature chunk
 constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 generators
-constexpr int kNStg = 4;        // TMEM staging buffers (32 hi + 32 lo columns each)
+constexpr int kNStg = 3;        // TMEM staging buffers (32 hi + 32 lo columns each); 3 leave room
+                                // for 5 state tiles, so fewer feature groups per sequence
 constexpr int kXtStride = kRows + 4;   // transposed key tile row (floats)
 
 constexpr int kErrMomWait = 201, kErrMomDrain = 202;
@@ -96,7 +97,7 @@ template <int DVP>
 struct MomLayout {
   // TMEM columns of a tile: one DVP-wide accumulator
   static constexpr int kTC = DVP;
-  static constexpr int kFT = (512 - kNStg * 2 * kChunk) / kTC > 4 ? 4 : (512 - kNStg * 2 * kChunk) / kTC;
+  static constexpr int kFT = (512 - kNStg * 2 * kChunk) / kTC > 5 ? 5 : (512 - kNStg * 2 * kChunk) / kTC;
                                                                        // state tiles per CTA
   // TMEM columns: tile j at j*kTC (dS_j, then Out_j); staging after the tiles
   static constexpr uint32_t kStg = kFT * kTC;

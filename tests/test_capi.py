@@ -82,9 +82,9 @@ def test_workspace_size_and_argument_errors_without_gpu():
     # feature groups, hi/lo copies of k, v (transposed) and of the reps, rep weights and
     # indices, and the gathered rep values before their transposing split
     fixed = 4 * 256 * 8192 * 64 * 4 + 4 * 256 * R * 64 * 4 + 256 * R * 4 + 256 * R * 4 + 256 * R * 64 * 4
-    per_group = 256 * 8192 * 65 * 4 + 256 * 4 * 128 * 64 * 4   # four state tiles of 128 features per group
+    per_group = 256 * 8192 * 65 * 4 + 256 * 5 * 128 * 64 * 4   # five state tiles of 128 features per group
     groups = (sz.value - fixed) // per_group
-    assert groups == 5   # 2376 padded features (d = 64, degree 2) in 19 tiles
+    assert groups == 4   # 2376 padded features (d = 64, degree 2) in 19 tiles
     assert fixed + groups * per_group <= sz.value < fixed + groups * per_group + 4096
     # argument errors return before any CUDA call
     assert lib.sa_fast_attention(None, None, None, 1, 16, 8, 8, 2, 0, 1.0, 1, None, None, None, 1e-12, None, None,
