@@ -465,16 +465,43 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     }
     asm volatile("bar.sync 1, 256;" ::: "memory");
     if (o_ok) {
+      // Four rows per pass (rows r, r+8, r+16, r+24 of this warp), every load of
+      // the pass issued before any store: the loads of a row do not wait for the
+      // stores of the row before (the output and the slices never overlap).
+      constexpr int kRP = 4, kNC = DVP / 32;
+      const float* __restrict__ lowp = p.low;
+      float* __restrict__ outp = p.out;
       const int nrows = (int)min((int64_t)kRowsQ, p.n - q0);
-      for (int r = warp - 2; r < nrows; r += 8) {
-        const int64_t gr = h * p.n + q0 + r;
-        const float* lr = p.low + gr * (int64_t)(p.dv + 1);
-        float* orow = p.out + gr * (int64_t)p.dv;
-        const float dm = dms[r];
-        for (int col = lane; col < p.dv; col += 32) {
-          float lv = 0.0f;
-          for (int gi = 0; gi < p.groups; ++gi) lv += __ldg(lr + gi * p.group_stride + col);
-          orow[col] = __fdiv_rn(os[r * OS + col] + lv, dm);
+      const int64_t ls = p.dv + 1;
+      for (int r0 = warp - 2; r0 < nrows; r0 += 8 * kRP) {
+        float lv[kRP][kNC];
+#pragma unroll
+        for (int a = 0; a < kRP; ++a)
+#pragma unroll
+          for (int c = 0; c < kNC; ++c) lv[a][c] = 0.0f;
+        for (int gi = 0; gi < p.groups; ++gi) {
+#pragma unroll
+          for (int a = 0; a < kRP; ++a) {
+            const int r = r0 + 8 * a;
+            const float* lr = lowp + (h * p.n + q0 + (r < nrows ? r : 0)) * ls + gi * p.group_stride;
+#pragma unroll
+            for (int c = 0; c < kNC; ++c) {
+              const int col = c * 32 + lane;
+              if (r < nrows && col < p.dv) lv[a][c] += __ldg(lr + col);
+            }
+          }
+        }
+#pragma unroll
+        for (int a = 0; a < kRP; ++a) {
+          const int r = r0 + 8 * a;
+          if (r >= nrows) continue;
+          float* orow = outp + (h * p.n + q0 + r) * (int64_t)p.dv;
+          const float dm = dms[r];
+#pragma unroll
+          for (int c = 0; c < kNC; ++c) {
+            const int col = c * 32 + lane;
+            if (col < p.dv) orow[col] = __fdiv_rn(os[r * OS + col] + lv[a][c], dm);
+          }
         }
       }
     }
