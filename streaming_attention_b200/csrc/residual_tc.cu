@@ -236,6 +236,20 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     if (lane == 0) {
       tma_prefetch_desc(&tm_rkh);
       tma_prefetch_desc(&tm_kh);
+      // The epilogue reads this CTA's rows of every low slice, written long ago
+      // by the moment kernel: start moving them into L2 now, under the main loop.
+      if ((reinterpret_cast<uintptr_t>(p.low) & 15) == 0) {
+        const uintptr_t base = reinterpret_cast<uintptr_t>(p.low);
+        const uintptr_t end = base + (uintptr_t)p.groups * (uintptr_t)p.group_stride * 4u;
+        const int64_t rows = min((int64_t)kRowsQ, p.n - q0);
+        for (int gi = 0; gi < p.groups; ++gi) {
+          const uintptr_t a0 =
+              (base + (uintptr_t)(((h * p.n + q0) * (int64_t)(p.dv + 1) + gi * p.group_stride) * 4)) & ~uintptr_t(15);
+          uintptr_t a1 = (a0 + (uintptr_t)(rows * (p.dv + 1) * 4) + 31) & ~uintptr_t(15);
+          if (a1 > (end & ~uintptr_t(15))) a1 = end & ~uintptr_t(15);
+          if (a1 > a0) bulk_prefetch_l2(reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0));
+        }
+      }
       int issued = 0;
       for (int t = 0; t < T; ++t) {
         const int s = t % kStages;

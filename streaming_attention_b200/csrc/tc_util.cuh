@@ -116,6 +116,12 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
+// Starts bringing `bytes` at src into L2 (src 16-byte aligned, bytes % 16 == 0);
+// no completion is tracked.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // TMEM
 // ---------------------------------------------------------------------------
