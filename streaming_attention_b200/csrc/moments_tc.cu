@@ -569,6 +569,37 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
       const float cf = j < ntiles ? seg_key_coef(p1, p2, c, p.d, p.degree) : 0.0f;
       fco[j * 256 + gi] = make_uint2((uint32_t)p1 | ((uint32_t)p2 << 10) | ((uint32_t)c << 20), __float_as_uint(cf));
     }
+    // the transposed key tile of update sub-tile st of block c into X
+    // (X[a * kXtStride + token]) from the prefetched rows; then the next tile's loads
+    auto stage_keys = [&](int64_t c, int st) {
+      const int64_t b1 = min(c * p.bs + (int64_t)p.bs, p.n);
+      const int64_t i = c * p.bs + (int64_t)st * kRows + t;
+      const bool valid = i < b1;
+      const int a0 = half * 32;
+      if (vec) {
+        const uint4 m = *my_map;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t e = tile_entry(m, k);
+          const int row = (int)(e >> 8), col4 = (int)(e & 255);
+          if (e != 0xffffu) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) X[(4 * col4 + e) * kXtStride + row] = rowv[4 * k + e];
+          }
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < 32; ++u)
+          if (a0 + u < p.d) X[(a0 + u) * kXtStride + t] = rowv[u];
+      }
+      const float* src = kh + (valid ? i : 0) * p.d;
+      for (int a = 64 + half; a < p.d; a += 2) X[a * kXtStride + t] = valid ? __ldg(src + a) : 0.0f;
+      // an invalid token's extended row is all zero, so are its features
+      if (half == 1)
+        for (int a = p.d; a < DX; ++a) X[a * kXtStride + t] = (a == dp && valid) ? 1.0f : 0.0f;
+      issue_next(c, false, st);
+    };
+    bool kstaged = false;   // the first key tile of the update phase is already in X
     for (int64_t c = 0; ok && c < nb; ++c) {
       const int64_t b0 = c * p.bs;
       const int64_t b1 = min(b0 + (int64_t)p.bs, p.n);
@@ -710,6 +741,15 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
             }
           }
           if (!ok) break;
+          // X (the query tile) is free once every thread has made its last Phi_q
+          // chunk: stage the first key tile of the update phase now, under the
+          // tail of the query products (the gen_sync after the readback below
+          // orders these writes before the update phase reads them)
+          if (st + 1 == nsq && has_update(c)) {
+            gen_sync();
+            stage_keys(c, 0);
+            kstaged = true;
+          }
           // Out_j of every tile sits in the tile's own TMEM columns: once all the
           // sub-tile's MMAs are done, add them up in tile order
           if (!mbar_wait(out_full, out_use & 1, ab, kErrMomWait)) { ok = false; break; }
@@ -756,37 +796,12 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
 #pragma unroll
       for (int j = 0; j < FT; ++j) sd[j] = 0.0f;
       for (int st = 0; ok && st < sub; ++st) {
-        const int64_t t0 = b0 + (int64_t)st * kRows;
-        gen_sync();  // everyone is done with X
-        {
-          // transposed key tile: X[a * kXtStride + token]
-          const int64_t i = t0 + t;
-          const bool valid = i < b1;
-          const int a0 = half * 32;
-          if (vec) {
-            const uint4 m = *my_map;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const uint32_t e = tile_entry(m, k);
-              const int row = (int)(e >> 8), col4 = (int)(e & 255);
-              if (e != 0xffffu) {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) X[(4 * col4 + e) * kXtStride + row] = rowv[4 * k + e];
-              }
-            }
-          } else {
-#pragma unroll
-            for (int u = 0; u < 32; ++u)
-              if (a0 + u < p.d) X[(a0 + u) * kXtStride + t] = rowv[u];
-          }
-          const float* src = kh + (valid ? i : 0) * p.d;
-          for (int a = 64 + half; a < p.d; a += 2) X[a * kXtStride + t] = valid ? __ldg(src + a) : 0.0f;
-          // an invalid token's extended row is all zero, so are its features
-          if (half == 1)
-            for (int a = p.d; a < DX; ++a) X[a * kXtStride + t] = (a == dp && valid) ? 1.0f : 0.0f;
+        if (!(st == 0 && kstaged)) {
+          gen_sync();  // everyone is done with X
+          stage_keys(c, st);
+          gen_sync();
         }
-        issue_next(c, false, st);
-        gen_sync();
+        kstaged = false;
         for (int tcn = 0; ok && tcn < kRows / kChunk; ++tcn) {
           const int tok0 = tcn * kChunk + half * 16;
 #pragma unroll
