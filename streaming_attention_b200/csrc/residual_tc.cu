@@ -87,7 +87,7 @@ struct Layout {
   static constexpr uint32_t kO = 2 * DP + 256;
   static constexpr bool kPVStack = kO + 2 * DVP <= 512;  // O' = P [V_hi | V_lo] fits
   static_assert(kO + DVP <= 512, "TMEM columns");
-  static constexpr uint32_t kSmemBytes = kStages * kStage + kW + (2 * kStages + 10) * 8 + 64 + 2 * 128 * 4 + 1024;
+  static constexpr uint32_t kSmemBytes = kStages * kStage + kW + (2 * kStages + 11) * 8 + 64 + 2 * 128 * 4 + 1024;
 };
 
 template <int DEG>
@@ -187,7 +187,8 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
   uint64_t* qready = sfree + 2;
   uint64_t* ofull = qready + 1;
   uint64_t* drain = ofull + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* lowfull = drain + 1;          // the epilogue's low-sum rows, bulk-copied into the stages
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(lowfull + 1);
   int* abort_word = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -204,6 +205,17 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
   const int64_t kb0 = c_first * p.bs;
   const int n_cur = (int)((q_last + 1 - kb0 + kTile - 1) / kTile);
   const int T = n_rep + n_cur;
+  // Epilogue input: this CTA's rows of the `groups` low slices.  When they fit in
+  // the stage buffers (free once O is complete) next to the O staging, and every
+  // row block is 16-byte aligned, the producer bulk-copies them into shared
+  // memory as soon as O is complete.
+  const int64_t erows = min((int64_t)kRowsQ, p.n - q0);
+  const int64_t lblk = erows * (int64_t)(p.dv + 1);          // floats of one slice's row block
+  const uint64_t lbytes = (uint64_t)p.groups * (uint64_t)lblk * 4u;
+  const uint64_t lbytes16 = (lbytes + 15) & ~uint64_t(15);
+  const bool bulk_low = (lblk * 4) % 16 == 0 && (p.group_stride * 4) % 16 == 0 &&
+                        ((reinterpret_cast<uintptr_t>(p.low) + (uintptr_t)((h * p.n + q0) * (int64_t)(p.dv + 1) * 4)) & 15) == 0 &&
+                        lbytes16 + (uint64_t)kRowsQ * (DVP + 1) * 4 + (uint64_t)kRowsQ * 4 <= (uint64_t)kStages * L::kStage;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -218,6 +230,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     mbar_init(qready, 256);
     mbar_init(ofull, 1);
     mbar_init(drain, 1);
+    mbar_init(lowfull, 1);
     *abort_word = 0;
     fence_mbar_init();
   }
@@ -281,6 +294,20 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
       for (int t = max(0, issued - kStages); t < issued; ++t) {
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(&full[t % kStages], (t / kStages) & 1)) {
+          if (globaltimer_ns() - t0 > 1000000000ull) {
+            atomicCAS(p.status, 0, kErrDrain);
+            break;
+          }
+        }
+      }
+      // once O is complete nothing reads the stages: bring in the epilogue's rows
+      if (bulk_low && issued == T && mbar_wait(ofull, 0, ab, kErrWaitO)) {
+        mbar_arrive_expect_tx(lowfull, (uint32_t)lbytes);
+        for (int gi = 0; gi < p.groups; ++gi)
+          bulk_load(reinterpret_cast<float*>(smem) + gi * lblk,
+                    p.low + (h * p.n + q0) * (int64_t)(p.dv + 1) + gi * p.group_stride, (uint32_t)(lblk * 4), lowfull);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(lowfull, 0)) {   // and never leave with them in flight
           if (globaltimer_ns() - t0 > 1000000000ull) {
             atomicCAS(p.status, 0, kErrDrain);
             break;
@@ -448,7 +475,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     // complete; then each warp takes whole rows, lanes on consecutive columns.
     const bool o_ok = ok && mbar_wait_warp(ofull, 0, ab, kErrWaitO);
     constexpr int OS = DVP + 1;                                  // odd row stride: conflict-free
-    float* os = reinterpret_cast<float*>(smem);                  // [128][DVP + 1]
+    float* os = reinterpret_cast<float*>(smem + (bulk_low ? lbytes16 : 0));   // [128][DVP + 1]
     float* dms = os + kRowsQ * OS;                               // [128] max(den, eps)
     if (o_ok) {
       tc_fence_after();
@@ -478,7 +505,23 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
       }
     }
     asm volatile("bar.sync 1, 256;" ::: "memory");
-    if (o_ok) {
+    if (o_ok && bulk_low) {
+      // the rows arrive by bulk copy: every read below is from shared memory
+      if (mbar_wait_warp(lowfull, 0, ab, kErrWaitO)) {
+        const float* lb = reinterpret_cast<const float*>(smem);
+        const int ls = p.dv + 1;
+        const int nrows = (int)erows;
+        for (int r = warp - 2; r < nrows; r += 8) {
+          float* orow = p.out + (h * p.n + q0 + r) * (int64_t)p.dv;
+          const float dm = dms[r];
+          for (int col = lane; col < p.dv; col += 32) {
+            float lv = 0.0f;
+            for (int gi = 0; gi < p.groups; ++gi) lv += lb[gi * lblk + r * ls + col];
+            orow[col] = __fdiv_rn(os[r * OS + col] + lv, dm);
+          }
+        }
+      }
+    } else if (o_ok) {
       // Four rows per pass (rows r, r+8, r+16, r+24 of this warp), every load of
       // the pass issued before any store: the loads of a row do not wait for the
       // stores of the row before (the output and the slices never overlap).
