@@ -424,18 +424,26 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
                 const int b = stg_use % kNStg;
                 if (!mbar_wait_warp(&stg_full[b], (stg_use / kNStg) & 1, ab, kErrMomWait)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t ahi = tmem + L::kStg + b * 2 * kChunk;
-                const uint32_t alo = ahi + kChunk;
+                // one elected lane issues the chunk's 12 MMAs and its commit back to back
+                // (at N = DVP an MMA takes only ~32 cycles, so per-MMA elections and
+                // descriptor arithmetic would starve the tensor pipe)
+                if (elect_one()) {
+                  const uint32_t ahi = tmem + L::kStg + b * 2 * kChunk;
+                  const uint32_t alo = ahi + kChunk;
+                  // 8 feature rows of 128 B per K step: the descriptors' start address
+                  // field (address >> 4) advances by 64 per step
+                  const uint64_t dbh = sdesc_sw128_atom32(bhi + kc * kChunk * 128, kRows * 128, 512);
+                  const uint64_t dbl = dbh + (L::kSbufHalf >> 4);
 #pragma unroll
-                for (int kk = 0; kk < kChunk / 8; ++kk) {
-                  const uint32_t off = (kc * kChunk + kk * 8) * 128;   // 8 feature rows of 128 B
-                  const uint64_t dbh = sdesc_sw128_atom32(bhi + off, kRows * 128, 512);
-                  const uint64_t dbl = sdesc_sw128_atom32(bhi + L::kSbufHalf + off, kRows * 128, 512);
-                  if (elect_one()) mma_tf32_ts(dO, ahi + kk * 8, dbh, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
-                  if (elect_one()) mma_tf32_ts(dO, ahi + kk * 8, dbl, idesc, 1u);
-                  if (elect_one()) mma_tf32_ts(dO, alo + kk * 8, dbh, idesc, 1u);
+                  for (int kk = 0; kk < kChunk / 8; ++kk) {
+                    const uint64_t dk = (uint64_t)(kk * 8 * 128 / 16);
+                    mma_tf32_ts(dO, ahi + kk * 8, dbh + dk, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+                    mma_tf32_ts(dO, ahi + kk * 8, dbl + dk, idesc, 1u);
+                    mma_tf32_ts(dO, alo + kk * 8, dbh + dk, idesc, 1u);
+                  }
+                  mma_commit(&stg_free[b]);
                 }
-                if (elect_one()) mma_commit(&stg_free[b]);
+                __syncwarp();
               }
               if (elect_one()) mma_commit(&sb_free[sb]);
             }
@@ -454,20 +462,25 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
                 const int b = stg_use % kNStg;
                 if (!mbar_wait_warp(&stg_full[b], (stg_use / kNStg) & 1, ab, kErrMomWait)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t ahi = tmem + L::kStg + b * 2 * kChunk;
-                const uint32_t alo = ahi + kChunk;
-                const uint32_t dS = tmem + j * L::kTC;
+                if (elect_one()) {
+                  const uint32_t ahi = tmem + L::kStg + b * 2 * kChunk;
+                  const uint32_t alo = ahi + kChunk;
+                  const uint32_t dS = tmem + j * L::kTC;
+                  // K-major V^T rows of 128 B: a K step of 8 tokens is 32 B further
+                  const uint64_t dbh = sdesc_sw128(vhi, 16, 1024);
+                  const uint64_t dbl = dbh + ((DVP * 128) >> 4);
 #pragma unroll
-                for (int kk = 0; kk < kChunk / 8; ++kk) {
-                  const uint64_t dbh = sdesc_sw128(vhi + kk * 32, 16, 1024);
-                  const uint64_t dbl = sdesc_sw128(vhi + DVP * 128 + kk * 32, 16, 1024);
-                  // dS_j starts from zero in every block
-                  const uint32_t acc = (st > 0 || tc > 0 || kk > 0) ? 1u : 0u;
-                  if (elect_one()) mma_tf32_ts(dS, ahi + kk * 8, dbh, idesc_v, acc);
-                  if (elect_one()) mma_tf32_ts(dS, ahi + kk * 8, dbl, idesc_v, 1u);
-                  if (elect_one()) mma_tf32_ts(dS, alo + kk * 8, dbh, idesc_v, 1u);
+                  for (int kk = 0; kk < kChunk / 8; ++kk) {
+                    const uint64_t dk = (uint64_t)(kk * 32 / 16);
+                    // dS_j starts from zero in every block
+                    const uint32_t acc = (st > 0 || tc > 0 || kk > 0) ? 1u : 0u;
+                    mma_tf32_ts(dS, ahi + kk * 8, dbh + dk, idesc_v, acc);
+                    mma_tf32_ts(dS, ahi + kk * 8, dbl + dk, idesc_v, 1u);
+                    mma_tf32_ts(dS, alo + kk * 8, dbh + dk, idesc_v, 1u);
+                  }
+                  mma_commit(&stg_free[b]);
                 }
-                if (elect_one()) mma_commit(&stg_free[b]);
+                __syncwarp();
               }
               if (elect_one()) mma_commit(&v_free[vs]);
             }
