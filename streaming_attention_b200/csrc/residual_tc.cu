@@ -330,22 +330,27 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
         const uint32_t vt = smem_u32(smem + sp * L::kStage + 2 * L::kKT);
         const uint32_t ph = tmem + L::kS0 + 128 * bp;
         const uint32_t pl = ph + 64;
+        // one elected lane issues the tile's MMAs and commits back to back; the
+        // descriptors' start address field (address >> 4) is advanced in place
+        if (elect_one()) {
+          const uint64_t vd = sdesc_sw128(vt, 16, 1024);
 #pragma unroll
-        for (int kk = 0; kk < kTile / 8; ++kk) {
-          // 8 keys of 32-key chunk kk / 4: rows = value columns (hi rows, then lo rows)
-          const uint32_t vc = vt + (kk >> 2) * (2 * DVP * 128) + (kk & 3) * 32;
-          const uint64_t bh_ = sdesc_sw128(vc, 16, 1024);
-          if (elect_one()) mma_tf32_ts(tmem + L::kO, ph + kk * 8, bh_, idesc_pv, (tp > 0 || kk > 0) ? 1u : 0u);
-          if (L::kPVStack) {
-            if (elect_one()) mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
-          } else {
-            const uint64_t bl_ = sdesc_sw128(vc + DVP * 128, 16, 1024);
-            if (elect_one()) mma_tf32_ts(tmem + L::kO, ph + kk * 8, bl_, idesc_pv, 1u);
-            if (elect_one()) mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
+          for (int kk = 0; kk < kTile / 8; ++kk) {
+            // 8 keys of 32-key chunk kk / 4: rows = value columns (hi rows, then lo rows)
+            const uint64_t bh_ = vd + (uint64_t)(((kk >> 2) * (2 * DVP * 128) + (kk & 3) * 32) >> 4);
+            mma_tf32_ts(tmem + L::kO, ph + kk * 8, bh_, idesc_pv, (tp > 0 || kk > 0) ? 1u : 0u);
+            if (L::kPVStack) {
+              mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
+            } else {
+              const uint64_t bl_ = bh_ + (uint64_t)((DVP * 128) >> 4);
+              mma_tf32_ts(tmem + L::kO, ph + kk * 8, bl_, idesc_pv, 1u);
+              mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
+            }
           }
+          mma_commit(&empty[sp]);
+          mma_commit(&sfree[bp]);
         }
-        if (elect_one()) mma_commit(&empty[sp]);
-        if (elect_one()) mma_commit(&sfree[bp]);
+        __syncwarp();
         return true;
       };
       for (int t = 0; ok && t < T; ++t) {
@@ -357,15 +362,18 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
         tc_fence_after();
         const uint32_t kh = smem_u32(smem + s * L::kStage);
         const uint32_t dS = tmem + L::kS0 + 128 * b;
+        if (elect_one()) {
+          const uint64_t kd = sdesc_sw128(kh, 16, 1024);
 #pragma unroll
-        for (int kk = 0; kk < DP / 8; ++kk) {
-          // N = 128 rows: the chunk's 64 hi rows, then its 64 lo rows
-          const uint32_t off = (kk >> 2) * (2 * kTile * 128) + (kk & 3) * 32;
-          const uint64_t bk = sdesc_sw128(kh + off, 16, 1024);
-          if (elect_one()) mma_tf32_ts(dS, tmem + L::kQhi + kk * 8, bk, idesc_qk, kk > 0 ? 1u : 0u);
-          if (elect_one()) mma_tf32_ts(dS, tmem + L::kQlo + kk * 8, bk, idesc_qk, 1u);
+          for (int kk = 0; kk < DP / 8; ++kk) {
+            // N = 128 rows: the chunk's 64 hi rows, then its 64 lo rows
+            const uint64_t bk = kd + (uint64_t)(((kk >> 2) * (2 * kTile * 128) + (kk & 3) * 32) >> 4);
+            mma_tf32_ts(dS, tmem + L::kQhi + kk * 8, bk, idesc_qk, kk > 0 ? 1u : 0u);
+            mma_tf32_ts(dS, tmem + L::kQlo + kk * 8, bk, idesc_qk, 1u);
+          }
+          mma_commit(&sfull[b]);
         }
-        if (elect_one()) mma_commit(&sfull[b]);
+        __syncwarp();
         if (t >= 1 && !issue_pv(t - 1)) { ok = false; break; }
       }
       if (ok && T > 0) ok = issue_pv(T - 1);
