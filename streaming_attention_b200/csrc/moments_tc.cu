@@ -808,8 +808,20 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
       float sd[FT];
 #pragma unroll
       for (int j = 0; j < FT; ++j) sd[j] = 0.0f;
+      // as in the query phase, a chunk's TMEM stores complete under the next
+      // chunk's arithmetic (within a key tile)
+      int held = -1;
+      auto hand_over = [&]() {
+        if (held >= 0) {
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&stg_full[held]);
+          held = -1;
+        }
+      };
       for (int st = 0; ok && st < sub; ++st) {
         if (!(st == 0 && kstaged)) {
+          hand_over();
           gen_sync();  // everyone is done with X
           stage_keys(c, st);
           gen_sync();
@@ -821,8 +833,6 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
           for (int j = 0; j < FT; ++j) {
             if (!ok || j >= ntiles) break;
             const int b = stg_use % kNStg;
-            if (stg_use >= kNStg && !mbar_wait(&stg_free[b], ((stg_use / kNStg) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
-            ++stg_use;
             const uint2 fc = fco[j * 256 + gi];
             const uint32_t fi = fc.x;
             const float cf = __uint_as_float(fc.y);
@@ -850,14 +860,16 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
               }
             }
             sd[j] += fsum;
+            hand_over();
+            if (stg_use >= kNStg && !mbar_wait(&stg_free[b], ((stg_use / kNStg) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+            ++stg_use;
             tmem_st16(la + L::kStg + b * 2 * kChunk + half * 16, hi);
             tmem_st16(la + L::kStg + b * 2 * kChunk + kChunk + half * 16, lo);
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(&stg_full[b]);
+            held = b;
           }
         }
       }
+      hand_over();
       // s += the features of this block's keys: the halves' sums meet in shared memory
       if (half == 1) {
 #pragma unroll
