@@ -3,9 +3,10 @@ attention forward on B200, one process per GPU.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config 3] [--impl ours|reference]
 
-For N > 1 launch under torchrun (one rank per GPU, NCCL); the B*H sequences
-of the configuration are split into N contiguous shards with no
-communication (every sequence is independent).  Rank 0 prints one JSON line.
+For N > 1 launch under torchrun (one rank per GPU, NCCL).  The headline
+configuration (config 3 by default) splits its B*H sequences into N
+contiguous shards with no communication (every sequence is independent).
+Rank 0 prints one JSON line.
 
 A step is one forward of the rank's shard.  ``value`` is timed with the
 inputs resident in HBM; ``e2e`` times the public entry point from pinned host
@@ -14,10 +15,22 @@ the output inside the timed region.  Inputs (>= 1.5 GB for the default
 configuration) are larger than the 126 MB L2, so no flush is needed between
 steps.
 
+Extra keys of the same line (after the headline's timed region):
+  ``kernels``         per-stage device times of the timed forward itself
+                      (CUDA events recorded by sa_fast_attention between its
+                      launches on the launching stream, sa_set_stage_events)
+  ``configs``         configs 1, 2 and 4 at full size (heads sharded over the
+                      ranks), with rel-L2 against exact attention
+  ``nshard_config5``  config 5 (64 sequences of 262144 tokens): on one GPU the
+                      single-device forward; on N GPUs the N-sharded forward
+                      (zig-zag chunks, NCCL all-gather of moment states and
+                      reps, device prefix scan) with in-run parity against
+                      the single-device forward on two sequences
+
 ``--impl reference`` times the CPU restatement of the reference algorithm
 (oracle/oracle.py in float32 numpy; the reference itself is a Python/torch
 package that is not present on the GPU host) on bounded samples of the same
-workload.
+workload, with every host core.
 """
 
 from __future__ import annotations
@@ -29,6 +42,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -43,6 +57,10 @@ UNIT = "queries/s"
 CLOCK_FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+# A tf32 tcgen05.mma of M = 128, N = 64, K = 8 issues every 32 cycles per SM
+# when run back to back (measured on B200): 2*128*64*8 / 32 = 4096 flop/clk/SM.
+RAW_TF32_FLOP_PER_CLK_PER_SM = 4096
+STAGES = ("splits", "compress", "moments", "residual")
 
 
 def parse_args():
@@ -56,18 +74,22 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-exact", action="store_true",
                     help="skip the accuracy check against exact attention and the exact kernel's timing")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the extra keys (configs 1/2/4 and config 5)")
+    ap.add_argument("--exact-only", action="store_true",
+                    help="profiling aid: time only the exact flash kernel on the configuration's inputs")
     ap.add_argument("--cpu-sample-heads", type=int, default=0, help="heads in the CPU sample (0 = auto)")
     ap.add_argument("--bh", type=int, default=0,
                     help="profiling only: replace B*H by this many sequences (B=1) to make a small case")
     return ap.parse_args()
 
 
-def bench_config(args) -> dict:
+def bench_config(cfg_id: int, bh: int = 0) -> dict:
     from streaming_attention_b200 import workloads
 
-    if args.bh:
-        return workloads.config(args.config, B=1, H=args.bh)
-    return workloads.config(args.config)
+    if bh:
+        return workloads.config(cfg_id, B=1, H=bh)
+    return workloads.config(cfg_id)
 
 
 # ---------------------------------------------------------------------------
@@ -109,12 +131,27 @@ def algorithmic_work(c: dict) -> dict:
     }
 
 
+def launches_per_forward(c: dict) -> int:
+    """Kernels sa_fast_attention launches for config c: the k / v operand
+    splits, the compressor and the split of its rep values, the moment scan,
+    the residual (tensor-core shapes; the CUDA-core shapes launch fewer)."""
+    d, dv, bs = c["d"], c["dv"], c["block_size"]
+    tc = d <= 64 and dv <= 128 and bs % 4 == 0
+    groups = dv <= 64 and d <= 128 and bs % 4 == 0
+    compress = c["compressor"] != "none" and c["N"] > bs
+    n = (1 if tc else 0) + (1 if (tc or groups) else 0)
+    n += (1 + (1 if tc else 0)) if compress else 0
+    return n + 2
+
+
 class ClockSampler:
-    """nvidia-smi samples of this GPU's clocks while the timed region runs."""
+    """nvidia-smi samples of this GPU's clocks while the timed region runs
+    (written to a temporary file, summarised into the JSON line)."""
 
     def __init__(self, device_index: int):
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{device_index}.csv")
+        fd, self.path = tempfile.mkstemp(prefix=f"sa_clocks_{device_index}_", suffix=".csv")
+        os.close(fd)
         try:
             uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
         except Exception:
@@ -123,7 +160,6 @@ class ClockSampler:
 
     def __enter__(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
             cmd = ["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
             if self.uuid:
                 cmd += ["-i", self.uuid]
@@ -148,6 +184,11 @@ class ClockSampler:
             rows = [r.split(", ") for r in open(self.path).read().strip().splitlines() if r.count(",") >= 9]
         except Exception:
             rows = []
+        finally:
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
@@ -156,30 +197,6 @@ class ClockSampler:
         reasons = sorted({names[j] for r in rows for j in range(4) if r[6 + j].strip().lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(rows)}
-
-
-def tf32_gemm_peak_tflops(dev: torch.device) -> float:
-    """Dense TF32 tensor-core throughput of this GPU, measured as a cuBLAS TF32
-    GEMM (8192^3, best of 5): the denominator of the tensor-core kernels."""
-    old = torch.backends.cuda.matmul.allow_tf32
-    torch.backends.cuda.matmul.allow_tf32 = True
-    try:
-        n = 8192
-        a = torch.randn(n, n, device=dev)
-        b = torch.randn(n, n, device=dev)
-        c = a @ b
-        best = float("inf")
-        for _ in range(5):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            torch.mm(a, b, out=c)
-            e1.record()
-            torch.cuda.synchronize(dev)
-            best = min(best, e0.elapsed_time(e1) / 1e3)
-        del a, b, c
-        return 2.0 * n ** 3 / best / 1e12
-    finally:
-        torch.backends.cuda.matmul.allow_tf32 = old
 
 
 def profiled_traffic(cfg_id: int) -> dict:
@@ -197,231 +214,155 @@ def profiled_traffic(cfg_id: int) -> dict:
     return out
 
 
-def measured_peaks() -> dict:
-    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+def roofline_peaks() -> dict:
+    """Fixed denominators: HBM and dense bf16 from MEASURED_PEAKS.json (the
+    driver's copy and cuBLAS measurements on this pool), dense TF32 as half of
+    the bf16 rate, and the ceiling of an fp32-accurate 3xTF32 product (three
+    TF32 MMAs per product) as a third of that."""
     try:
-        with open(path) as f:
-            return json.load(f)
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
     except Exception:
-        return {}
+        p = {}
+    if "bf16_tflops" in p:
+        bf16, src = float(p["bf16_tflops"]), "of measured"
+    else:
+        bf16, src = 1590.0, "of fallback"
+    hbm = float(p.get("hbm_gbs", 6650.0))
+    return {"bf16_tflops": bf16, "tf32_tflops": bf16 / 2, "x3tf32_tflops": bf16 / 6, "hbm_gbs": hbm,
+            "source": src, "hbm_source": "of measured" if "hbm_gbs" in p else "of fallback"}
 
 
-_FMA_SRC = r"""
-extern "C" __global__ void fma_probe(float* out, int iters) {
-  float a0 = threadIdx.x * 1e-7f, a1 = a0 + 1e-6f, a2 = a0 + 2e-6f, a3 = a0 + 3e-6f;
-  float a4 = a0 + 4e-6f, a5 = a0 + 5e-6f, a6 = a0 + 6e-6f, a7 = a0 + 7e-6f;
-  for (int i = 0; i < iters; ++i) {
-#pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      a0 = fmaf(a0, 0.9999f, 1e-7f); a1 = fmaf(a1, 0.9999f, 1e-7f);
-      a2 = fmaf(a2, 0.9999f, 1e-7f); a3 = fmaf(a3, 0.9999f, 1e-7f);
-      a4 = fmaf(a4, 0.9999f, 1e-7f); a5 = fmaf(a5, 0.9999f, 1e-7f);
-      a6 = fmaf(a6, 0.9999f, 1e-7f); a7 = fmaf(a7, 0.9999f, 1e-7f);
-    }
-  }
-  out[blockIdx.x * blockDim.x + threadIdx.x] = a0 + a1 + a2 + a3 + a4 + a5 + a6 + a7;
-}
-"""
+def raw_tf32_tflops(sm_mhz) -> float:
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    mhz = sm_mhz or 1965.0
+    return RAW_TF32_FLOP_PER_CLK_PER_SM * sms * mhz * 1e6 / 1e12
 
 
-def fp32_fma_peak_tflops(dev: torch.device) -> float:
-    """FP32 FMA-pipe throughput of this GPU, measured with a small NVRTC-compiled
-    kernel (8 independent FMA chains per thread, all SMs full)."""
-    from cuda.bindings import driver, nvrtc
+def reduce_max(ms: float, world: int, dev) -> float:
+    if world == 1:
+        return ms
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
 
-    prog = nvrtc.nvrtcCreateProgram(_FMA_SRC.encode(), b"fma_probe.cu", 0, [], [])[1]
-    opts = [b"--gpu-architecture=sm_100a"]
-    if nvrtc.nvrtcCompileProgram(prog, len(opts), opts)[0] != nvrtc.nvrtcResult.NVRTC_SUCCESS:
-        return float("nan")
-    size = nvrtc.nvrtcGetCUBINSize(prog)[1]
-    cubin = b" " * size
-    nvrtc.nvrtcGetCUBIN(prog, cubin)
+
+def barrier(world: int, dev) -> None:
+    if world > 1:
+        torch.distributed.barrier()
     torch.cuda.synchronize(dev)
-    mod = driver.cuModuleLoadData(cubin)[1]
-    fn = driver.cuModuleGetFunction(mod, b"fma_probe")[1]
-    sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    blocks, threads, iters = sms * 8, 256, 4096
-    out = torch.empty(blocks * threads, device=dev)
-    import ctypes
-    p_out = ctypes.c_void_p(out.data_ptr())
-    p_it = ctypes.c_int(iters)
-    args = (ctypes.c_void_p * 2)(ctypes.addressof(p_out), ctypes.addressof(p_it))
-    stream = torch.cuda.current_stream(dev).cuda_stream
-    best = float("inf")
-    for _ in range(5):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        driver.cuLaunchKernel(fn, blocks, 1, 1, threads, 1, 1, 0, stream, ctypes.addressof(args), 0)
-        e1.record()
-        torch.cuda.synchronize(dev)
-        best = min(best, e0.elapsed_time(e1) / 1e3)
-    driver.cuModuleUnload(mod)
-    flops = blocks * threads * iters * 16 * 8 * 2
-    return flops / best / 1e12
+
+
+def timed(fn, steps: int, warmup: int, world: int, dev) -> float:
+    """ms per call of fn() on the current stream, max over ranks."""
+    for _ in range(warmup):
+        fn()
+    barrier(world, dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        fn()
+    t1.record()
+    barrier(world, dev)
+    return reduce_max(t0.elapsed_time(t1), world, dev) / steps
+
+
+def rel_l2_over_ranks(out: torch.Tensor, exact: torch.Tensor, world: int) -> dict:
+    sums = torch.stack([(out - exact).double().pow(2).sum(), exact.double().pow(2).sum(),
+                        (out - exact).abs().max().double()])
+    if world > 1:
+        torch.distributed.all_reduce(sums[:2])
+        torch.distributed.all_reduce(sums[2:], op=torch.distributed.ReduceOp.MAX)
+    return {"rel_l2_vs_exact": math.sqrt(float(sums[0]) / max(float(sums[1]), 1e-300)),
+            "max_abs_vs_exact": float(sums[2])}
 
 
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
 
-class Staged:
-    """The forward as its three C-ABI launches, with CUDA events between them
-    so every kernel's device time is measured on the launching stream."""
+class Forward:
+    """The fused forward (sa_fast_attention) of one rank's sequences, inputs
+    resident in HBM, with its draw tables and workspace made once."""
 
-    def __init__(self, sa_lib, c, q3, k3, v3, head_range, dev):
-        from streaming_attention_b200 import draws
-        self.lib = sa_lib
+    def __init__(self, c, q3, k3, v3, head_range, dev):
+        from streaming_attention_b200 import _lib, draws
+        self.lib = _lib.load()
         self.c = c
         self.q3, self.k3, self.v3 = q3, k3, v3
         bh, n, d = q3.shape
-        dv = v3.shape[-1]
-        self.bh, self.n, self.d, self.dv = bh, n, d, dv
+        self.bh, self.n, self.d, self.dv = bh, n, d, v3.shape[-1]
         self.scale = float(1.0 / math.sqrt(d) if c["scale"] is None else c["scale"])
-        self.comp = {"none": 0, "sorted_pair": 1, "random": 2}[c["compressor"]]
+        self.comp = _lib.COMPRESSORS[c["compressor"]]
         self.tables = draws.draw_tables(seed=0, batch=c["B"], heads=c["H"], n=n, d=d, block_size=c["block_size"],
                                         compressor=c["compressor"], device=dev, head_range=head_range)
-        nc = self.tables.completed_blocks
-        m = self.tables.reps_per_block
-        R = nc * m if self.comp else 0
-        self.R = R
-        self.low = torch.empty(bh, n, dv + 1, device=dev)
-        self.out = torch.empty(bh, n, dv, device=dev)
-        self.rep_idx = torch.empty(bh, max(R, 1), device=dev, dtype=torch.int32)
-        self.rk = torch.empty(bh, max(R, 1), d, device=dev)
-        self.rv = torch.empty(bh, max(R, 1), dv, device=dev)
-        self.rw = torch.empty(bh, max(R, 1), device=dev)
+        self.out = torch.empty(bh, n, self.dv, device=dev)
         import ctypes
-        nbytes = ctypes.c_size_t(0)
-        sa_lib.sa_residual_combine_workspace_size(bh, n, d, dv, c["block_size"], self.comp, ctypes.byref(nbytes))
-        self.res_ws = torch.empty(max(int(nbytes.value), 256), device=dev, dtype=torch.uint8)
-        mb = ctypes.c_size_t(0)
-        sa_lib.sa_low_moments_workspace_size(bh, n, d, dv, c["degree"], c["block_size"], ctypes.byref(mb))
-        self.mom_ws = torch.empty(max(int(mb.value), 256), device=dev, dtype=torch.uint8)
-        self.times = {"compress": [], "moments": [], "residual": []}
-        # the fused entry point (the timed `value`)
         fb = ctypes.c_size_t(0)
-        sa_lib.sa_fast_attention_workspace_size(bh, n, d, dv, c["degree"], c["block_size"], self.comp,
-                                                ctypes.byref(fb))
+        _lib.check(self.lib.sa_fast_attention_workspace_size(bh, n, d, self.dv, c["degree"], c["block_size"],
+                                                             self.comp, ctypes.byref(fb)), "workspace size")
         self.ws = torch.empty(max(int(fb.value), 256), device=dev, dtype=torch.uint8)
-        tc = int(nbytes.value) > 0
-        # kernels per fused forward: (split k, split v,) compress, moments, residual
-        self.launches = (2 if tc else 0) + (1 if R else 0) + 2
+        self.launches = launches_per_forward(c)
 
-    def fused(self, stream):
+    def __call__(self):
         from streaming_attention_b200 import _lib
         c, t = self.c, self.tables
         ptr = lambda x: None if x is None else x.data_ptr()  # noqa: E731
+        stream = torch.cuda.current_stream().cuda_stream
         _lib.check(self.lib.sa_fast_attention(
             self.q3.data_ptr(), self.k3.data_ptr(), self.v3.data_ptr(), self.bh, self.n, self.d, self.dv,
-            c["degree"], c["block_size"], self.scale, self.comp, ptr(t.dirs), ptr(t.coins), ptr(t.perms), 1e-12,
-            self.out.data_ptr(), None, self.ws.data_ptr(), self.ws.numel(), stream), "sa_fast_attention")
+            self.c["degree"], self.c["block_size"], self.scale, self.comp, ptr(t.dirs), ptr(t.coins), ptr(t.perms),
+            1e-12, self.out.data_ptr(), None, self.ws.data_ptr(), self.ws.numel(), stream), "sa_fast_attention")
 
-    def step(self, stream, record=False):
-        from streaming_attention_b200 import _lib
-        c, t = self.c, self.tables
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
-        if record:
-            ev[0].record()
-        if self.R:
-            _lib.check(self.lib.sa_compress_blocks(
-                self.k3.data_ptr(), self.v3.data_ptr(), self.bh, self.n, self.d, self.dv, c["block_size"],
-                self.comp, t.dirs.data_ptr() if t.dirs is not None else None,
-                t.coins.data_ptr() if t.coins is not None else None,
-                t.perms.data_ptr() if t.perms is not None else None, self.rep_idx.data_ptr(), self.rk.data_ptr(),
-                self.rv.data_ptr(), self.rw.data_ptr(), stream), "compress")
-        if record:
-            ev[1].record()
-        _lib.check(self.lib.sa_low_moments(self.q3.data_ptr(), self.k3.data_ptr(), self.v3.data_ptr(), self.bh,
-                                           self.n, self.d, self.dv, c["degree"], c["block_size"], self.scale,
-                                           self.low.data_ptr(), self.mom_ws.data_ptr(), self.mom_ws.numel(),
-                                           stream), "moments")
-        if record:
-            ev[2].record()
-        rk = self.rk if self.R else self.k3
-        rv = self.rv if self.R else self.v3
-        _lib.check(self.lib.sa_residual_combine(
-            self.q3.data_ptr(), self.k3.data_ptr(), self.v3.data_ptr(), rk.data_ptr(), rv.data_ptr(),
-            self.rw.data_ptr() if self.R else None, self.low.data_ptr(), self.bh, self.n, self.d, self.dv,
-            c["degree"], c["block_size"], self.comp, self.scale, 1e-12, self.out.data_ptr(), self.res_ws.data_ptr(),
-            self.res_ws.numel(), stream), "residual")
-        if record:
-            ev[3].record()
-        return ev
-
-    def collect(self, evs):
-        for ev in evs:
-            self.times["compress"].append(ev[0].elapsed_time(ev[1]))
-            self.times["moments"].append(ev[1].elapsed_time(ev[2]))
-            self.times["residual"].append(ev[2].elapsed_time(ev[3]))
+    def stage_times(self, steps: int) -> dict:
+        """Device time of each stage of the fused forward, from CUDA events that
+        sa_fast_attention records between its launches on the launching stream."""
+        import ctypes
+        per = {k: [] for k in STAGES}
+        for _ in range(steps):
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+            for e in evs:   # torch creates the CUDA event at its first record
+                e.record()
+            handles = (ctypes.c_void_p * 5)(*[ctypes.c_void_p(e.cuda_event) for e in evs])
+            self.lib.sa_set_stage_events(handles, 5)
+            try:
+                self()
+            finally:
+                self.lib.sa_set_stage_events(None, 0)
+            torch.cuda.synchronize()
+            for j, k in enumerate(STAGES):
+                per[k].append(evs[j].elapsed_time(evs[j + 1]))
+        return {k: statistics.mean(v) for k, v in per.items()}
 
 
-def run_nshard(args, rank, world, dev):
-    """Config 5 over several GPUs: every sequence split along N (rank r holds
-    tokens [r N/P, (r+1) N/P) of all sequences); each step is one collective
-    sharded forward (local scan, NCCL all-gather of states and reps, device
-    prefix scan, residual)."""
-    from streaming_attention_b200 import nshard, workloads
-
-    c = bench_config(args)
-    N, P = c["N"], world
-    chunks = nshard.owned_chunks(rank, world, "zigzag")
-    L = N // (P * len(chunks))
-    q, k, v = workloads.make_inputs(c, seed=0, device=dev, generator_device="cuda")
-    q, k, v = (torch.cat([x[:, :, j * L:(j + 1) * L] for j in chunks], dim=2).contiguous() for x in (q, k, v))
-    torch.cuda.empty_cache()
-    kw = dict(degree=c["degree"], block_size=c["block_size"], scale=c["scale"], compressor=c["compressor"], seed=0)
-
-    def step():
-        return nshard.fast_article_causal_attention_nshard(q, k, v, rank=rank, world=world, **kw)
-
-    def barrier():
-        torch.distributed.barrier()
-        torch.cuda.synchronize(dev)
-
-    for _ in range(args.warmup):
-        step()
-    barrier()
-    with ClockSampler(dev.index) as clk:
-        barrier()
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record()
-        for _ in range(args.steps):
-            step()
-        t1.record()
-        barrier()
-    ms_max = reduce_max(t0.elapsed_time(t1), world, dev)
-    out = None
-    if rank == 0:
-        work = algorithmic_work(c)
-        flops = (work["moment_flops"] + work["residual_flops"]) * c["B"] * c["H"]
-        tf32_peak = tf32_gemm_peak_tflops(dev)
-        achieved = flops * args.steps / (ms_max / 1e3) / 1e12 / world
-        out = {
-            "metric": METRIC, "value": c["B"] * c["H"] * N * args.steps / (ms_max / 1e3), "unit": UNIT,
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded, CUDA generator)",
-            "config": {"workload": workload_name(c, args.config), "B": c["B"], "H": c["H"], "N": N, "d": c["d"],
-                       "dv": c["dv"], "degree": c["degree"], "block_size": c["block_size"],
-                       "compressor": c["compressor"],
-                       "parallelism": f"N sharded over {world} GPU(s) in zig-zag chunk pairs: NCCL all-gather "
-                                      "of moment states and reps",
-                       "l2": "inputs larger than L2 (no flush needed)"},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
-                         "frac": achieved / tf32_peak, "frac_3xtf32": 3 * achieved / tf32_peak,
-                         "kernel": "whole sharded forward, per GPU", "traffic": None,
-                         "peak_source": "measured cuBLAS TF32 GEMM (8192^3) in this run"},
-            "e2e": None, "gpu_launches": None, "clocks": clk.summary(),
-        }
-    return out, c
+def kernel_table(c: dict, stage_ms: dict, per: int, peaks: dict, sm_mhz) -> dict:
+    work = algorithmic_work(c)
+    total = sum(stage_ms.values())
+    raw = raw_tf32_tflops(sm_mhz)
+    out = {}
+    for k, ms in stage_ms.items():
+        out[k] = {"ms": ms, "share": ms / total if total else None}
+    for name, key in (("moments", "moment_flops"), ("residual", "residual_flops")):
+        if stage_ms.get(name, 0) > 0:
+            tfl = work[key] * per / (stage_ms[name] / 1e3) / 1e12
+            out[name].update({"tflops": tfl, "bound": "tensor (3xTF32)",
+                              "frac_3xtf32": tfl / peaks["x3tf32_tflops"],
+                              "frac_tf32": tfl / peaks["tf32_tflops"],
+                              "frac_3xtf32_raw_rate": 3 * tfl / raw})
+    if stage_ms.get("compress", 0) > 0 and work["compress_bytes"]:
+        gbs = work["compress_bytes"] * per / (stage_ms["compress"] / 1e3) / 1e9
+        out["compress"].update({"gbs": gbs, "bound": "hbm", "frac_hbm": gbs / peaks["hbm_gbs"],
+                                "includes": "the compressor and the split of its rep values"})
+    out["splits"]["includes"] = "tf32 hi/lo splits of k (rows) and v (transposed)"
+    return out
 
 
 def run_ours(args, rank, world, dev):
     import streaming_attention_b200 as sa
-    from streaming_attention_b200 import _lib, workloads
+    from streaming_attention_b200 import workloads
 
-    c = bench_config(args)
+    c = bench_config(args.config, args.bh)
     bh_total = c["B"] * c["H"]
     if bh_total % world:
         raise SystemExit(f"B*H={bh_total} does not split over {world} GPUs")
@@ -429,38 +370,26 @@ def run_ours(args, rank, world, dev):
     h0, h1 = rank * per, (rank + 1) * per
     q, k, v = workloads.make_inputs(c, seed=0, device=dev, generator_device="cuda", heads=(h0, h1))
     q3, k3, v3 = q.reshape(per, c["N"], c["d"]), k.reshape(per, c["N"], c["d"]), v.reshape(per, c["N"], c["dv"])
-    lib = _lib.load()
-    st = Staged(lib, c, q3, k3, v3, (h0, h1), dev)
-    stream = torch.cuda.current_stream(dev).cuda_stream
-
-    def barrier():
-        if world > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize(dev)
+    fwd = Forward(c, q3, k3, v3, (h0, h1), dev)
+    peaks = roofline_peaks()
 
     # the headline: the fused entry point, inputs resident in HBM
     for _ in range(args.warmup):
-        st.fused(stream)
-    barrier()
+        fwd()
+    barrier(world, dev)
     with ClockSampler(dev.index) as clk:
-        barrier()
+        barrier(world, dev)
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
         for _ in range(args.steps):
-            st.fused(stream)
+            fwd()
         t1.record()
-        barrier()
-    ms = t0.elapsed_time(t1)
-    ms_max = reduce_max(ms, world, dev)
-    # per-kernel device times: the same kernels through the staged entry points,
-    # CUDA events between the launches on the launching stream
-    for _ in range(max(1, args.warmup)):
-        st.step(stream)
-    barrier()
-    evs = [st.step(stream, record=True) for _ in range(args.steps)]
-    barrier()
-    st.collect(evs)
+        barrier(world, dev)
+    ms_max = reduce_max(t0.elapsed_time(t1), world, dev)
+    clocks = clk.summary()
+    # per-stage device times of the same fused forward
+    stage_ms = fwd.stage_times(max(3, min(args.steps, 10)))
 
     # end to end through the public entry point, from pinned host buffers
     e2e = None
@@ -469,7 +398,6 @@ def run_ours(args, rank, world, dev):
         hout = torch.empty(q.shape[:-1] + (c["dv"],), dtype=torch.float32).pin_memory()
         kw = dict(degree=c["degree"], block_size=c["block_size"], scale=c["scale"], compressor=c["compressor"],
                   seed=0)
-
         grid = (c["B"], c["H"], c["N"])
 
         def e2e_step():
@@ -483,95 +411,51 @@ def run_ours(args, rank, world, dev):
                                                                 heads=c["H"], **kw)
             assert o.device.type == "cpu" and o.shape[-1] == c["dv"]
 
-        for _ in range(max(1, args.warmup)):
-            e2e_step()
-        barrier()
-        a0 = torch.cuda.Event(enable_timing=True)
-        a1 = torch.cuda.Event(enable_timing=True)
-        a0.record()
-        for _ in range(args.steps):
-            e2e_step()
-        a1.record()
-        barrier()
-        e2e_ms = reduce_max(a0.elapsed_time(a1), world, dev)
-        e2e = {"value": bh_total * c["N"] * args.steps / (e2e_ms / 1e3), "unit": UNIT,
+        e2e_ms = timed(e2e_step, args.steps, max(1, args.warmup), world, dev)
+        e2e = {"value": bh_total * c["N"] / (e2e_ms / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": int((hq.numel() + hk.numel() + hv.numel()) * 4 * world),
-               "d2h_bytes_per_step": int(hout.numel() * 4 * world), "ms_per_step": e2e_ms / args.steps}
+               "d2h_bytes_per_step": int(hout.numel() * 4 * world), "ms_per_step": e2e_ms}
+        del hq, hk, hv, hout
 
     # the metric's accuracy part: the timed output against exact causal
     # attention (this library's fp32-accurate flash kernel) on the same inputs,
     # over every rank's heads; and that exact kernel timed on them as a comparator
     accuracy = exact = None
     if not args.no_exact:
-        st.fused(stream)
-        exact_out = sa.triton_flash_causal_attention(q3[None], k3[None], v3[None], scale=st.scale)[0]
-        sums = torch.stack([(st.out - exact_out).double().pow(2).sum(), exact_out.double().pow(2).sum(),
-                            (st.out - exact_out).abs().max().double()])
-        if world > 1:
-            torch.distributed.all_reduce(sums[:2])
-            torch.distributed.all_reduce(sums[2:], op=torch.distributed.ReduceOp.MAX)
-        accuracy = {"rel_l2_vs_exact": math.sqrt(float(sums[0]) / max(float(sums[1]), 1e-300)),
-                    "max_abs_vs_exact": float(sums[2]),
-                    "exact": "causal softmax attention, triton_flash_causal_attention (3xTF32 tensor cores)"}
+        fwd()
+        exact_out = sa.triton_flash_causal_attention(q3[None], k3[None], v3[None], scale=fwd.scale)[0]
+        accuracy = rel_l2_over_ranks(fwd.out, exact_out, world)
+        accuracy["exact"] = "causal softmax attention, triton_flash_causal_attention (3xTF32 tensor cores)"
         del exact_out
-        for _ in range(2):
-            sa.triton_flash_causal_attention(q3[None], k3[None], v3[None], scale=st.scale)
-        barrier()
-        x0 = torch.cuda.Event(enable_timing=True)
-        x1 = torch.cuda.Event(enable_timing=True)
-        x_steps = max(1, min(args.steps, 5))
-        x0.record()
-        for _ in range(x_steps):
-            sa.triton_flash_causal_attention(q3[None], k3[None], v3[None], scale=st.scale)
-        x1.record()
-        barrier()
-        x_ms = reduce_max(x0.elapsed_time(x1), world, dev) / x_steps
-        exact = {"value": bh_total * c["N"] / (x_ms / 1e3), "unit": UNIT, "ms_per_step": x_ms, "steps": x_steps,
+        x_ms = timed(lambda: sa.triton_flash_causal_attention(q3[None], k3[None], v3[None], scale=fwd.scale),
+                     max(1, min(args.steps, 5)), 2, world, dev)
+        exact = {"value": bh_total * c["N"] / (x_ms / 1e3), "unit": UNIT, "ms_per_step": x_ms,
                  "what": "exact causal attention on the same inputs (the comparator, not the headline)"}
 
     out = None
     if rank == 0:
         work = algorithmic_work(c)
-        avg = {k_: statistics.mean(v_) for k_, v_ in st.times.items() if v_}
-        dominant = max(avg, key=avg.get)
-        peaks = measured_peaks()
-        try:
-            fma_peak = fp32_fma_peak_tflops(dev)
-        except Exception as exc:  # the probe is a measurement aid only
-            print(f"fp32 probe failed: {exc!r}", file=sys.stderr)
-            fma_peak = float("nan")
-        tf32_peak = tf32_gemm_peak_tflops(dev)
-        hbm_peak = peaks.get("hbm_gbs", 6650.0)
-        # full-size bytes per launch at one GPU; a rank's launch covers per / bh_total of it
+        kernels = kernel_table(c, stage_ms, per, peaks, clocks.get("sm_mhz"))
+        dominant = max(STAGES, key=lambda s: stage_ms.get(s, 0.0))
         traffic = {k_: v_ * per / bh_total for k_, v_ in profiled_traffic(args.config).items()} if not args.bh else {}
-        # The contractions of both tensor-core kernels run on the TF32 tensor pipe
-        # with a 3xTF32 split (hi*hi + hi*lo + lo*hi per fp32 product), so their
-        # ceiling for fp32-accurate work is a third of the TF32 rate; both
-        # fractions are given.
-        kernels = {}
-        for name, t_ in avg.items():
-            kernels[name] = {"ms": t_, "share": t_ / sum(avg.values())}
-        for name, key in (("moments", "moment_flops"), ("residual", "residual_flops")):
-            tfl = work[key] * per / (avg[name] / 1e3) / 1e12
-            kernels[name].update({"tflops": tfl, "frac_tf32": tfl / tf32_peak,
-                                  "frac_3xtf32": 3.0 * tfl / tf32_peak})
-        kernels["residual"]["frac_fp32_fma"] = kernels["residual"]["tflops"] / fma_peak
-        if "compress" in avg and avg["compress"] > 0:
-            kernels["compress"]["gbs"] = work["compress_bytes"] * per / (avg["compress"] / 1e3) / 1e9
-            kernels["compress"]["frac_hbm"] = kernels["compress"]["gbs"] / hbm_peak
-        if dominant == "compress":
-            roof = {"bound": "hbm", "achieved": kernels["compress"]["gbs"], "peak": hbm_peak, "unit": "GB/s",
-                    "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured copy)"}
+        if dominant in ("compress", "splits"):
+            roof = {"bound": "hbm", "achieved": kernels[dominant].get("gbs"), "peak": peaks["hbm_gbs"],
+                    "unit": "GB/s", "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peaks['hbm_source']})"}
         else:
-            roof = {"bound": "tensor", "achieved": kernels[dominant]["tflops"], "peak": tf32_peak, "unit": "TFLOP/s",
-                    "peak_source": "measured cuBLAS TF32 GEMM (8192^3) in this run; bf16 of measured "
-                                   f"{peaks.get('bf16_tflops')} TFLOP/s for context",
-                    "frac_3xtf32": kernels[dominant]["frac_3xtf32"]}
-        roof["frac"] = roof["achieved"] / roof["peak"] if roof["peak"] else None
+            roof = {"bound": "tensor", "achieved": kernels[dominant]["tflops"], "peak": peaks["x3tf32_tflops"],
+                    "unit": "TFLOP/s",
+                    "peak_source": (f"3xTF32 ceiling: a third of dense TF32, which is half the dense bf16 rate "
+                                    f"{peaks['bf16_tflops']} TFLOP/s {peaks['source']} (MEASURED_PEAKS.json)"),
+                    "frac_tf32": kernels[dominant]["frac_tf32"],
+                    "frac_3xtf32_raw_rate": kernels[dominant]["frac_3xtf32_raw_rate"],
+                    "raw_rate_note": "raw tcgen05 tf32 MMA rate (4096 flop/clk/SM, measured) at the sampled "
+                                     "median SM clock; its third is the 3xTF32 ceiling of the hardware"}
+        roof["frac"] = roof["achieved"] / roof["peak"] if roof.get("achieved") and roof["peak"] else None
         roof["kernel"] = dominant
         roof["traffic"] = traffic.get(dominant)
         roof["algorithmic_per_launch"] = (work["compress_bytes"] if dominant == "compress"
                                           else work["moment_flops" if dominant == "moments" else "residual_flops"]) * per
+        roof["kernel_ms"] = stage_ms[dominant]
         value = bh_total * c["N"] * args.steps / (ms_max / 1e3)
         out = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -582,31 +466,191 @@ def run_ours(args, rank, world, dev):
                        "compressor": c["compressor"], "parallelism": f"heads sharded over {world} GPU(s)",
                        "l2": "inputs larger than L2 (no flush needed)"},
             "roofline": roof, "kernels": kernels,
-            "e2e": e2e, "gpu_launches": st.launches * args.steps, "accuracy": accuracy, "exact_attention": exact,
-            "clocks": clk.summary(), "fp32_fma_peak_tflops": fma_peak, "tf32_gemm_peak_tflops": tf32_peak,
+            "e2e": e2e, "gpu_launches": fwd.launches * args.steps, "accuracy": accuracy, "exact_attention": exact,
+            "clocks": clocks, "peaks": peaks,
         }
+    del fwd, q, k, v, q3, k3, v3
+    torch.cuda.empty_cache()
     return out, c
 
 
-def reduce_max(ms: float, world: int, dev) -> float:
+def run_exact_only(args, rank, world, dev):
+    """Profiling aid: the exact flash kernel alone on the configuration's inputs."""
+    import streaming_attention_b200 as sa
+    from streaming_attention_b200 import workloads
+
+    c = bench_config(args.config, args.bh)
+    per = c["B"] * c["H"] // world
+    q, k, v = workloads.make_inputs(c, seed=0, device=dev, generator_device="cuda",
+                                    heads=(rank * per, (rank + 1) * per))
+    s = workloads.attention_scale(c)
+    ms = timed(lambda: sa.triton_flash_causal_attention(q[None, :, 0], k[None, :, 0], v[None, :, 0], scale=s),
+               args.steps, args.warmup, world, dev)
+    if rank != 0:
+        return None
+    return {"metric": "exact causal attention, queries/s", "value": c["B"] * c["H"] * c["N"] / (ms / 1e3),
+            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "config": {"workload": workload_name(c, args.config)}, "what": "triton_flash_causal_attention only"}
+
+
+def run_extra_config(cfg_id: int, rank: int, world: int, dev, steps: int, warmup: int):
+    """One of configs 1, 2, 4 at full size, heads sharded over the ranks (config
+    1 is a single sequence: measured on one GPU only)."""
+    import streaming_attention_b200 as sa
+    from streaming_attention_b200 import workloads
+
+    c = bench_config(cfg_id)
+    bh_total = c["B"] * c["H"]
+    if bh_total % world:
+        return {"skipped": f"B*H={bh_total} does not split over {world} GPUs"}
+    per = bh_total // world
+    h0, h1 = rank * per, (rank + 1) * per
+    q, k, v = workloads.make_inputs(c, seed=0, device=dev, generator_device="cuda", heads=(h0, h1))
+    q3, k3, v3 = (x.reshape(per, c["N"], -1) for x in (q, k, v))
+    fwd = Forward(c, q3, k3, v3, (h0, h1), dev)
+    ms = timed(fwd, steps, warmup, world, dev)
+    stage_ms = fwd.stage_times(3)
+    exact_out = sa.triton_flash_causal_attention(q3[None], k3[None], v3[None], scale=fwd.scale)[0]
+    acc = rel_l2_over_ranks(fwd.out, exact_out, world)
+    res = None
+    if rank == 0:
+        peaks = roofline_peaks()
+        res = {"workload": workload_name(c, cfg_id), "value": bh_total * c["N"] / (ms / 1e3), "unit": UNIT,
+               "ms_per_step": ms, "steps": steps, "warmup": warmup,
+               "parallelism": f"heads sharded over {world} GPU(s)",
+               "kernels": kernel_table(c, stage_ms, per, peaks, None), **acc}
+    del fwd, q, k, v, q3, k3, v3, exact_out
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_config5(rank: int, world: int, dev, steps: int, warmup: int):
+    """Config 5: 64 sequences of 262144 tokens.  One GPU: the single-device
+    forward.  N GPUs: every sequence split along N into 2N zig-zag chunks
+    (NCCL all-gather of moment states and reps, device prefix scan), with
+    parity against the single-device forward on sequences 0 and 63."""
+    import streaming_attention_b200 as sa
+    from streaming_attention_b200 import fast, nshard, workloads
+
+    c = bench_config(5)
+    N, bh = c["N"], c["B"] * c["H"]
+    kw = dict(degree=c["degree"], block_size=c["block_size"], scale=c["scale"], compressor=c["compressor"], seed=0)
+    q, k, v = workloads.make_inputs(c, seed=0, device=dev, generator_device="cuda")
+    s = workloads.attention_scale(c)
+    sample = (0, bh - 1)
     if world == 1:
-        return ms
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    return float(t.item())
+        out_holder = {}
+
+        def step():
+            out_holder["o"] = sa.fast_article_causal_attention(q, k, v, **kw)
+
+        ms = timed(step, steps, warmup, world, dev)
+        o = out_holder.pop("o")
+        exact = sa.triton_flash_causal_attention(q[:, list(sample)], k[:, list(sample)], v[:, list(sample)],
+                                                 scale=s)
+        acc = rel_l2_over_ranks(o[:, list(sample)], exact, 1)
+        del o, exact
+        res = {"workload": workload_name(c, 5), "value": bh * N / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
+               "steps": steps, "warmup": warmup, "n_gpus": 1, "parallelism": "single device (no N split)",
+               "accuracy_sequences": list(sample), **acc}
+    else:
+        chunks = nshard.owned_chunks(rank, world, "zigzag")
+        L = N // (2 * world)
+        qs, ks, vs = (torch.cat([x[:, :, j * L:(j + 1) * L] for j in chunks], dim=2).contiguous() for x in (q, k, v))
+        holder = {}
+
+        def step():
+            holder["r"] = nshard.fast_article_causal_attention_nshard(qs, ks, vs, rank=rank, world=world,
+                                                                      return_rep_idx=True, **kw)
+
+        ms = timed(step, steps, warmup, world, dev)
+        out_sh, idx_sh = holder.pop("r")
+        # parity on the sampled sequences: gather their output chunks and rep
+        # indices from every rank (padded to a common size), rebuild them in
+        # chunk order on rank 0 and compare with the single-device forward
+        m_blk = (c["block_size"] + 1) // 2
+        rows_chunk = (L // c["block_size"]) * m_blk
+        o_part = out_sh[0, list(sample)].contiguous()                         # [2, 2L, dv]
+        i_part = torch.full((2, len(chunks), rows_chunk), -1, device=dev, dtype=torch.int32)
+        for slot, ix in enumerate(idx_sh):
+            if ix is not None:
+                i_part[:, slot, :ix.shape[1]] = ix[list(sample)]
+        o_all = [torch.empty_like(o_part) for _ in range(world)]
+        i_all = [torch.empty_like(i_part) for _ in range(world)]
+        torch.distributed.all_gather(o_all, o_part)
+        torch.distributed.all_gather(i_all, i_part)
+        res = None
+        if rank == 0:
+            o_full = torch.empty(2, N, c["dv"], device=dev)
+            i_full = []
+            owner = {}
+            for r in range(world):
+                for slot, j in enumerate(nshard.owned_chunks(r, world, "zigzag")):
+                    owner[j] = (r, slot)
+            for j in range(2 * world):
+                r, slot = owner[j]
+                o_full[:, j * L:(j + 1) * L] = o_all[r][:, slot * L:(slot + 1) * L]
+                i_full.append(i_all[r][:, slot])
+            i_full = torch.cat(i_full, dim=1)
+            rel, idx_equal = [], True
+            for t, hsel in enumerate(sample):
+                ref, ridx = fast._run(q[0, hsel][None].contiguous(), k[0, hsel][None].contiguous(),
+                                      v[0, hsel][None].contiguous(), batch=1, heads=bh, degree=c["degree"],
+                                      block_size=c["block_size"], scale=s, compressor=c["compressor"], seed=0,
+                                      eps=1e-12, want_rep_idx=True, head_range=(hsel, hsel + 1))
+                rel.append(float(torch.linalg.vector_norm((o_full[t] - ref[0]).double())
+                                 / torch.linalg.vector_norm(ref[0].double())))
+                got = i_full[t][i_full[t] >= 0]
+                idx_equal = idx_equal and torch.equal(got, ridx[0])
+            res = {"workload": workload_name(c, 5), "value": bh * N / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
+                   "steps": steps, "warmup": warmup, "n_gpus": world,
+                   "parallelism": f"N sharded over {world} GPUs in zig-zag chunk pairs: NCCL all-gather of "
+                                  "moment states and reps, device prefix scan",
+                   "parity": {"sequences": list(sample), "rel_l2_vs_single_device": max(rel),
+                              "rep_idx_equal": bool(idx_equal), "tolerance": 1e-5,
+                              "ok": bool(max(rel) <= 1e-5 and idx_equal)}}
+        del out_sh, idx_sh, qs, ks, vs
+    del q, k, v
+    torch.cuda.empty_cache()
+    return res
 
 
 # ---------------------------------------------------------------------------
 # CPU: the oracle port (the reference's algorithm in float32 numpy)
 # ---------------------------------------------------------------------------
 
-def cpu_threads() -> int:
+def host_cpu() -> dict:
+    """Host cores the CPU runs may use, and what they are."""
     try:
-        from threadpoolctl import threadpool_info
-        info = threadpool_info()
-        return max([i.get("num_threads", 1) for i in info] or [1])
+        avail = len(os.sched_getaffinity(0))
     except Exception:
-        return os.cpu_count() or 1
+        avail = os.cpu_count() or 1
+    try:
+        import psutil
+        phys = psutil.cpu_count(logical=False) or avail
+    except Exception:
+        phys = avail
+    model = "unknown"
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"nproc": os.cpu_count(), "available": avail, "physical": phys, "model": model,
+            "threads": max(1, min(avail, phys))}
+
+
+def set_cpu_threads(n: int) -> None:
+    """Every host thread pool (torch and numpy's BLAS) to n threads; torchrun
+    sets OMP_NUM_THREADS=1 for its workers, which this overrides."""
+    torch.set_num_threads(n)
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(limits=n)
+    except Exception:
+        pass
 
 
 def cpu_sample(c: dict, heads: int, seed: int = 0):
@@ -630,11 +674,11 @@ def auto_sample_heads(c: dict, budget_s: float) -> int:
 
 
 def run_reference(args, rank, world):
-    from streaming_attention_b200 import workloads
-
     if rank != 0:
         return None
-    c = bench_config(args)
+    cpu = host_cpu()
+    set_cpu_threads(cpu["threads"])
+    c = bench_config(args.config, args.bh)
     heads = args.cpu_sample_heads or auto_sample_heads(c, 2.0)
     for _ in range(args.warmup):
         cpu_sample(c, heads)
@@ -647,7 +691,8 @@ def run_reference(args, rank, world):
         "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, CPU generator)",
         "config": {"workload": workload_name(c, args.config)},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu["threads"], "kind": "port", "sample": sample,
+                         "host": cpu},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -670,19 +715,36 @@ def main():
     torch.cuda.set_device(dev)
     if world > 1:
         import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                             device_id=dev)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     try:
-        if args.config == 5 and world > 1:
-            line, c = run_nshard(args, rank, world, dev)
-        else:
-            line, c = run_ours(args, rank, world, dev)
+        if args.exact_only:
+            line = run_exact_only(args, rank, world, dev)
+            if rank == 0:
+                print(json.dumps(line), flush=True)
+            return
+        line, c = run_ours(args, rank, world, dev)
+        if not args.no_extra and not args.bh:
+            xs, xw = max(1, min(args.steps, 5)), max(1, min(args.warmup, 3))
+            configs = {}
+            for cfg_id in (1, 2, 4):
+                if cfg_id == args.config:
+                    continue
+                if cfg_id == 1 and world > 1:
+                    configs["config1"] = {"skipped": "a single sequence: measured on one GPU"}
+                    continue
+                configs[f"config{cfg_id}"] = run_extra_config(cfg_id, rank, world, dev, xs, xw)
+            c5 = run_config5(rank, world, dev, max(1, min(args.steps, 3)), max(1, min(args.warmup, 2)))
+            if rank == 0:
+                line["configs"] = configs
+                line["nshard_config5"] = c5
         if rank == 0:
             if world == 1 and not args.no_cpu_baseline:
+                cpu = host_cpu()
+                set_cpu_threads(cpu["threads"])
                 heads = args.cpu_sample_heads or auto_sample_heads(c, 10.0)
                 secs = cpu_sample(c, heads)
-                line["cpu_baseline"] = {"value": heads * c["N"] / secs, "unit": UNIT, "cores": cpu_threads(),
-                                        "kind": "port",
+                line["cpu_baseline"] = {"value": heads * c["N"] / secs, "unit": UNIT, "cores": cpu["threads"],
+                                        "kind": "port", "host": cpu,
                                         "sample": f"{heads} of {c['B'] * c['H']} sequences (full N={c['N']}), "
                                                   "oracle/oracle.py in float32"}
             print(json.dumps(line), flush=True)

@@ -131,6 +131,31 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
                       float* out, int32_t* rep_idx, void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/* ---- run-time controls and status (no counterpart in the reference) -------
+ * The reference runs eagerly on one device and has neither device-side waits
+ * nor a status word; these entry points belong to this library's own runtime. */
+
+/* The launch status word that sa_fast_attention, sa_low_moments,
+ * sa_residual_combine, sa_article_segment_mean, sa_flash_causal_attention and
+ * the shard calls keep in the first 4 bytes of their workspace: synchronises
+ * `stream`, then returns SA_OK when no bounded device-side wait of the last
+ * call on that workspace gave up, else SA_ERR_TIMEOUT (sa_last_error() names
+ * the kernel's wait code). */
+int sa_workspace_status(const void* workspace, void* stream);
+
+/* How long one bounded device-side wait of the tensor-core kernels may take
+ * before its CTA gives up, drains what it issued, records SA_ERR_TIMEOUT's
+ * cause in the status word and leaves (the process-wide default, 0, means
+ * 2 s).  Applies to launches made after the call, from any thread. */
+int sa_set_wait_limit_ns(uint64_t limit_ns);
+
+/* Measurement hook for the calling host thread: while `count` > 0,
+ * sa_fast_attention records events[i] (cudaEvent_t handles, created by the
+ * caller) on its stream at stage boundaries: 0 start, 1 after the k / v
+ * operand splits, 2 after the compressor (and the split of its reps), 3 after
+ * the moment scan, 4 after the residual (the end).  count = 0 turns it off. */
+int sa_set_stage_events(void* const* events, int count);
+
 /* ---- streaming (decode) state: ArticleStreamingAttention -------------------
  * The reference keeps, per attention stream, a Taylor moment sketch and a
  * merge-and-reduce coreset (streaming_taylor_coreset_attention.py:229-616).

@@ -34,6 +34,9 @@ _sz = ctypes.c_size_t
 # name -> argtypes; every function returns int status
 SIGNATURES = {
     "sa_version": [],
+    "sa_workspace_status": [_vp, _vp],
+    "sa_set_wait_limit_ns": [ctypes.c_uint64],
+    "sa_set_stage_events": [ctypes.POINTER(_vp), _i32],
     "sa_feature_count": [_i32, _i32, ctypes.POINTER(_i64)],
     "sa_block_counts": [_i64, _i32, _i32, ctypes.POINTER(_i64), ctypes.POINTER(_i64)],
     "sa_compress_blocks": [_vp, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp],

@@ -14,6 +14,8 @@
 //    (SA_FORCE_SIMT=1, for A/B comparisons).
 #include <cuda.h>
 #include <stdarg.h>
+
+#include <atomic>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -62,6 +64,23 @@ int launch_flash_simt(const float* q, const float* k, const float* v, int64_t bh
 
 namespace {
 thread_local char g_err[512] = {0};
+// sa_set_wait_limit_ns (0: the default)
+std::atomic<uint64_t> g_wait_limit_ns{0};
+// sa_set_stage_events, per host thread
+constexpr int kMaxStageEvents = 8;
+thread_local cudaEvent_t g_stage_events[kMaxStageEvents] = {};
+thread_local int g_stage_count = 0;
+
+// Records stage event i of sa_fast_attention on stream s, if the calling
+// thread asked for it.
+void stage_mark(int i, cudaStream_t s) {
+  if (i < g_stage_count && g_stage_events[i]) cudaEventRecord(g_stage_events[i], s);
+}
+}  // namespace
+
+uint64_t wait_limit_ns() {
+  const uint64_t v = g_wait_limit_ns.load(std::memory_order_relaxed);
+  return v ? v : 2000000000ull;
 }
 
 int set_error(int code, const char* fmt, ...) {
@@ -400,7 +419,32 @@ using namespace sa;
 
 extern "C" {
 
-int sa_version(void) { return 100; }
+int sa_version(void) { return 110; }
+
+int sa_workspace_status(const void* workspace, void* stream) {
+  if (!workspace) return set_error(SA_ERR_INVALID_ARG, "null workspace");
+  int code = 0;
+  cudaError_t e = cudaMemcpyAsync(&code, workspace, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return set_error(SA_ERR_CUDA, "status read: %s", cudaGetErrorString(e));
+  if (code != 0) return set_error(SA_ERR_TIMEOUT, "a bounded device-side wait gave up (wait code %d)", code);
+  return SA_OK;
+}
+
+int sa_set_wait_limit_ns(uint64_t limit_ns) {
+  g_wait_limit_ns.store(limit_ns, std::memory_order_relaxed);
+  return SA_OK;
+}
+
+int sa_set_stage_events(void* const* events, int count) {
+  if (count < 0 || count > kMaxStageEvents)
+    return set_error(SA_ERR_INVALID_ARG, "count must lie in [0, %d]", kMaxStageEvents);
+  if (count > 0 && !events) return set_error(SA_ERR_INVALID_ARG, "null event array");
+  for (int i = 0; i < kMaxStageEvents; ++i)
+    g_stage_events[i] = i < count ? static_cast<cudaEvent_t>(events[i]) : nullptr;
+  g_stage_count = count;
+  return SA_OK;
+}
 
 const char* sa_last_error(void) { return g_err; }
 
@@ -571,6 +615,7 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
   int32_t* ridx = rep_idx ? rep_idx : reinterpret_cast<int32_t*>(ws + w.rep_idx);
   rc = reset_status(status, s);
   if (rc) return rc;
+  stage_mark(0, s);
 
   // operand splits shared by the tensor-core kernels
   float* khi = reinterpret_cast<float*>(ws + w.khi);
@@ -585,6 +630,7 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
     rc = launch_split_t(v, bh, n, dv, w.dvp, w.n_pad, vthi, vtlo, s);
     if (rc) return rc;
   }
+  stage_mark(1, s);
 
   // C1: compressor
   const float* rk = k;
@@ -623,6 +669,8 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
     }
   }
 
+  stage_mark(2, s);
+
   // M: low-degree moments
   if (w.groups > 0)
     rc = moments_tc_from_split(w, ws, vthi, vtlo, q, k, low, status, bh, n, d, dv, degree, block_size, scale, s);
@@ -630,16 +678,21 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
     rc = launch_low_moments(q, k, v, bh, n, d, dv, degree, block_size, scale, low, s);
   if (rc) return rc;
   const int groups = w.groups > 0 ? w.groups : 1;
+  stage_mark(3, s);
 
   // R: residual + combine
-  if (w.tc)
-    return residual_tc_from_split(w, rep_ops, cur_ops, rw, q, low, groups, out, status, bh, n, d, dv, degree,
-                                  block_size, reps_per_block(compressor, block_size), scale, eps, s);
-  if (groups > 1) {  // the CUDA-core residual reads one summed slice
-    rc = launch_sum_groups(low, groups, bh * n * (dv + 1), low, s);
-    if (rc) return rc;
+  if (w.tc) {
+    rc = residual_tc_from_split(w, rep_ops, cur_ops, rw, q, low, groups, out, status, bh, n, d, dv, degree,
+                                block_size, reps_per_block(compressor, block_size), scale, eps, s);
+  } else {
+    if (groups > 1)  // the CUDA-core residual reads one summed slice
+      rc = launch_sum_groups(low, groups, bh * n * (dv + 1), low, s);
+    if (!rc)
+      rc = launch_residual(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, block_size, compressor, scale, eps, out,
+                           s);
   }
-  return launch_residual(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, block_size, compressor, scale, eps, out, s);
+  if (!rc) stage_mark(4, s);
+  return rc;
 }
 
 

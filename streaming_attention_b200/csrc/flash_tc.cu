@@ -62,6 +62,7 @@ struct FlashParams {
   int64_t n;
   int d, dv;
   float scale;
+  uint64_t wait_ns;  // limit of one bounded wait
 };
 
 template <int DP, int DVP>
@@ -138,7 +139,7 @@ flash_tc_kernel(const __grid_constant__ CUtensorMap tm_kh, const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const Abort ab{abort_word, p.status};
+  const Abort ab{abort_word, p.status, p.wait_ns};
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -410,7 +411,7 @@ flash_tc_kernel(const __grid_constant__ CUtensorMap tm_kh, const __grid_constant
     lsum[half * 128 + row] = l;
     asm volatile("bar.sync 1, 256;" ::: "memory");
     const float l_all = lsum[row] + lsum[128 + row];
-    if (ok && mbar_wait(ofull, 0, ab, kErrWaitO)) {
+    if (ok && mbar_wait_warp(ofull, 0, ab, kErrWaitO)) {
       tc_fence_after();
       const float dmax = fmaxf(l_all, 1.0e-20f);
       float* orow = p.out + (h * p.n + (valid ? i : 0)) * (int64_t)p.dv;
@@ -466,7 +467,7 @@ int launch_flash_tc(const CUtensorMap* maps, const float* q, float* out, int* st
   if (bh == 0 || n == 0) return SA_OK;
   if (bh > 65535 || (n + kRowsQ - 1) / kRowsQ > 2147483647LL)
     return set_error(SA_ERR_UNSUPPORTED, "grid too large for the tensor-core flash kernel");
-  const FlashParams prm{q, out, status, n, d, dv, scale};
+  const FlashParams prm{q, out, status, n, d, dv, scale, wait_limit_ns()};
   const int dp = d <= 32 ? 32 : (d <= 64 ? 64 : 0);
   const int dvp = dv <= 32 ? 32 : (dv <= 64 ? 64 : (dv <= 128 ? 128 : 0));
   if (dp == 32 && dvp == 32) return launch_flash<32, 32>(maps, prm, bh, stream);

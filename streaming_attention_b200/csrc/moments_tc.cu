@@ -16,19 +16,26 @@
 // A segment position that is not a canonical monomial (c below the prefix, or
 // past d) gets key coefficient 0, so its state row stays exactly zero and its
 // query-side value never matters.  This spends ~10% extra MMA work (degree 2,
-// d = 64) to let every feature run be produced with vector loads.
+// d = 64) to let every feature run be produced with vector loads.  The key
+// coefficient (1/prod alpha!, or 0) is applied to a state row when its change
+// is folded into the master state, not to every key feature: for the
+// coefficients 1/2 and 1 that scaling is exact, so the state is the same.
 //
 // Work split: one CTA per (group of up to FT feature tiles of 128, sequence).
 // The CTA scans the sequence block by block:
 //   update phase  dS_j[128 features x dv] = Phi_k^T[features x tokens] . V   (M = features)
 //   query phase   Out_j[128 tokens x dv]  = Phi_q[tokens x features of j] . S_j (M = tokens)
 // Both feature matrices are generated on the CUDA cores directly into TMEM
-// (tcgen05.st), where they are the A operand.  Eight generator warps, two per
-// TMEM lane quarter: thread t of each half owns TMEM lane t, i.e. token t in
-// the query phase and feature t of the tile in the update phase, and each
-// half writes half of every chunk's columns.  V chunks (tf32 hi / fp32
-// remainder copies made by the transposing split pass) arrive by TMA, K-major
-// with the 128-byte swizzle: dv hi rows, then dv lo rows, of 32 tokens.
+// (tcgen05.st), where they are the A operand.  Sixteen generator warps, four
+// per TMEM lane quarter: thread t of each of the four column groups owns TMEM
+// lane t, i.e. token t in the query phase and feature t of the tile in the
+// update phase, and each column group writes a quarter of every chunk's
+// columns (one 8-feature segment, or 8 tokens).  Four warps per scheduler
+// hide the latency of each warp's dependent loads, products and TMEM stores.
+// A warp hands a finished chunk to the MMA issuer with one arrival (after
+// every lane's stores are complete).  V chunks (tf32 hi / fp32 remainder
+// copies made by the transposing split pass) arrive by TMA, K-major with the
+// 128-byte swizzle: dv hi rows, then dv lo rows, of 32 tokens.
 //
 // Each 8-wide K step takes the three products of 3xTF32 as three MMAs of
 // N = DVP into one accumulator: A_hi B_hi, A_hi B_lo, A_lo B_hi (the hi and
@@ -47,6 +54,10 @@
 // summed in registers.  The denominator column is a dot product with the same
 // features on the CUDA cores.  Each CTA writes its partial sums; the residual
 // kernel adds the groups.
+//
+// Every wait is bounded, including the generator warps' own barrier (an
+// mbarrier, not bar.sync): a role that gives up leaves its loops, and the
+// others then give up at their next wait instead of waiting for it forever.
 #include "sa_common.cuh"
 #include "tc_util.cuh"
 
@@ -64,13 +75,17 @@ using namespace tc;
 // stay NaN.
 __device__ __forceinline__ uint32_t tf32_trunc(float x) { return __float_as_uint(x) & 0xffffe000u; }
 
-
 constexpr int kRows = 128;      // tokens per sub-tile = features per tile = TMEM lanes
 constexpr int kChunk = 32;      // K columns per staged feature chunk
-constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 generators
+constexpr int kNCG = 4;         // column groups of generator warps (warps per TMEM lane quarter)
+constexpr int kGenWarps = 4 * kNCG;
+constexpr int kGenThreads = 32 * kGenWarps;
+constexpr int kThreads = 64 + kGenThreads;   // warp 0 TMA, warp 1 MMA, warps 2.. generators
+constexpr int kCgCols = kChunk / kNCG;       // chunk columns one column group writes (8)
 constexpr int kNStg = 3;        // TMEM staging buffers (32 hi + 32 lo columns each); 3 leave room
                                 // for 5 state tiles, so fewer feature groups per sequence
 constexpr int kXtStride = kRows + 4;   // transposed key tile row (floats)
+constexpr int kTileVals = 4 * (kRows * 64 / 4) / kGenThreads;   // row-tile floats a thread prefetches (16)
 
 constexpr int kErrMomWait = 201, kErrMomDrain = 202;
 
@@ -91,6 +106,7 @@ struct MomTCParams {
   //    sequence, e.g. earlier shards of a split sequence).
   int mode;
   float* den_io;
+  uint64_t wait_ns;   // limit of one bounded wait
 };
 
 template <int DVP>
@@ -190,37 +206,33 @@ __device__ float seg_key_coef(int p1, int p2, int c, int d, int t) {
   return 1.0f;
 }
 
-// named barrier among the 256 generator threads (warps 2..9)
-__device__ __forceinline__ void gen_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-
-// HC consecutive columns (16 or 32) of this thread's TMEM lane
-template <int HC>
-__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[HC]) {
-  if constexpr (HC == 32) {
-    tmem_ld32(taddr, v);
-  } else {
-    static_assert(HC == 16, "16 or 32 columns");
-    uint32_t r[16];
+// N consecutive 32-bit columns (8 or 16) of this thread's TMEM lane, then wait.
+template <int N>
+__device__ __forceinline__ void tmem_ld_wait(uint32_t taddr, float (&v)[N]) {
+  uint32_t r[N];
+  if constexpr (N == 16) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
         "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
-#pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+  } else {
+    static_assert(N == 8, "8 or 16 columns");
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
   }
   tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < N; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-// 16 consecutive 32-bit columns of this thread's TMEM lane (no wait).
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
+// 8 consecutive 32-bit columns of this thread's TMEM lane (no wait).
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
+               ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
 }
 
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
@@ -230,41 +242,40 @@ __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast
 //
 // Vector path (d % 4 == 0, 16-byte aligned rows): the first min(d, 64) columns
 // of the tile are cut into blocks of 8 rows x 4 float4 (64 contiguous bytes per
-// row); generator warp w takes blocks k * 8 + w, k < 8, and lane l the float4
-// (row 8 rb + l / 4, float4 column 4 cb + l % 4) of block (rb, cb).  A warp
-// access then covers eight 64-byte segments, and the transposed store of a key
-// tile meets at most two-way bank conflicts.  Scalar path: thread t reads row
-// t, columns [32 half, 32 half + 32).  Columns from 64 on are read when the
-// tile is stored.
-// The eight (row, float4 column) pairs of a thread, packed as 16-bit
-// (row << 8 | col4) entries of a uint4, 0xffff where the thread has no element;
+// row); generator warp w (0..15) takes blocks k * 16 + w, k < 4, and lane l the
+// float4 (row 8 rb + l / 4, float4 column 4 cb + l % 4) of block (rb, cb).  A
+// warp access then covers eight 64-byte segments.  Scalar path: thread t of
+// column group cg reads row t, columns [16 cg, 16 cg + 16).  Columns from 64 on
+// are read when the tile is stored.
+// The four (row, float4 column) pairs of a thread, packed as 16-bit
+// (row << 8 | col4) entries of a uint2, 0xffff where the thread has no element;
 // built once per CTA and kept in shared memory (not in registers across phases).
-__device__ __forceinline__ uint4 tile_map_entries(int d, int wg, int l) {
+__device__ __forceinline__ uint2 tile_map_entries(int d, int wg, int l) {
   const int d4 = min(d, 64) >> 2, cb = (d4 + 3) >> 2;
-  uint32_t w[4];
+  uint32_t w[2];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const int b = k * 8 + wg;
+  for (int k = 0; k < 4; ++k) {
+    const int b = k * kGenWarps + wg;
     const int rb = b / cb;
     const int row = 8 * rb + (l >> 2), col4 = 4 * (b - rb * cb) + (l & 3);
     const uint32_t e = (rb < 16 && col4 < d4) ? (uint32_t)((row << 8) | col4) : 0xffffu;
     if (k & 1) w[k >> 1] |= e << 16;
     else w[k >> 1] = e;
   }
-  return make_uint4(w[0], w[1], w[2], w[3]);
+  return make_uint2(w[0], w[1]);
 }
 
-__device__ __forceinline__ uint32_t tile_entry(const uint4& m, int k) {
-  const uint32_t w = (k >> 1) == 0 ? m.x : (k >> 1) == 1 ? m.y : (k >> 1) == 2 ? m.z : m.w;
+__device__ __forceinline__ uint32_t tile_entry(const uint2& m, int k) {
+  const uint32_t w = (k >> 1) == 0 ? m.x : m.y;
   return (k & 1) ? (w >> 16) : (w & 0xffffu);
 }
 
-__device__ __forceinline__ void rows_issue(const float* head, int64_t i0, int nvalid, int d, int t, int half,
-                                           bool vec, const uint4* tmap, float (&v)[32]) {
+__device__ __forceinline__ void rows_issue(const float* head, int64_t i0, int nvalid, int d, int t, int cg,
+                                           bool vec, const uint2* tmap, float (&v)[kTileVals]) {
   if (vec) {
-    const uint4 m = *tmap;
+    const uint2 m = *tmap;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < 4; ++k) {
       const uint32_t e = tile_entry(m, k);
       const int row = (int)(e >> 8), col4 = (int)(e & 255);
       float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -276,11 +287,11 @@ __device__ __forceinline__ void rows_issue(const float* head, int64_t i0, int nv
       v[4 * k + 3] = x.w;
     }
   } else {
-    const int a0 = half * 32;
+    const int a0 = cg * 16;
     const bool valid = t < nvalid;
     const float* src = head + (i0 + (valid ? t : 0)) * d + a0;
 #pragma unroll
-    for (int u = 0; u < 32; ++u) v[u] = (valid && a0 + u < d) ? __ldg(src + u) : 0.0f;
+    for (int u = 0; u < 16; ++u) v[u] = (valid && a0 + u < d) ? __ldg(src + u) : 0.0f;
   }
 }
 
@@ -290,7 +301,8 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
                   const MomTCParams p) {
   using L = MomLayout<DVP>;
   constexpr int FT = L::kFT;
-  constexpr int HC = DVP / 2;                              // state / output columns per half
+  constexpr int HC = DVP / kNCG;                           // state / output columns per column group
+  static_assert(HC == 8 || HC == 16, "column group share of the state");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sbuf = smem;                                    // [2][hi, lo]
@@ -302,23 +314,24 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
   const int xwords = max(max(kRows * XS, DX * kXtStride), kRows * (DVP + 1));
   uint32_t* segtab = reinterpret_cast<uint32_t*>(X + xwords);            // [FT*16]
   float* sden = reinterpret_cast<float*>(segtab + FT * 16);              // [FT*128]
-  float* xch = sden + FT * kRows;                                        // [2][128]
-  float* sdx = xch + 2 * kRows;                                          // [FT*128]
-  uint4* tmaps = reinterpret_cast<uint4*>(
-      (reinterpret_cast<uintptr_t>(sdx + FT * kRows) + 15) & ~uintptr_t(15));   // [256] tile load maps
-  uint2* fco = reinterpret_cast<uint2*>(tmaps + 256);                    // [FT][256] update-phase feature of a thread
-  uint64_t* bars = reinterpret_cast<uint64_t*>(fco + FT * 256);
-  uint64_t* stg_full = bars;                // [kNStg] 256 arrivals
+  float* xch = sden + FT * kRows;                                        // [kNCG][128]
+  float* sdx = xch + kNCG * kRows;                                       // [kNCG-1][FT*128]
+  uint2* tmaps = reinterpret_cast<uint2*>(
+      (reinterpret_cast<uintptr_t>(sdx + (kNCG - 1) * FT * kRows) + 15) & ~uintptr_t(15));   // [kGenThreads]
+  uint2* fco = tmaps + kGenThreads;                                      // [FT][128] update-phase feature of lane t
+  uint64_t* bars = reinterpret_cast<uint64_t*>(fco + FT * kRows);
+  uint64_t* stg_full = bars;                // [kNStg] one arrival per generator warp
   uint64_t* stg_free = bars + kNStg;        // [kNStg] commit
-  uint64_t* sb_full = bars + 2 * kNStg;     // [2] 256 arrivals
+  uint64_t* sb_full = bars + 2 * kNStg;     // [2] one arrival per generator warp
   uint64_t* sb_free = sb_full + 2;          // [2] commit
   uint64_t* v_full = sb_free + 2;           // [2] TMA
   uint64_t* v_free = v_full + 2;            // [2] commit
   uint64_t* out_full = v_free + 2;          // commit, once per query sub-tile
-  uint64_t* out_free = out_full + 1;        // 256 arrivals, once per sub-tile
+  uint64_t* out_free = out_full + 1;        // one arrival per generator warp, once per sub-tile
   uint64_t* u_done = out_free + 1;          // commit, once per update phase
   uint64_t* drain = u_done + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* gbar = drain + 1;               // the generator threads' own barrier
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbar + 1);
   int* abort_word = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -334,19 +347,20 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
 
   if (threadIdx.x == 0) {
     for (int b = 0; b < kNStg; ++b) {
-      mbar_init(&stg_full[b], 256);
+      mbar_init(&stg_full[b], kGenWarps);
       mbar_init(&stg_free[b], 1);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&sb_full[b], 256);
+      mbar_init(&sb_full[b], kGenWarps);
       mbar_init(&sb_free[b], 1);
       mbar_init(&v_full[b], 1);
       mbar_init(&v_free[b], 1);
     }
     mbar_init(out_full, 1);
-    mbar_init(out_free, 256);
+    mbar_init(out_free, kGenWarps);
     mbar_init(u_done, 1);
     mbar_init(drain, 1);
+    mbar_init(gbar, kGenThreads);
     *abort_word = 0;
     fence_mbar_init();
   }
@@ -355,8 +369,17 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     seg_of(seg0 + s, p.d, p.degree, p1, p2, c0);
     segtab[s] = (uint32_t)p1 | ((uint32_t)p2 << 10) | ((uint32_t)c0 << 20);
   }
-  for (int f = threadIdx.x; f < FT * kRows; f += kThreads)
+  __syncthreads();
+  for (int f = threadIdx.x; f < FT * kRows; f += kThreads) {
     sden[f] = p.mode == 2 ? p.den_io[((int64_t)g * p.bh + h) * (FT * kRows) + f] : 0.0f;
+    // the update-phase feature of lane t of tile j (f = j * 128 + t): its indices
+    // and key coefficient
+    const int j = f / kRows, t = f % kRows;
+    const uint32_t sg = segtab[j * 16 + (t >> 3)];
+    const int p1 = sg & 1023, p2 = (sg >> 10) & 1023, c = (int)(sg >> 20) + (t & 7);
+    const float cf = j < ntiles ? seg_key_coef(p1, p2, c, p.d, p.degree) : 0.0f;
+    fco[f] = make_uint2((uint32_t)p1 | ((uint32_t)p2 << 10) | ((uint32_t)c << 20), __float_as_uint(cf));
+  }
   if (threadIdx.x >= 64) tmaps[threadIdx.x - 64] = tile_map_entries(p.d, (threadIdx.x >> 5) - 2, threadIdx.x & 31);
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -366,7 +389,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const Abort ab{abort_word, p.status};
+  const Abort ab{abort_word, p.status, p.wait_ns};
   const float* qh = p.q + h * p.n * p.d;
   const float* kh = p.k + h * p.n * p.d;
 
@@ -500,15 +523,34 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     }
   } else {
     // -------------------------------------------------------------- generators
-    // two warps per TMEM lane quarter: `half` 0 (warps 2..5) and 1 (warps 6..9);
-    // thread t owns TMEM lane t, each half owns half of every chunk's columns
+    // four warps per TMEM lane quarter, one per column group cg: thread t owns
+    // TMEM lane t, and column group cg writes columns [8 cg, 8 cg + 8) of every
+    // chunk's hi and lo halves and columns [HC cg, HC cg + HC) of every state row
+    const int gi = threadIdx.x - 64;
+    const int cg = (warp - 2) >> 2;
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
     const int t = quarter * 32 + lane;                   // TMEM lane = token or feature
     const uint32_t la = tmem + ((uint32_t)(quarter * 32) << 16);
     int stg_use = 0, sb_use = 0, out_use = 0;
     bool ok = true;
     const int64_t col_stride = p.dv + 1;
+    // The generator threads' barrier: an mbarrier all of them arrive on, waited
+    // on with the bounded wait (a generator that gave up stops arriving, and
+    // the others then give up instead of hanging).  Every wait of a generator
+    // warp has one verdict for all its lanes (mbar_wait_warp), so the warp's
+    // .sync.aligned TMEM instructions always run converged.
+    uint32_t gphase = 0;
+    auto gen_sync = [&]() -> bool {
+      mbar_arrive(gbar);
+      const bool r = mbar_wait_warp(gbar, gphase, ab, kErrMomWait);
+      gphase ^= 1;
+      return r;
+    };
+    // one arrival per warp, once every lane's stores (TMEM or shared) are done
+    auto warp_arrive = [&](uint64_t* bar) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar);
+    };
 
     float* part_h = p.part + ((int64_t)g * p.bh + h) * p.n * col_stride;
     // staged query sums of one sub-tile ([rows, dv + 1] in the state buffer)
@@ -520,7 +562,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
       if (out_rows > 0) {
         const int total = out_rows * (int)col_stride;
         float* dst = part_h + out_i0 * col_stride;
-        for (int e = threadIdx.x - 64; e < total; e += 256) dst[e] = ostg[e];
+        for (int e = gi; e < total; e += kGenThreads) dst[e] = ostg[e];
         out_rows = 0;
       }
     };
@@ -530,12 +572,12 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     // Row tiles are loaded one tile ahead, in the order the phases consume them:
     // per block c, the query sub-tiles of c (c > 0), then the key sub-tiles of c
     // (c + 1 < nb).  rowv holds this thread's share of the next tile.
-    const uint4* my_map = tmaps + (threadIdx.x - 64);
-    float rowv[32];
+    const uint2* my_map = tmaps + gi;
+    float rowv[kTileVals];
     auto issue_tile = [&](int64_t uc, bool uq, int ust) {
       const int64_t i0 = uc * p.bs + (int64_t)ust * kRows;
       const int nvalid = (int)min((int64_t)kRows, min(uc * p.bs + p.bs, p.n) - i0);
-      rows_issue(uq ? qh : kh, i0, nvalid, p.d, t, half, vec, my_map, rowv);
+      rows_issue(uq ? qh : kh, i0, nvalid, p.d, t, cg, vec, my_map, rowv);
     };
     // issue the loads of the tile after (uc, uq, ust), if there is one
     auto issue_next = [&](int64_t uc, bool uq, int ust) {
@@ -552,12 +594,12 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     };
     if (has_query(0)) issue_tile(0, true, 0);
     else if (has_update(0)) issue_tile(0, false, 0);
-    // Master state: only the thread that owns feature t of a tile (and its half of
-    // the columns) ever touches those entries, so they are stored in the order
-    // that makes a warp's accesses contiguous: float4 u4 of (tile j, half, lane
-    // t) at float4 index ((j * 2 + half) * (HC / 4) + u4) * 128 + t.
+    // Master state: only the thread that owns feature t of a tile (and its column
+    // group's columns) ever touches those entries, so they are stored in the order
+    // that makes a warp's accesses contiguous: float4 u4 of (tile j, column group
+    // cg, lane t) at float4 index ((j * kNCG + cg) * (HC / 4) + u4) * 128 + t.
     auto mrow_of = [&](int j) {
-      return reinterpret_cast<float4*>(master_h) + (int64_t)((j * 2 + half) * (HC / 4)) * kRows + t;
+      return reinterpret_cast<float4*>(master_h) + (int64_t)((j * kNCG + cg) * (HC / 4)) * kRows + t;
     };
     // master state row of the next tile to fold (prefetched one tile ahead)
     float mp[HC];
@@ -572,43 +614,33 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
         mp[4 * u4 + 3] = m4.w;
       }
     };
-    // this thread's feature of every tile in the update phase: indices and key factor
-    // (kept in shared memory, [tile][generator thread], to spare registers)
-    const int gi = threadIdx.x - 64;
-#pragma unroll
-    for (int j = 0; j < FT; ++j) {
-      const uint32_t sg = segtab[j * 16 + (t >> 3)];
-      const int p1 = sg & 1023, p2 = (sg >> 10) & 1023, c = (int)(sg >> 20) + (t & 7);
-      const float cf = j < ntiles ? seg_key_coef(p1, p2, c, p.d, p.degree) : 0.0f;
-      fco[j * 256 + gi] = make_uint2((uint32_t)p1 | ((uint32_t)p2 << 10) | ((uint32_t)c << 20), __float_as_uint(cf));
-    }
     // the transposed key tile of update sub-tile st of block c into X
     // (X[a * kXtStride + token]) from the prefetched rows; then the next tile's loads
     auto stage_keys = [&](int64_t c, int st) {
       const int64_t b1 = min(c * p.bs + (int64_t)p.bs, p.n);
       const int64_t i = c * p.bs + (int64_t)st * kRows + t;
       const bool valid = i < b1;
-      const int a0 = half * 32;
       if (vec) {
-        const uint4 m = *my_map;
+        const uint2 m = *my_map;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 0; k < 4; ++k) {
           const uint32_t e = tile_entry(m, k);
           const int row = (int)(e >> 8), col4 = (int)(e & 255);
           if (e != 0xffffu) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) X[(4 * col4 + e) * kXtStride + row] = rowv[4 * k + e];
+            for (int u = 0; u < 4; ++u) X[(4 * col4 + u) * kXtStride + row] = rowv[4 * k + u];
           }
         }
       } else {
+        const int a0 = cg * 16;
 #pragma unroll
-        for (int u = 0; u < 32; ++u)
+        for (int u = 0; u < 16; ++u)
           if (a0 + u < p.d) X[(a0 + u) * kXtStride + t] = rowv[u];
       }
       const float* src = kh + (valid ? i : 0) * p.d;
-      for (int a = 64 + half; a < p.d; a += 2) X[a * kXtStride + t] = valid ? __ldg(src + a) : 0.0f;
+      for (int a = 64 + cg; a < p.d; a += kNCG) X[a * kXtStride + t] = valid ? __ldg(src + a) : 0.0f;
       // an invalid token's extended row is all zero, so are its features
-      if (half == 1)
+      if (cg == kNCG - 1)
         for (int a = p.d; a < DX; ++a) X[a * kXtStride + t] = (a == dp && valid) ? 1.0f : 0.0f;
       issue_next(c, false, st);
     };
@@ -618,10 +650,10 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
       const int64_t b1 = min(b0 + (int64_t)p.bs, p.n);
       // ---------------- query phase: tokens of block c read S_{<c}
       if (!has_query(c)) {
-        for (int64_t i = b0 + t + half * kRows; i < b1; i += 2 * kRows) {
-          float* dst = part_h + i * col_stride;
-          for (int col = 0; col <= p.dv; ++col) dst[col] = 0.0f;
-        }
+        // no earlier block: this block's low sums are zero
+        float* dst = part_h + b0 * col_stride;
+        const int64_t total = (b1 - b0) * col_stride;
+        for (int64_t e = gi; e < total; e += kGenThreads) dst[e] = 0.0f;
       } else {
         const bool frozen = p.mode == 2;
         if (c >= 2 || frozen) mload(0);   // the state rows written by the previous query phase
@@ -630,14 +662,14 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
           const int64_t i = b0 + (int64_t)st * kRows + t;
           const bool valid = i < b1;
           float* xr = X + t * XS;
-          gen_sync();  // X is free, and sden of the previous update phase is visible
+          // X is free, and sden of the previous update phase is visible
+          if (!gen_sync()) { ok = false; break; }
           {
             // x~ = [scale q_i, zeros, 1 at dp, zeros]
-            const int a0 = half * 32;
             if (vec) {
-              const uint4 m = *my_map;
+              const uint2 m = *my_map;
 #pragma unroll
-              for (int k = 0; k < 8; ++k) {
+              for (int k = 0; k < 4; ++k) {
                 const uint32_t e = tile_entry(m, k);
                 const int row = (int)(e >> 8), col4 = (int)(e & 255);
                 if (e != 0xffffu)
@@ -646,70 +678,67 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
                                   rowv[4 * k + 3] * p.scale);
               }
             } else {
+              const int a0 = cg * 16;
 #pragma unroll
-              for (int u = 0; u < 32; ++u)
+              for (int u = 0; u < 16; ++u)
                 if (a0 + u < p.d) xr[a0 + u] = rowv[u] * p.scale;
             }
             const float* src = qh + (valid ? i : 0) * p.d;
-            for (int a = 64 + half; a < p.d; a += 2) xr[a] = valid ? __ldg(src + a) * p.scale : 0.0f;
-            if (half == 1)
+            for (int a = 64 + cg; a < p.d; a += kNCG) xr[a] = valid ? __ldg(src + a) * p.scale : 0.0f;
+            if (cg == kNCG - 1)
               for (int a = p.d; a < DX; ++a) xr[a] = (a == dp) ? 1.0f : 0.0f;
           }
           issue_next(c, true, st);
-          gen_sync();
+          if (!gen_sync()) { ok = false; break; }
           // the fold below reads the update products of block c - 1: wait for them
           // only now, so that staging the query tile overlaps their tail
           if (st == 0 && !frozen) {
-            if (!mbar_wait(u_done, (int)((c - 1) & 1), ab, kErrMomWait)) { ok = false; break; }
+            if (!mbar_wait_warp(u_done, (int)((c - 1) & 1), ab, kErrMomWait)) { ok = false; break; }
             tc_fence_after();
           }
           float den_acc = 0.0f;
           for (int j = 0; ok && j < ntiles; ++j, ++sb_use) {
             const int sb = sb_use & 1;
-            if (sb_use >= 2 && !mbar_wait(&sb_free[sb], ((sb_use >> 1) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+            if (sb_use >= 2 && !mbar_wait_warp(&sb_free[sb], ((sb_use >> 1) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
             {
-              // State row of feature t of tile j, this half's columns, 16 at a time:
-              // fold dS_j (first sub-tile) into the fp32 master and write the hi/lo
-              // split into the B buffer (MN-major: row t of chunk (half * HC) / 32,
+              // State row of feature t of tile j, this column group's HC columns:
+              // fold cf * dS_j (first sub-tile) into the fp32 master and write the
+              // hi/lo split into the B buffer (MN-major: row t of chunk (cg HC) / 32,
               // 32-byte granule g stored at g ^ (t & 3)).
               float4* mrow = mrow_of(j);
-              uint8_t* bhi = sbuf + sb * L::kSbuf + ((half * HC) / 32) * (kRows * 128) + t * 128;
+              uint8_t* bhi = sbuf + sb * L::kSbuf + ((cg * HC) / 32) * (kRows * 128) + t * 128;
               uint8_t* blo = bhi + L::kSbufHalf;
-              const int g0 = ((half * HC) % 32) / 8;
+              const int g0 = ((cg * HC) % 32) / 8;
+              float sv[HC];
+              if (st == 0 && !frozen) {
+                tmem_ld_wait<HC>(la + j * L::kTC + cg * HC, sv);
+                const float cf = __uint_as_float(fco[j * kRows + t].y);
 #pragma unroll
-              for (int q = 0; q < HC / 16; ++q) {
-                float sv[16];
-                if (st == 0 && !frozen) {
-                  uint32_t a[16];
-                  tmem_ld16(la + j * L::kTC + half * HC + 16 * q, a);
-                  tmem_wait_ld();
+                for (int u = 0; u < HC; ++u) sv[u] *= cf;
+                if (c >= 2) {
 #pragma unroll
-                  for (int u = 0; u < 16; ++u) sv[u] = __uint_as_float(a[u]);
-                  if (c >= 2) {
-#pragma unroll
-                    for (int u = 0; u < 16; ++u) sv[u] += mp[16 * q + u];
-                  }
-#pragma unroll
-                  for (int u4 = 0; u4 < 4; ++u4)
-                    mrow[(4 * q + u4) * kRows] = make_float4(sv[4 * u4], sv[4 * u4 + 1], sv[4 * u4 + 2], sv[4 * u4 + 3]);
-                } else {
-#pragma unroll
-                  for (int u = 0; u < 16; ++u) sv[u] = mp[16 * q + u];
+                  for (int u = 0; u < HC; ++u) sv[u] += mp[u];
                 }
 #pragma unroll
-                for (int gg = 0; gg < 2; ++gg) {
-                  const uint32_t off = (uint32_t)(((g0 + 2 * q + gg) ^ (t & 3)) * 32);
-                  float hv[8], lv[8];
+                for (int u4 = 0; u4 < HC / 4; ++u4)
+                  mrow[u4 * kRows] = make_float4(sv[4 * u4], sv[4 * u4 + 1], sv[4 * u4 + 2], sv[4 * u4 + 3]);
+              } else {
 #pragma unroll
-                  for (int u = 0; u < 8; ++u) {
-                    hv[u] = __uint_as_float(tf32_trunc(sv[gg * 8 + u]));
-                    lv[u] = sv[gg * 8 + u] - hv[u];
-                  }
-                  *reinterpret_cast<float4*>(bhi + off) = make_float4(hv[0], hv[1], hv[2], hv[3]);
-                  *reinterpret_cast<float4*>(bhi + off + 16) = make_float4(hv[4], hv[5], hv[6], hv[7]);
-                  *reinterpret_cast<float4*>(blo + off) = make_float4(lv[0], lv[1], lv[2], lv[3]);
-                  *reinterpret_cast<float4*>(blo + off + 16) = make_float4(lv[4], lv[5], lv[6], lv[7]);
+                for (int u = 0; u < HC; ++u) sv[u] = mp[u];
+              }
+#pragma unroll
+              for (int gg = 0; gg < HC / 8; ++gg) {
+                const uint32_t off = (uint32_t)(((g0 + gg) ^ (t & 3)) * 32);
+                float hv[8], lv[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                  hv[u] = __uint_as_float(tf32_trunc(sv[gg * 8 + u]));
+                  lv[u] = sv[gg * 8 + u] - hv[u];
                 }
+                *reinterpret_cast<float4*>(bhi + off) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+                *reinterpret_cast<float4*>(bhi + off + 16) = make_float4(hv[4], hv[5], hv[6], hv[7]);
+                *reinterpret_cast<float4*>(blo + off) = make_float4(lv[0], lv[1], lv[2], lv[3]);
+                *reinterpret_cast<float4*>(blo + off + 16) = make_float4(lv[4], lv[5], lv[6], lv[7]);
               }
             }
             // prefetch the state row of the next tile to fold: tile j + 1, or tile 0 of
@@ -721,36 +750,33 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
             }
             tc_fence_before();   // the dS_j reads are ordered before the MMAs that reuse its columns
             fence_proxy_async_smem();
-            mbar_arrive(&sb_full[sb]);
-            // Phi_q chunks of tile j for this thread's token: 2 segments (16 features) per half
+            warp_arrive(&sb_full[sb]);
+            // Phi_q chunks of tile j for this thread's token: one segment (8 features) each
             for (int kc = 0; kc < kRows / kChunk; ++kc, ++stg_use) {
               const int b = stg_use % kNStg;
-              if (stg_use >= kNStg && !mbar_wait(&stg_free[b], ((stg_use / kNStg) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
-              uint32_t hi[16], lo[16];
+              const int sl = j * 16 + kc * 4 + cg;    // segment within the group
+              const uint32_t pk = segtab[sl];
+              float pre = xr[pk & 1023];
+              if (DEG3) pre *= xr[(pk >> 10) & 1023];
+              const float* xc = xr + (pk >> 20);
+              const float4 x0 = ld4(xc), x1 = ld4(xc + 4);
+              const float4 d0 = ld4(sden + sl * 8), d1 = ld4(sden + sl * 8 + 4);
+              const float ph[8] = {pre * x0.x, pre * x0.y, pre * x0.z, pre * x0.w,
+                                   pre * x1.x, pre * x1.y, pre * x1.z, pre * x1.w};
+              const float dd[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+              uint32_t hi[8], lo[8];
 #pragma unroll
-              for (int sg = 0; sg < 2; ++sg) {
-                const int sl = j * 16 + kc * 4 + half * 2 + sg;    // segment within the group
-                const uint32_t pk = segtab[sl];
-                float pre = xr[pk & 1023];
-                if (DEG3) pre *= xr[(pk >> 10) & 1023];
-                const float* xc = xr + (pk >> 20);
-                const float4 x0 = ld4(xc), x1 = ld4(xc + 4);
-                const float4 d0 = ld4(sden + sl * 8), d1 = ld4(sden + sl * 8 + 4);
-                const float ph[8] = {pre * x0.x, pre * x0.y, pre * x0.z, pre * x0.w,
-                                     pre * x1.x, pre * x1.y, pre * x1.z, pre * x1.w};
-                const float dd[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                  den_acc = fmaf(ph[u], dd[u], den_acc);
-                  hi[sg * 8 + u] = tf32_trunc(ph[u]);
-                  lo[sg * 8 + u] = __float_as_uint(ph[u] - __uint_as_float(hi[sg * 8 + u]));
-                }
+              for (int u = 0; u < 8; ++u) {
+                den_acc = fmaf(ph[u], dd[u], den_acc);
+                hi[u] = tf32_trunc(ph[u]);
+                lo[u] = __float_as_uint(ph[u] - __uint_as_float(hi[u]));
               }
-              tmem_st16(la + L::kStg + b * 2 * kChunk + half * 16, hi);
-              tmem_st16(la + L::kStg + b * 2 * kChunk + kChunk + half * 16, lo);
+              if (stg_use >= kNStg && !mbar_wait_warp(&stg_free[b], ((stg_use / kNStg) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+              tmem_st8(la + L::kStg + b * 2 * kChunk + cg * kCgCols, hi);
+              tmem_st8(la + L::kStg + b * 2 * kChunk + kChunk + cg * kCgCols, lo);
               tmem_wait_st();
               tc_fence_before();
-              mbar_arrive(&stg_full[b]);
+              warp_arrive(&stg_full[b]);
             }
           }
           if (!ok) break;
@@ -759,13 +785,13 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
           // tail of the query products (the gen_sync after the readback below
           // orders these writes before the update phase reads them)
           if (st + 1 == nsq && has_update(c)) {
-            gen_sync();
+            if (!gen_sync()) { ok = false; break; }
             stage_keys(c, 0);
             kstaged = true;
           }
           // Out_j of every tile sits in the tile's own TMEM columns: once all the
           // sub-tile's MMAs are done, add them up in tile order
-          if (!mbar_wait(out_full, out_use & 1, ab, kErrMomWait)) { ok = false; break; }
+          if (!mbar_wait_warp(out_full, out_use & 1, ab, kErrMomWait)) { ok = false; break; }
           ++out_use;
           tc_fence_after();
           float acc[HC];
@@ -773,15 +799,14 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
           for (int u = 0; u < HC; ++u) acc[u] = 0.0f;
           for (int j = 0; j < ntiles; ++j) {
             float ov[HC];
-            tmem_ld_cols<HC>(la + j * L::kTC + half * HC, ov);
+            tmem_ld_wait<HC>(la + j * L::kTC + cg * HC, ov);
 #pragma unroll
             for (int u = 0; u < HC; ++u) acc[u] += ov[u];
           }
-          if (!ok) break;
           tc_fence_before();
-          mbar_arrive(out_free);
-          xch[half * kRows + t] = den_acc;
-          gen_sync();
+          warp_arrive(out_free);
+          xch[cg * kRows + t] = den_acc;
+          if (!gen_sync()) { ok = false; break; }
           {
             // Stage the sub-tile's [rows, dv + 1] sums in the state buffer (every
             // product that reads it is done; row stride dv + 1 is odd, so the
@@ -792,56 +817,59 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
             const int cs = (int)col_stride;
 #pragma unroll
             for (int u = 0; u < HC; ++u)
-              if (half * HC + u < p.dv) ostg[t * cs + half * HC + u] = acc[u];
-            if (half == 0) ostg[t * cs + p.dv] = xch[t] + xch[kRows + t];
+              if (cg * HC + u < p.dv) ostg[t * cs + cg * HC + u] = acc[u];
+            if (cg == 0) {
+              float dsum = xch[t];
+#pragma unroll
+              for (int x = 1; x < kNCG; ++x) dsum += xch[x * kRows + t];
+              ostg[t * cs + p.dv] = dsum;
+            }
             out_i0 = b0 + (int64_t)st * kRows;
             out_rows = (int)min((int64_t)kRows, b1 - out_i0);
           }
           if (st + 1 < nsq || !has_update(c)) {
-            gen_sync();
+            if (!gen_sync()) { ok = false; break; }
             copy_out();
           }
         }
       }
       if (!ok || !has_update(c)) continue;
-      // ---------------- update phase: dS_j of block c
+      // ---------------- update phase: dS_j of block c (unscaled key features;
+      // the key coefficient is applied at the fold)
       float sd[FT];
 #pragma unroll
       for (int j = 0; j < FT; ++j) sd[j] = 0.0f;
-      // as in the query phase, a chunk's TMEM stores complete under the next
-      // chunk's arithmetic (within a key tile)
+      // a chunk's TMEM stores complete under the next chunk's arithmetic
       int held = -1;
       auto hand_over = [&]() {
         if (held >= 0) {
           tmem_wait_st();
           tc_fence_before();
-          mbar_arrive(&stg_full[held]);
+          warp_arrive(&stg_full[held]);
           held = -1;
         }
       };
       for (int st = 0; ok && st < sub; ++st) {
         if (!(st == 0 && kstaged)) {
           hand_over();
-          gen_sync();  // everyone is done with X
+          if (!gen_sync()) { ok = false; break; }   // everyone is done with X
           stage_keys(c, st);
-          gen_sync();
+          if (!gen_sync()) { ok = false; break; }
         }
         kstaged = false;
         for (int tcn = 0; ok && tcn < kRows / kChunk; ++tcn) {
-          const int tok0 = tcn * kChunk + half * 16;
+          const int tok0 = tcn * kChunk + cg * kCgCols;
 #pragma unroll
           for (int j = 0; j < FT; ++j) {
             if (!ok || j >= ntiles) break;
             const int b = stg_use % kNStg;
-            const uint2 fc = fco[j * 256 + gi];
-            const uint32_t fi = fc.x;
-            const float cf = __uint_as_float(fc.y);
+            const uint32_t fi = fco[j * kRows + t].x;
             const float* r1 = X + (fi & 1023) * kXtStride + tok0;
             const float* rc = X + (fi >> 20) * kXtStride + tok0;
-            uint32_t hi[16], lo[16];
+            uint32_t hi[8], lo[8];
             float fsum = 0.0f;
 #pragma unroll
-            for (int u4 = 0; u4 < 4; ++u4) {
+            for (int u4 = 0; u4 < 2; ++u4) {
               float4 a4 = ld4(r1 + 4 * u4);
               const float4 c4 = ld4(rc + 4 * u4);
               if (DEG3) {
@@ -851,7 +879,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
                 a4.z *= b4.z;
                 a4.w *= b4.w;
               }
-              const float ph[4] = {a4.x * cf * c4.x, a4.y * cf * c4.y, a4.z * cf * c4.z, a4.w * cf * c4.w};
+              const float ph[4] = {a4.x * c4.x, a4.y * c4.y, a4.z * c4.z, a4.w * c4.w};
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
                 fsum += ph[u];
@@ -861,59 +889,64 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
             }
             sd[j] += fsum;
             hand_over();
-            if (stg_use >= kNStg && !mbar_wait(&stg_free[b], ((stg_use / kNStg) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
+            if (stg_use >= kNStg && !mbar_wait_warp(&stg_free[b], ((stg_use / kNStg) - 1) & 1, ab, kErrMomWait)) { ok = false; break; }
             ++stg_use;
-            tmem_st16(la + L::kStg + b * 2 * kChunk + half * 16, hi);
-            tmem_st16(la + L::kStg + b * 2 * kChunk + kChunk + half * 16, lo);
+            tmem_st8(la + L::kStg + b * 2 * kChunk + cg * kCgCols, hi);
+            tmem_st8(la + L::kStg + b * 2 * kChunk + kChunk + cg * kCgCols, lo);
             held = b;
           }
         }
       }
       hand_over();
-      // s += the features of this block's keys: the halves' sums meet in shared memory
-      if (half == 1) {
+      if (!ok) continue;
+      // s += cf * (the features of this block's keys): the column groups' sums
+      // meet in shared memory, added in column-group order
+      if (cg > 0) {
 #pragma unroll
         for (int j = 0; j < FT; ++j)
-          if (j < ntiles) sdx[j * kRows + t] = sd[j];
+          if (j < ntiles) sdx[((cg - 1) * FT + j) * kRows + t] = sd[j];
       }
-      gen_sync();  // all reads of sden by the query phase are done; sdx is written
-      if (half == 0) {
+      if (!gen_sync()) { ok = false; continue; }   // all reads of sden by the query phase are done
+      if (cg == 0) {
 #pragma unroll
-        for (int j = 0; j < FT; ++j)
-          if (j < ntiles) sden[j * kRows + t] += sd[j] + sdx[j * kRows + t];
+        for (int j = 0; j < FT; ++j) {
+          if (j < ntiles) {
+            float s4 = sd[j];
+#pragma unroll
+            for (int x = 0; x < kNCG - 1; ++x) s4 += sdx[(x * FT + j) * kRows + t];
+            sden[j * kRows + t] += __uint_as_float(fco[j * kRows + t].y) * s4;
+          }
+        }
       }
       copy_out();   // the query sums of this block, staged before the update phase
     }
     if (ok && p.mode == 1) {
       // total: fold the last block's dS into the master (which then holds the
       // state of every block) and hand out the feature sums
-      if (!mbar_wait(u_done, (int)((nb - 1) & 1), ab, kErrMomWait)) {
+      if (!mbar_wait_warp(u_done, (int)((nb - 1) & 1), ab, kErrMomWait)) {
         ok = false;
       } else {
         tc_fence_after();
         for (int j = 0; j < ntiles; ++j) {
           float4* mrow = mrow_of(j);
+          const float cf = __uint_as_float(fco[j * kRows + t].y);
+          float a[HC];
+          tmem_ld_wait<HC>(la + j * L::kTC + cg * HC, a);
 #pragma unroll
-          for (int q = 0; q < HC / 16; ++q) {
-            uint32_t a[16];
-            tmem_ld16(la + j * L::kTC + half * HC + 16 * q, a);
-            tmem_wait_ld();
-#pragma unroll
-            for (int u4 = 0; u4 < 4; ++u4) {
-              float4 v4 = make_float4(__uint_as_float(a[4 * u4]), __uint_as_float(a[4 * u4 + 1]),
-                                      __uint_as_float(a[4 * u4 + 2]), __uint_as_float(a[4 * u4 + 3]));
-              if (nb >= 2) {
-                const float4 m4 = mrow[(4 * q + u4) * kRows];
-                v4.x += m4.x;
-                v4.y += m4.y;
-                v4.z += m4.z;
-                v4.w += m4.w;
-              }
-              mrow[(4 * q + u4) * kRows] = v4;
+          for (int u4 = 0; u4 < HC / 4; ++u4) {
+            float4 v4 = make_float4(cf * a[4 * u4], cf * a[4 * u4 + 1], cf * a[4 * u4 + 2], cf * a[4 * u4 + 3]);
+            if (nb >= 2) {
+              const float4 m4 = mrow[u4 * kRows];
+              v4.x += m4.x;
+              v4.y += m4.y;
+              v4.z += m4.z;
+              v4.w += m4.w;
             }
+            mrow[u4 * kRows] = v4;
           }
         }
-        if (half == 0)
+        // the feature sums: sden was last written by column group 0 of each lane
+        if (cg == 0)
           for (int j = 0; j < ntiles; ++j)
             p.den_io[((int64_t)g * p.bh + h) * (FT * kRows) + j * kRows + t] = sden[j * kRows + t];
       }
@@ -933,8 +966,8 @@ size_t mom_smem(int d) {
   const int dp = dpad8(d), DX = dp + 8, XS = DX + 4;
   const size_t xwords = (size_t)max(max(kRows * XS, DX * kXtStride), kRows * (DVP + 1));
   return 1024 + 2 * L::kSbuf + L::kVStages * L::kVStage + xwords * 4 + (size_t)L::kFT * 16 * 4 +
-         (size_t)L::kFT * kRows * 8 + 2 * kRows * 4 + 16 + 256 * 16 + (size_t)L::kFT * 256 * 8 +
-         (2 * kNStg + 12) * 8 + 16;
+         (size_t)L::kFT * kRows * 4 + (size_t)kNCG * kRows * 4 + (size_t)(kNCG - 1) * L::kFT * kRows * 4 + 16 +
+         (size_t)kGenThreads * 8 + (size_t)L::kFT * kRows * 8 + (2 * kNStg + 14) * 8 + 16;
 }
 
 template <int DVP, bool DEG3>
@@ -1036,7 +1069,7 @@ int launch_moments_tc(const CUtensorMap* maps, const float* q, const float* k, f
   if (bh > 65535) return set_error(SA_ERR_UNSUPPORTED, "too many sequences for one launch");
   if (mode != 0 && !den_io) return set_error(SA_ERR_INVALID_ARG, "moment state modes need the feature-sum buffer");
   MomTCParams prm{q, k, part, master, status, n, bh, d, dv, bs, degree, (int)mom_seg_count(d, degree), G, scale,
-                  mode, den_io};
+                  mode, den_io, wait_limit_ns()};
   if (degree == 3) return dv <= 32 ? launch_mom_tc<32, true>(maps, prm, stream) : launch_mom_tc<64, true>(maps, prm, stream);
   return dv <= 32 ? launch_mom_tc<32, false>(maps, prm, stream) : launch_mom_tc<64, false>(maps, prm, stream);
 }

@@ -69,6 +69,7 @@ struct ResTCParams {
   int64_t group_stride;  // floats between slices (bh * n * (dv+1))
   int64_t c_off;         // global index of the sequence's first block (a shard of a longer sequence:
                          // rep rows and each query's active reps count from global block 0)
+  uint64_t wait_ns;      // limit of one bounded wait
 };
 
 template <int DP, int DVP>
@@ -242,7 +243,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const Abort ab{abort_word, p.status};
+  const Abort ab{abort_word, p.status, p.wait_ns};
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -427,10 +428,11 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     bool ok = true;
     for (int t = 0; t < T; ++t) {
       const int s = t % kStages, b = t & 1;
-      if (!mbar_wait(&sfull[b], (t >> 1) & 1, ab, kErrWaitS)) { ok = false; break; }
+      // warp-uniform verdicts: the TMEM loads and stores below are .sync.aligned
+      if (!mbar_wait_warp(&sfull[b], (t >> 1) & 1, ab, kErrWaitS)) { ok = false; break; }
       const bool rep = t < n_rep;
       const bool with_w = rep && p.rep_w != nullptr;
-      if (with_w && !mbar_wait(&full[s], (t / kStages) & 1, ab, kErrWaitFull)) { ok = false; break; }
+      if (with_w && !mbar_wait_warp(&full[s], (t / kStages) & 1, ab, kErrWaitFull)) { ok = false; break; }
       tc_fence_after();
       const uint32_t tS = lane_addr + L::kS0 + 128 * b + half * 32;
       const int64_t row0 = rep ? (int64_t)t * kTile : kb0 + (int64_t)(t - n_rep) * kTile;
@@ -625,7 +627,7 @@ int launch_residual_tc(const CUtensorMap* maps, const float* q, const float* rep
   if (bh > 65535 || (n + kRowsQ - 1) / kRowsQ > 2147483647LL)
     return set_error(SA_ERR_UNSUPPORTED, "grid too large for the tensor-core residual");
   ResTCParams prm{q, rep_w, low, out, status, n, m_blk, r_pad, d, dv, bs, scale, eps, groups, bh * n * (dv + 1),
-                  c_off};
+                  c_off, wait_limit_ns()};
   const int dp = residual_tc_dp(d), dvp = residual_tc_dvp(dv);
   if (dp == 32 && dvp == 32) return launch_deg<32, 32>(degree, maps, prm, bh, stream, clamp_exp);
   if (dp == 32 && dvp == 64) return launch_deg<32, 64>(degree, maps, prm, bh, stream, clamp_exp);

@@ -14,6 +14,11 @@ int set_error(int code, const char* fmt, ...);
 // Maps the last CUDA launch error (if any) to SA_ERR_CUDA.
 int check_launch(const char* what);
 
+// How long one bounded device-side wait of the tensor-core kernels may take
+// before its CTA gives up and records an error in the status word
+// (sa_set_wait_limit_ns; 2 s unless set).
+uint64_t wait_limit_ns();
+
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // Feature count sum_{l<=t} C(d+l-1, l) for t <= 3.

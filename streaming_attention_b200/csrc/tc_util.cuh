@@ -65,19 +65,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 struct Abort {
   volatile int* cta;     // shared memory: nonzero once any role of this CTA gave up
   int* global_status;    // device memory: first error code of the launch
+  uint64_t limit_ns;     // how long one wait may take before the CTA gives up
 };
 
-// Waits for the given phase parity; gives up after `limit_ns` (or at once if
+// Waits for the given phase parity; gives up after ab.limit_ns (or at once if
 // the CTA is already aborting), records `code` and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const Abort& ab, int code,
-                                          uint64_t limit_ns = 2000000000ull) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const Abort& ab, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63) == 63) {
       if (*ab.cta) return false;
-      if (globaltimer_ns() - t0 > limit_ns) {
+      if (globaltimer_ns() - t0 > ab.limit_ns) {
         *ab.cta = 1;
         if (ab.global_status) atomicCAS(ab.global_status, 0, code);
         return false;

@@ -138,6 +138,12 @@ def _check_modes(n: int, block_size: int, degree: int, compressor: str, low_mode
         raise ValueError("compressor must be one of {'sorted_pair', 'random', 'none'}")
 
 
+def _check_dtype(t: Tensor) -> None:
+    if not t.dtype.is_floating_point:
+        raise ValueError(f"unsupported dtype {t.dtype}: the kernels compute in float32 "
+                         "(float32, float64, float16 and bfloat16 inputs are accepted)")
+
+
 def _check_device(*ts: Tensor) -> torch.device:
     dev = ts[0].device
     if dev.type != "cuda":
@@ -145,15 +151,15 @@ def _check_device(*ts: Tensor) -> torch.device:
     for t in ts:
         if t.device != dev:
             raise ValueError("q, k and v must be on the same device")
-        if t.dtype == torch.float64 or not t.dtype.is_floating_point:
-            raise ValueError(f"unsupported dtype {t.dtype}: the kernels compute in float32 "
-                             "(float32, float16 and bfloat16 inputs are accepted)")
+        _check_dtype(t)
     return dev
 
 
 def _stats(n: int, dim: int, dv: int, degree: int, block_size: int, compressor: str, low_mode: str,
-           query_chunk_size: int, elem: int) -> FastArticleStats:
-    """fast_article_attention.py:580-631 for one sequence on a CUDA device."""
+           query_chunk_size: int, elem: int, device_type: str = "cuda") -> FastArticleStats:
+    """fast_article_attention.py:580-631 for one sequence whose inputs live on
+    ``device_type``: ``low_mode="auto"`` resolves to "prefix" for CUDA inputs and
+    to "stream" for host inputs, as the reference resolves it (:616)."""
     F = num_taylor_features(dim, degree)
     if compressor == "none":
         items = n
@@ -167,7 +173,10 @@ def _stats(n: int, dim: int, dv: int, degree: int, block_size: int, compressor: 
             block_scratch = max(block_scratch, b * b * elem)
         resid = max(min(query_chunk_size, n) * max(items, 1) * elem, block_scratch)
     approx = F * (1 + dv) * elem + items * (dim + dv + 1) * elem + min(block_size, n) * (dim + dv) * elem
-    resolved = "prefix" if low_mode == "auto" else low_mode
+    if low_mode == "auto":
+        resolved = "prefix" if device_type == "cuda" else "stream"
+    else:
+        resolved = low_mode
     low_bytes = F * (1 + dv) * elem if resolved == "stream" else n * F * (1 + dv) * elem
     return FastArticleStats(degree, block_size, F, items, int(approx), int(low_bytes), int(resid))
 
@@ -296,19 +305,19 @@ def _host_inputs(*ts: Tensor) -> bool:
     if not torch.cuda.is_available():
         raise ValueError("the B200 kernels need a CUDA device; none is available")
     for t in ts:
-        if t.dtype == torch.float64 or not t.dtype.is_floating_point:
-            raise ValueError(f"unsupported dtype {t.dtype}: the kernels compute in float32 "
-                             "(float32, float16 and bfloat16 inputs are accepted)")
+        _check_dtype(t)
     return True
 
 
 def check_device_status(workspace: Tensor) -> None:
-    """Read the launch status word (the first 4 bytes of the workspace): the
-    tensor-core kernels bound every wait and record a nonzero code there when
-    one gives up.  Synchronises the stream."""
-    code = int(workspace[:4].view(torch.int32).item())
-    if code != 0:
-        raise _lib.SAError(f"device status {code}: a bounded device-side wait gave up")
+    """Read the launch status word (the first 4 bytes of the workspace) through
+    sa_workspace_status: the tensor-core kernels bound every wait and record a
+    nonzero code there when one gives up (raised here as SAError).
+    Synchronises the current stream."""
+    with torch.cuda.device(workspace.device):
+        rc = _lib.load().sa_workspace_status(workspace.data_ptr(),
+                                             torch.cuda.current_stream(workspace.device).cuda_stream)
+    _lib.check(rc, "device status")
 
 
 def _as_f32(t: Tensor) -> Tensor:
@@ -339,7 +348,7 @@ def fast_article_causal_attention_single(
     if not return_stats:
         return out
     return out, _stats(n, dim, v.shape[-1], degree, block_size, compressor, low_mode, query_chunk_size,
-                       q.element_size())
+                       q.element_size(), q.device.type)
 
 
 @torch.no_grad()
@@ -390,7 +399,8 @@ def fast_article_causal_attention(
     if bh == 0:
         stats = FastArticleStats(degree, block_size, num_taylor_features(dim, degree), 0, 0, 0, 0)
     else:
-        stats = _stats(n, dim, dv, degree, block_size, compressor, low_mode, query_chunk_size, q.element_size())
+        stats = _stats(n, dim, dv, degree, block_size, compressor, low_mode, query_chunk_size, q.element_size(),
+                       q.device.type)
     return out, stats
 
 

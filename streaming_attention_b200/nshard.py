@@ -200,13 +200,15 @@ def _prep(q: Tensor, k: Tensor, v: Tensor):
 def fast_article_causal_attention_nshard(
     q: Tensor, k: Tensor, v: Tensor, *, rank: int, world: int, group=None, layout: str = "zigzag", degree: int = 2,
     block_size: int = 128, scale: Optional[float] = None, compressor: str = "sorted_pair", seed: int = 0,
-    denominator_eps: float = 1e-12,
-) -> Tensor:
+    denominator_eps: float = 1e-12, return_rep_idx: bool = False,
+):
     """This rank's part of fast_article_causal_attention over [B, H, N, *]
     sequences split along N.  q, k, v hold the rank's chunks (see
     ``owned_chunks``) concatenated along N in that order; the result is the
     matching [B, H, len, Dv] slice of the output.  Every rank of ``group``
-    calls it collectively."""
+    calls it collectively.  With ``return_rep_idx`` it also returns, per owned
+    chunk in the same order, the global token indices [B*H, rows] of the reps
+    that chunk's blocks kept (None for compressor none)."""
     B, H, Lr, d, dv = _prep(q, k, v)
     _check_device(q, k, v)
     chunks = owned_chunks(rank, world, layout)
@@ -247,7 +249,10 @@ def fast_article_causal_attention_nshard(
         out = torch.empty(bh, L, dv, device=q.device, dtype=torch.float32)
         outs.append(sh.end(before.contiguous(), _assemble(by_chunk[1][:j + 1]), _assemble(by_chunk[2][:j + 1]),
                            _assemble(by_chunk[3][:j + 1]), out))
-    return torch.cat(outs, dim=1).reshape(B, H, Lr, dv).to(q.dtype)
+    full = torch.cat(outs, dim=1).reshape(B, H, Lr, dv).to(q.dtype)
+    if return_rep_idx:
+        return full, [b[4] for b in begun]
+    return full
 
 
 @torch.no_grad()

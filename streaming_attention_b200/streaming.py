@@ -94,9 +94,8 @@ class ArticleStreamingAttention:
         self.dtype = _resolve_dtype(dtype)
         if block_size < 2:
             raise ValueError("block_size must be at least 2")
-        if self.dtype == torch.float64:
-            raise ValueError("unsupported dtype torch.float64: the kernels compute in float32 "
-                             "(float32, float16 and bfloat16 are accepted)")
+        # the state and the arithmetic are float32 whatever ``dtype`` is; outputs
+        # are returned in ``dtype`` and state sizes are counted in it
         self.dim = int(dim)
         self.value_dim = int(value_dim)
         self.degree = int(degree)

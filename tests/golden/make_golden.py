@@ -15,7 +15,10 @@ reference's outputs:
 * the representative weights, and the ``FastArticleStats`` fields;
 * for the segment-mean variant (triton_article_attention.py), the reps of
   ``build_segment_mean_coreset`` and, at compress_stride 1, the exact
-  attention it reduces to (``segment_*.npz``).
+  attention it reduces to (``segment_*.npz``);
+* the selections of every completed block of full-length config-shaped
+  sequences (``selections_full.npz``: block-local indices and a digest of the
+  keys, which selection_inputs.py regenerates at test time).
 
 Degree 3 is outside the reference fast path (``num_taylor_features`` raises at
 fast_article_attention.py:141-142).  For degree 3 the fixture is composed from
@@ -359,14 +362,56 @@ def make_segment(path: str):
         np.savez_compressed(os.path.join(HERE, name + ".npz"), **rec)
 
 
+def make_selections(fa) -> None:
+    """selections_full.npz: the reference's coreset selection of every completed
+    block of full-length config-shaped sequences (all heads of configs 3 and 4,
+    two heads of config 5), as block-local indices (uint8: block_size <= 256),
+    with a SHA-256 of each sequence's keys (regenerated at test time by
+    selection_inputs.keys_for)."""
+    sys.path.insert(0, HERE)
+    import selection_inputs as si
+
+    rec = {}
+    meta = {}
+    for cfg_id, c in si.CONFIGS.items():
+        N, bs = c["N"], c["bs"]
+        nc = (N - 1) // bs
+        m = (bs + 1) // 2
+        local = np.zeros((len(c["heads"]), nc * m), np.uint8)
+        digest = np.zeros((len(c["heads"]), 32), np.uint8)
+        for row, head in enumerate(c["heads"]):
+            k = si.keys_for(cfg_id, head)
+            digest[row] = si.keys_digest(k)
+            kt = torch.from_numpy(k)
+            idx, _ = _selected_indices(fa, kt, torch.zeros(N, 1), bs, c["compressor"], seed=head)
+            starts = (np.arange(nc * m) // m) * bs
+            loc = idx.astype(np.int64) - starts
+            assert loc.min() >= 0 and loc.max() < bs
+            local[row] = loc.astype(np.uint8)
+        rec[f"cfg{cfg_id}_local"] = local
+        rec[f"cfg{cfg_id}_digest"] = digest
+        rec[f"cfg{cfg_id}_heads"] = np.asarray(c["heads"], np.int32)
+        meta[str(cfg_id)] = {k_: v_ for k_, v_ in c.items() if k_ != "heads"}
+        print(f"config {cfg_id}: {len(c['heads'])} sequences, {nc} blocks each", flush=True)
+    rec["meta"] = np.frombuffer(json.dumps(meta).encode(), dtype=np.uint8)
+    np.savez_compressed(os.path.join(HERE, "selections_full.npz"), **rec)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
     ap.add_argument("--only", default=None)
     ap.add_argument("--streaming-only", action="store_true")
     ap.add_argument("--segment-only", action="store_true")
+    ap.add_argument("--selections-only", action="store_true",
+                    help="only selections_full.npz (full-size selection pins)")
     args = ap.parse_args()
     torch.set_num_threads(1)
+    if args.selections_only:
+        fa, _ = _load_reference(args.reference)
+        make_selections(fa)
+        print("wrote selections_full")
+        return
     if args.segment_only:
         make_segment(args.reference)
         print("wrote segment")
@@ -385,7 +430,8 @@ def main() -> None:
         make_misc(fa, st)
         make_streaming(fa, st)
         make_segment(args.reference)
-        print("wrote misc, streaming, segment")
+        make_selections(fa)
+        print("wrote misc, streaming, segment, selections_full")
 
 
 if __name__ == "__main__":

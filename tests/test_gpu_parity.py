@@ -139,6 +139,33 @@ def test_stats_and_two_dim_entry(dev):
     assert O.relative_l2(out.cpu().numpy(), g["out"][0, 0]) < TOL
 
 
+def test_host_inputs_report_the_reference_cpu_stats(dev):
+    """Host tensors with low_mode="auto": the stats the reference reports for
+    CPU inputs (the streaming low path), the output computed on the GPU."""
+    g = load_golden("reftest_shapes_sorted_pair")
+    q, k, v = (torch.from_numpy(g[x][0, 0]) for x in "qkv")
+    out, st = sa.fast_article_causal_attention(q, k, v, degree=2, block_size=32, scale=1.0,
+                                               compressor="sorted_pair", return_stats=True)
+    assert out.device.type == "cpu"
+    for key, val in g["meta"]["stats"].items():
+        assert getattr(st, key) == val, key
+    assert O.relative_l2(out.numpy(), g["out"][0, 0]) < TOL
+
+
+def test_float64_inputs_are_computed_and_returned(dev):
+    """float64 inputs: computed in float32 by the kernels, returned as float64."""
+    g = load_golden("cfg1_full")
+    q, k, v = (torch.from_numpy(g[x]).to(dev).double() for x in "qkv")
+    out = sa.fast_article_causal_attention(q, k, v, degree=2, block_size=128, scale=1.0)
+    assert out.dtype == torch.float64
+    assert O.relative_l2(out.cpu().numpy(), g["out"]) < TOL
+    att = sa.ArticleStreamingAttention(32, 32, block_size=16, dtype="float64", device=dev)
+    att.update(k[0, 0, 0], v[0, 0, 0])
+    y = att.query(q[0, 0, 0])
+    assert y.dtype == torch.float64
+    assert att.state_size_bytes() == (att.features * 33 + 64) * 8
+
+
 def test_half_precision_inputs_and_strided_views(dev):
     g = load_golden("cfg1_full")
     q, k, v = (torch.from_numpy(g[x]).to(dev) for x in "qkv")

@@ -53,6 +53,22 @@ def test_stats_formula_matches_reference(name):
         assert getattr(st, key) == val, key
 
 
+def test_stats_auto_low_mode_resolves_by_input_device():
+    """low_mode="auto" means "stream" for host inputs and "prefix" for CUDA inputs
+    (fast_article_attention.py:616); the fixture ran the reference on CPU."""
+    g = load_golden("reftest_shapes_sorted_pair")
+    m = g["meta"]
+    n, d = g["q"].shape[2:]
+    dv = g["v"].shape[-1]
+    host = fast._stats(n, d, dv, m["degree"], m["bs"], m["compressor"], "auto", 2048, 4, "cpu")
+    for key, val in m["stats"].items():
+        assert getattr(host, key) == val, key
+    dev = fast._stats(n, d, dv, m["degree"], m["bs"], m["compressor"], "auto", 2048, 4, "cuda")
+    F = sa.num_taylor_features(d, m["degree"])
+    assert dev.scratch_low_prefix_bytes == n * F * (1 + dv) * 4
+    assert host.scratch_low_prefix_bytes == F * (1 + dv) * 4
+
+
 def test_num_taylor_features():
     assert sa.num_taylor_features(64, 2) == 2145
     assert sa.num_taylor_features(16, 3) == 969

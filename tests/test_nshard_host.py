@@ -74,3 +74,56 @@ def test_zigzag_ownership_covers_every_chunk_once():
         assert nshard.owned_chunks(1, 4, "contiguous") == [1]
     with pytest.raises(ValueError, match="layout"):
         nshard.owned_chunks(0, 2, "striped")
+
+
+# ---------------------------------------------------------------------------
+# failure detection: a rank that is gone before the exchange
+# ---------------------------------------------------------------------------
+
+def _failing_rank(rank, world, port, how, results):
+    """Rank 1 leaves (or raises) after joining the group and before the
+    exchange; rank 0 runs the exchange and records how it ended."""
+    import datetime
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        results[1] = "left"
+        if how == "raise":
+            raise RuntimeError("rank 1 failed before the exchange")
+        return          # leaves between steps: none of its collectives is in flight
+    state = torch.ones(5)
+    rk = torch.zeros(2, 3, 4)
+    t0 = time.monotonic()
+    try:
+        nshard.exchange(state, rk, rk[..., :2], torch.zeros(2, 3), rank, world)
+        results[0] = ("completed", time.monotonic() - t0, "")
+    except Exception as exc:   # the survivor must get an error, not hang
+        results[0] = ("raised", time.monotonic() - t0, f"{type(exc).__name__}: {exc}"[:300])
+
+
+@pytest.mark.timeout(180)
+@pytest.mark.parametrize("how", ["exit", "raise"])
+def test_exchange_fails_with_an_error_when_a_rank_is_gone(how):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    with ctx.Manager() as mgr:
+        results = mgr.dict()
+        procs = [ctx.Process(target=_failing_rank, args=(r, 2, port, how, results)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=150)
+        alive = [p.is_alive() for p in procs]
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+        res = dict(results)
+    assert not any(alive), "a rank hung"
+    assert res.get(1) == "left"
+    outcome, secs, msg = res[0]
+    assert outcome == "raised", f"the exchange finished without the other rank: {outcome}"
+    # within the process group's 5 s timeout (plus start-up slack), not after a hang
+    assert secs < 60, (secs, msg)
