@@ -242,9 +242,11 @@ int sa_shard_end(const float* q, const float* k, const float* v, int64_t bh, int
  * workspace: the scratch is a SA_STATIC_SCRATCH_BYTES array built into the
  * library, held by every GPU that loads it until the process exits.  Problems
  * whose sa_fast_attention_workspace_size exceeds it are rejected with
- * SA_ERR_INVALID_ARG.  The first call on each device looks up the array's
- * address (make it before any stream capture).  All calls share the array:
- * calls that overlap on the GPU race, so order them.  Allocates nothing. */
+ * SA_ERR_INVALID_ARG.  The first call on each device loads the library's
+ * device code there (make it before any stream capture); every call looks up
+ * the array's address anew, so a device reset that moves it is harmless.  All
+ * calls share the array: calls that overlap on the GPU race, so order them.
+ * Allocates nothing. */
 int sa_fast_attention_static_scratch(const float* q, const float* k, const float* v, int64_t bh,
                                      int64_t n, int d, int dv, int degree, int block_size,
                                      float scale, int compressor, const float* dirs,

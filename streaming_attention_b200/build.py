@@ -3,13 +3,16 @@
     python -m streaming_attention_b200.build        # or build() from Python
 
 The library is written next to this file so that it travels with the source
-tree; objects go to ``_build/`` at the repository root.  Rebuilds only when a
-source or header is newer than the library.
+tree; objects go to ``_build/`` at the repository root.  Rebuilds only when the
+sources, headers or flags differ from those the library was built from (a
+content hash kept beside it, so that a copied tree with new file times does
+not rebuild).
 """
 
 from __future__ import annotations
 
 import glob
+import hashlib
 import os
 import shutil
 import subprocess
@@ -19,6 +22,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libsa_b200.so")
+STAMP = LIB + ".stamp"
 BUILD_DIR = os.path.join(ROOT, "_build")
 
 NVCC_FLAGS = [
@@ -45,11 +49,21 @@ def headers():
     return sorted(glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(ROOT, "include", "*.h")))
 
 
+def source_hash() -> str:
+    h = hashlib.sha256()
+    h.update(" ".join(NVCC_FLAGS).encode())
+    for p in sources() + headers() + [__file__]:
+        h.update(os.path.relpath(p, ROOT).encode())
+        with open(p, "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()
+
+
 def needs_build() -> bool:
-    if not os.path.exists(LIB):
+    if not os.path.exists(LIB) or not os.path.exists(STAMP):
         return True
-    t = os.path.getmtime(LIB)
-    return any(os.path.getmtime(p) > t for p in sources() + headers() + [__file__])
+    with open(STAMP) as f:
+        return f.read().strip() != source_hash()
 
 
 def build(force: bool = False, verbose: bool = False, jobs: int = 8) -> str:
@@ -77,6 +91,8 @@ def build(force: bool = False, verbose: bool = False, jobs: int = 8) -> str:
     if out.returncode != 0:
         raise RuntimeError("link failed:\n" + out.stdout)
     os.replace(tmp, LIB)
+    with open(STAMP, "w") as f:
+        f.write(source_hash() + "\n")
     return LIB
 
 

@@ -17,13 +17,15 @@
 // streams, or different host threads, without ordering between them) race on
 // the array and corrupt each other's results; callers must order them.
 //
-// Set-up: the first call on each device (with that device current) looks up
-// the array's device address with cudaGetSymbolAddress and caches it.  Host
-// code cannot use the array's name as a device pointer (it names a host-side
-// stand-in), which is why the looked-up address is what goes to the kernels.
-// Make that first call before any stream capture begins.
-#include <mutex>
-
+// Set-up: host code cannot use the array's name as a device pointer (it names
+// a host-side stand-in), so the device address goes to the kernels instead,
+// taken with cudaGetSymbolAddress with the caller's device current.  The first
+// call on a device also loads the library's device code there; make it before
+// any stream capture begins.  The address is taken again on every call (a
+// host-side table lookup once the code is loaded) rather than cached: after a
+// cudaDeviceReset, or when the device's context is destroyed and made again,
+// the code is reloaded and the array can sit at a new address, and a cached
+// one would then point at memory the library no longer owns.
 #include "sa_common.cuh"
 
 namespace {
@@ -32,24 +34,13 @@ static_assert(SA_STATIC_SCRATCH_BYTES % 256 == 0, "static scratch must be a mult
 
 static __device__ __align__(256) unsigned char g_static_scratch[SA_STATIC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};
-
+// The array's address in the current device's context.
 int static_scratch_address(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return sa::set_error(SA_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevices) return sa::set_error(SA_ERR_UNSUPPORTED, "device index %d too large", dev);
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_static_scratch);
-    if (e != cudaSuccess || p == nullptr)
-      return sa::set_error(SA_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
-    g_scratch_addr[dev] = p;
-  }
-  *out = g_scratch_addr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+  if (e != cudaSuccess || p == nullptr)
+    return sa::set_error(SA_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
+  *out = p;
   return SA_OK;
 }
 

@@ -59,11 +59,13 @@ def _with_workspace(lib, c, qkv, t, stream):
     return out, idx
 
 
-def _static(lib, c, qkv, t, stream):
+def _static(lib, c, qkv, t, stream, with_idx=True):
     bh, n, _ = qkv[0].shape
     out = torch.empty(bh, n, qkv[2].shape[-1], device=qkv[0].device)
-    idx = torch.empty(bh, max(1, t.completed_blocks * t.reps_per_block), device=qkv[0].device, dtype=torch.int32)
-    _lib.check(lib.sa_fast_attention_static_scratch(*_args(c, qkv, t), out.data_ptr(), idx.data_ptr(), stream),
+    idx = (torch.empty(bh, max(1, t.completed_blocks * t.reps_per_block), device=qkv[0].device, dtype=torch.int32)
+           if with_idx else None)
+    _lib.check(lib.sa_fast_attention_static_scratch(*_args(c, qkv, t), out.data_ptr(),
+                                                    None if idx is None else idx.data_ptr(), stream),
                "sa_fast_attention_static_scratch")
     return out, idx
 
@@ -93,3 +95,28 @@ def test_static_scratch_rejects_problems_above_its_size():
                                               1e-12, None, None, None)
     assert rc == _lib.SA_ERR_INVALID_ARG
     assert "static scratch" in _lib.last_error()
+
+
+def test_static_scratch_call_allocates_no_device_memory():
+    """The device's free memory is the same before and after a call (the
+    outputs are made before the first reading); rep_idx=None makes the call
+    keep the selected indices in the built-in array as well."""
+    assert torch.cuda.is_available(), "GPU test"
+    dev = torch.device("cuda:0")
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    c, qkv, t = _problem(3, 13, dev, B=1, H=2, N=1500, block_size=128)
+    ref, _ = _with_workspace(lib, c, qkv, t, stream)
+    _static(lib, c, qkv, t, stream, with_idx=False)      # loads the device code on this device
+    torch.cuda.synchronize(dev)
+    bh, n, _ = qkv[0].shape
+    out = torch.full((bh, n, qkv[2].shape[-1]), float("nan"), device=dev)
+    torch.cuda.synchronize(dev)
+    free0 = torch.cuda.mem_get_info(dev)[0]
+    _lib.check(lib.sa_fast_attention_static_scratch(*_args(c, qkv, t), out.data_ptr(), None, stream),
+               "sa_fast_attention_static_scratch")
+    torch.cuda.synchronize(dev)
+    free1 = torch.cuda.mem_get_info(dev)[0]
+    assert free1 == free0, (free0, free1)
+    err = O.relative_l2(out.cpu().numpy(), ref.cpu().numpy())
+    assert err < TOL, err
