@@ -81,6 +81,9 @@ def parse_args():
     ap.add_argument("--cpu-sample-heads", type=int, default=0, help="heads in the CPU sample (0 = auto)")
     ap.add_argument("--bh", type=int, default=0,
                     help="profiling only: replace B*H by this many sequences (B=1) to make a small case")
+    ap.add_argument("--profile-nshard", type=int, default=0, metavar="W",
+                    help="profiling aid: config 5's 64 sequences at N = 2048 W, split along N into W shards "
+                         "run in one process (the all-gather replaced by stacking), once")
     return ap.parse_args()
 
 
@@ -493,6 +496,26 @@ def run_exact_only(args, rank, world, dev):
             "config": {"workload": workload_name(c, args.config)}, "what": "triton_flash_causal_attention only"}
 
 
+def run_profile_nshard(world_emulated: int, dev):
+    """Profiling aid: the N-sharded arithmetic of config 5 (64 sequences) at
+    N = 2048 W on one GPU, every shard in one process, so that a single-GPU
+    profiler sees the shard kernels, the state prefix scan over up to W - 1
+    earlier states (45 MB each) among them."""
+    from streaming_attention_b200 import nshard, workloads
+
+    c = workloads.config(5, N=2048 * world_emulated)
+    q, k, v = workloads.make_inputs(c, seed=0, device=dev, generator_device="cuda")
+    kw = dict(degree=c["degree"], block_size=c["block_size"], scale=c["scale"], compressor=c["compressor"], seed=0)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    nshard.nshard_emulate(q, k, v, world=world_emulated, **kw)
+    t1.record()
+    torch.cuda.synchronize(dev)
+    return {"what": "config 5 N-sharded arithmetic, shards emulated in one process", "N": c["N"],
+            "shards": world_emulated, "ms": t0.elapsed_time(t1)}
+
+
 def run_extra_config(cfg_id: int, rank: int, world: int, dev, steps: int, warmup: int):
     """One of configs 1, 2, 4 at full size, heads sharded over the ranks (config
     1 is a single sequence: measured on one GPU only)."""
@@ -719,6 +742,11 @@ def main():
     try:
         if args.exact_only:
             line = run_exact_only(args, rank, world, dev)
+            if rank == 0:
+                print(json.dumps(line), flush=True)
+            return
+        if args.profile_nshard:
+            line = run_profile_nshard(args.profile_nshard, dev)
             if rank == 0:
                 print(json.dumps(line), flush=True)
             return
