@@ -487,7 +487,8 @@ def run_exact_only(args, rank, world, dev):
     q, k, v = workloads.make_inputs(c, seed=0, device=dev, generator_device="cuda",
                                     heads=(rank * per, (rank + 1) * per))
     s = workloads.attention_scale(c)
-    ms = timed(lambda: sa.triton_flash_causal_attention(q[None, :, 0], k[None, :, 0], v[None, :, 0], scale=s),
+    q3, k3, v3 = (x.reshape(per, c["N"], -1) for x in (q, k, v))
+    ms = timed(lambda: sa.triton_flash_causal_attention(q3[None], k3[None], v3[None], scale=s),
                args.steps, args.warmup, world, dev)
     if rank != 0:
         return None

@@ -234,17 +234,32 @@ _CHECK_STATUS = os.environ.get("SA_CHECK_STATUS", "0") == "1"
 _HOST_CHUNK_BYTES = int(os.environ.get("SA_HOST_CHUNK_BYTES", str(384 << 20)))
 
 
+def _chunk_plan(bh: int, base: int) -> list:
+    """Sequences per chunk of the host path: full chunks of `base` while more
+    than two are left, then chunks of half the rest (at least base / 8), so that
+    the last chunk's kernels and copy-back -- the part no later copy hides --
+    are short."""
+    sizes, rem, low = [], bh, max(1, base // 8)
+    while rem > 0:
+        c = base if rem > 2 * base else max(low, -(-rem // 2))
+        c = min(c, rem)
+        sizes.append(c)
+        rem -= c
+    return sizes
+
+
 def _run_host(q3: Tensor, k3: Tensor, v3: Tensor, *, batch: int, heads: int, degree: int, block_size: int,
               scale: float, compressor: str, seed: int, eps: float, head_range: Optional[Tuple[int, int]] = None,
               device: Optional[torch.device] = None) -> Tensor:
     """Forward of host-resident sequences (contiguous float32 [bh, n, *] CPU
-    tensors) on the GPU.  The sequences go through in chunks: chunk i's
-    host->device copy, its kernels and its device->host copy run on three
-    streams, so the copies of one chunk overlap the kernels of its neighbours;
-    chunks alternate between two compute streams (each with its own device
-    slot), which lets one chunk's last wave of CTAs share the GPU with the
-    next chunk's first.  Pinned inputs give asynchronous copies; the output is
-    a pinned CPU tensor."""
+    tensors) on the GPU.  The sequences go through in chunks (_chunk_plan):
+    chunk i's host->device copy, its kernels and its device->host copy run on
+    separate streams, so the copies of one chunk overlap the kernels of its
+    neighbours and the two copy directions overlap each other; chunks take
+    turns over three device slots and alternate between two compute streams,
+    which lets one chunk's last wave of CTAs share the GPU with the next
+    chunk's first.  Pinned inputs give asynchronous copies; the output is a
+    pinned CPU tensor."""
     bh, n, d = q3.shape
     dv = v3.shape[-1]
     dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -254,14 +269,17 @@ def _run_host(q3: Tensor, k3: Tensor, v3: Tensor, *, batch: int, heads: int, deg
     g0 = head_range[0] if head_range is not None else 0
     per_seq = n * (2 * d + dv) * 4
     chunk = max(1, min(bh, _HOST_CHUNK_BYTES // max(per_seq, 1)))
-    bounds = [(s0, min(s0 + chunk, bh)) for s0 in range(0, bh, chunk)]
+    bounds, s0 = [], 0
+    for c in _chunk_plan(bh, chunk):
+        bounds.append((s0, s0 + c))
+        s0 += c
     with torch.cuda.device(dev):
         main = torch.cuda.current_stream(dev)
         h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         comp = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
         for s_ in (h2d, d2h, *comp):
             s_.wait_stream(main)
-        nslot = min(2, len(bounds))
+        nslot = min(3, len(bounds))
         dq = [torch.empty(chunk, n, d, device=dev) for _ in range(nslot)]
         dk = [torch.empty(chunk, n, d, device=dev) for _ in range(nslot)]
         dvv = [torch.empty(chunk, n, dv, device=dev) for _ in range(nslot)]
@@ -271,16 +289,16 @@ def _run_host(q3: Tensor, k3: Tensor, v3: Tensor, *, batch: int, heads: int, deg
         copied_out = [torch.cuda.Event() for _ in range(nslot)]
         for i, (s0, s1) in enumerate(bounds):
             slot, cnt = i % nslot, s1 - s0
-            if i >= nslot:   # the slot's inputs are free once chunk i - 2's kernels are done
+            if i >= nslot:   # the slot's inputs are free once chunk i - nslot's kernels are done
                 h2d.wait_event(computed[slot])
             with torch.cuda.stream(h2d):
                 dq[slot][:cnt].copy_(q3[s0:s1], non_blocking=True)
                 dk[slot][:cnt].copy_(k3[s0:s1], non_blocking=True)
                 dvv[slot][:cnt].copy_(v3[s0:s1], non_blocking=True)
                 in_ready[slot].record(h2d)
-            cs = comp[slot]
+            cs = comp[i % 2]
             cs.wait_event(in_ready[slot])
-            if i >= nslot:   # and its output once chunk i - 2 has been copied back
+            if i >= nslot:   # and its output once chunk i - nslot has been copied back
                 cs.wait_event(copied_out[slot])
             with torch.cuda.stream(cs):
                 _run(dq[slot][:cnt], dk[slot][:cnt], dvv[slot][:cnt], batch=batch, heads=heads, degree=degree,

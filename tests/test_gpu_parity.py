@@ -116,8 +116,8 @@ def test_host_tensors_stream_through_the_gpu(dev, monkeypatch):
     q, k, v = workloads.make_inputs(c, seed=5)
     kw = dict(degree=2, block_size=128, compressor="sorted_pair", seed=7)
     ref = sa.fast_article_causal_attention(q.to(dev), k.to(dev), v.to(dev), **kw).cpu()
-    # small chunks: 6 sequences in 4 chunks over both device slots
-    monkeypatch.setattr(fast, "_HOST_CHUNK_BYTES", 700 * (2 * 64 + 64) * 4 * 2 - 1)
+    # small chunks: 6 sequences in chunks of 2, 2, 1, 1 over the three device slots
+    monkeypatch.setattr(fast, "_HOST_CHUNK_BYTES", 700 * (2 * 64 + 64) * 4 * 2)
     out = sa.fast_article_causal_attention(q.pin_memory(), k.pin_memory(), v.pin_memory(), **kw)
     assert out.device.type == "cpu"
     assert torch.equal(out, ref)

@@ -138,3 +138,14 @@ def test_bench_csv_columns_and_inputs_match_the_reference_benchmark():
     q, k, v = bench_csv.make_data(1024, 32, 32, radius=1.0, data="unit_ball", seed=0)
     np.testing.assert_array_equal(q.numpy(), g["q"].reshape(1024, 32))
     np.testing.assert_array_equal(v.numpy(), g["v"].reshape(1024, 32))
+
+
+def test_host_chunk_plan_tapers_and_covers_every_sequence():
+    from streaming_attention_b200.fast import _chunk_plan
+    assert _chunk_plan(256, 61) == [61, 61, 61, 37, 18, 9, 7, 2]
+    assert _chunk_plan(6, 2) == [2, 2, 1, 1]
+    assert _chunk_plan(1, 61) == [1]
+    for bh in range(1, 200, 7):
+        for base in (1, 3, 16, 61):
+            plan = _chunk_plan(bh, base)
+            assert sum(plan) == bh and max(plan) <= base and min(plan) >= 1
