@@ -220,7 +220,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
   uint64_t* out_free = out_full + 1;        // one arrival per generator warp, once per sub-tile
   uint64_t* u_done = out_free + 1;          // commit, once per update phase
   uint64_t* drain = u_done + 1;
-  uint64_t* gbar = drain + 1;               // the generator threads' own barrier
+  uint64_t* gbar = drain + 1;               // the generator warps' own barrier
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbar + 1);
   int* abort_word = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -250,7 +250,7 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     mbar_init(out_free, kGenWarps);
     mbar_init(u_done, 1);
     mbar_init(drain, 1);
-    mbar_init(gbar, kGenThreads);
+    mbar_init(gbar, kGenWarps);
     *abort_word = 0;
     fence_mbar_init();
   }
@@ -424,22 +424,24 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     int stg_use = 0, sb_use = 0, out_use = 0;
     bool ok = true;
     const int64_t col_stride = p.dv + 1;
-    // The generator threads' barrier: an mbarrier all of them arrive on, waited
+    // The generator warps' barrier: an mbarrier each warp arrives on once, waited
     // on with the bounded wait (a generator that gave up stops arriving, and
     // the others then give up instead of hanging).  Every wait of a generator
     // warp has one verdict for all its lanes (mbar_wait_warp), so the warp's
     // .sync.aligned TMEM instructions always run converged.
     uint32_t gphase = 0;
-    auto gen_sync = [&]() -> bool {
-      mbar_arrive(gbar);
-      const bool r = mbar_wait_warp(gbar, gphase, ab, kErrMomWait);
-      gphase ^= 1;
-      return r;
-    };
     // one arrival per warp, once every lane's stores (TMEM or shared) are done
     auto warp_arrive = [&](uint64_t* bar) {
       __syncwarp();
       if (lane == 0) mbar_arrive(bar);
+    };
+    // (one arrival per warp rather than per thread: 512 arrivals on one mbarrier
+    // serialize in the shared-memory atomics unit)
+    auto gen_sync = [&]() -> bool {
+      warp_arrive(gbar);
+      const bool r = mbar_wait_warp(gbar, gphase, ab, kErrMomWait);
+      gphase ^= 1;
+      return r;
     };
 
     float* part_h = p.part + ((int64_t)g * p.bh + h) * p.n * col_stride;

@@ -516,18 +516,44 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     }
     asm volatile("bar.sync 1, 256;" ::: "memory");
     if (o_ok && bulk_low) {
-      // the rows arrive by bulk copy: every read below is from shared memory
+      // The rows arrive by bulk copy: every read below is from shared memory.
+      // Four rows per pass (rows r, r+8, r+16, r+24 of this warp), the slices'
+      // loads of a pass independent of each other, so their latencies overlap
+      // instead of forming one chain per element.
       if (mbar_wait_warp(lowfull, 0, ab, kErrWaitO)) {
+        constexpr int kRP = 4, kNC = DVP / 32;
         const float* lb = reinterpret_cast<const float*>(smem);
         const int ls = p.dv + 1;
         const int nrows = (int)erows;
-        for (int r = warp - 2; r < nrows; r += 8) {
-          float* orow = p.out + (h * p.n + q0 + r) * (int64_t)p.dv;
-          const float dm = dms[r];
-          for (int col = lane; col < p.dv; col += 32) {
-            float lv = 0.0f;
-            for (int gi = 0; gi < p.groups; ++gi) lv += lb[gi * lblk + r * ls + col];
-            orow[col] = __fdiv_rn(os[r * OS + col] + lv, dm);
+        for (int r0 = warp - 2; r0 < nrows; r0 += 8 * kRP) {
+          float lv[kRP][kNC];
+#pragma unroll
+          for (int a = 0; a < kRP; ++a)
+#pragma unroll
+            for (int c = 0; c < kNC; ++c) lv[a][c] = 0.0f;
+          for (int gi = 0; gi < p.groups; ++gi) {
+#pragma unroll
+            for (int a = 0; a < kRP; ++a) {
+              const int r = r0 + 8 * a;
+              const float* lr = lb + gi * lblk + (r < nrows ? r : 0) * ls;
+#pragma unroll
+              for (int c = 0; c < kNC; ++c) {
+                const int col = c * 32 + lane;
+                if (col < p.dv) lv[a][c] += lr[col];
+              }
+            }
+          }
+#pragma unroll
+          for (int a = 0; a < kRP; ++a) {
+            const int r = r0 + 8 * a;
+            if (r >= nrows) continue;
+            float* orow = p.out + (h * p.n + q0 + r) * (int64_t)p.dv;
+            const float dm = dms[r];
+#pragma unroll
+            for (int c = 0; c < kNC; ++c) {
+              const int col = c * 32 + lane;
+              if (col < p.dv) orow[col] = __fdiv_rn(os[r * OS + col] + lv[a][c], dm);
+            }
           }
         }
       }
