@@ -154,6 +154,18 @@ __global__ void split_rows_kernel(const float* __restrict__ src, int64_t rows, i
   }
 }
 
+// The same split of n4 float4 elements (rows without padding).
+__global__ void split_flat4_kernel(const float4* __restrict__ src, int64_t n4, float4* __restrict__ hi,
+                                   float4* __restrict__ lo) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n4; e += (int64_t)gridDim.x * blockDim.x) {
+    const float4 x = __ldg(src + e);
+    const float4 h = make_float4(__uint_as_float(tc_split_hi(x.x)), __uint_as_float(tc_split_hi(x.y)),
+                                 __uint_as_float(tc_split_hi(x.z)), __uint_as_float(tc_split_hi(x.w)));
+    hi[e] = h;
+    lo[e] = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+  }
+}
+
 // Transposing split: src [bh, rows, cols] -> hi / lo [bh, cols_pad, rows_pad]
 // (tf32 hi and fp32 remainder, zero padded), through a 32 x 32 shared tile so
 // that both the reads and the writes are coalesced.  This is the K-major
@@ -231,6 +243,16 @@ int launch_split(const float* src, int64_t rows, int cols, int cols_pad, float* 
   if (rows == 0) return SA_OK;
   const int64_t total = rows * cols_pad;
   const int threads = 256;
+  if (cols == cols_pad && cols % 4 == 0 &&
+      ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo)) & 15) == 0) {
+    // unpadded rows: the split is elementwise over the whole array, 16 bytes a thread
+    const int64_t n4 = total / 4;
+    const int64_t blocks = min((n4 + threads - 1) / threads, (int64_t)148 * 16);
+    split_flat4_kernel<<<(unsigned)blocks, threads, 0, stream>>>(reinterpret_cast<const float4*>(src), n4,
+                                                                 reinterpret_cast<float4*>(hi),
+                                                                 reinterpret_cast<float4*>(lo));
+    return check_launch("split_flat4_kernel");
+  }
   const int64_t blocks = min((total + threads - 1) / threads, (int64_t)148 * 16);
   split_rows_kernel<<<(unsigned)blocks, threads, 0, stream>>>(src, rows, cols, cols_pad, hi, lo);
   return check_launch("split_rows_kernel");

@@ -122,10 +122,10 @@ flash_tc_kernel(const __grid_constant__ CUtensorMap tm_kh, const __grid_constant
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sfull[b], 1);
-      mbar_init(&pfull[b], 256);
+      mbar_init(&pfull[b], 8);   // one arrival per query-row warp
       mbar_init(&sfree[b], 1);
     }
-    mbar_init(qready, 256);
+    mbar_init(qready, 8);
     mbar_init(ofull, 1);
     mbar_init(drain, 1);
     *abort_word = 0;
@@ -273,7 +273,8 @@ flash_tc_kernel(const __grid_constant__ CUtensorMap tm_kh, const __grid_constant
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(qready);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(qready);
     }
     // O columns this half rescales and writes: 32-column chunks c with (c & 1) == half
     // (for DVP = 32 the single chunk belongs to half 0)
@@ -405,7 +406,8 @@ flash_tc_kernel(const __grid_constant__ CUtensorMap tm_kh, const __grid_constant
       tmem_st32(tS + 64, lo);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&pfull[b]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pfull[b]);
     }
     // both halves' sums (they share m)
     lsum[half * 128 + row] = l;

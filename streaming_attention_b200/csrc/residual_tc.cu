@@ -225,10 +225,10 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sfull[b], 1);
-      mbar_init(&pfull[b], 256);
+      mbar_init(&pfull[b], 8);   // one arrival per query-row warp
       mbar_init(&sfree[b], 1);
     }
-    mbar_init(qready, 256);
+    mbar_init(qready, 8);
     mbar_init(ofull, 1);
     mbar_init(drain, 1);
     mbar_init(lowfull, 1);
@@ -419,7 +419,8 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(qready);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(qready);
     }
     const int64_t ci = valid ? i / p.bs : 0;
     const int64_t lim = valid ? (p.c_off + ci) * p.m_blk : 0;    // reps r < lim are active for this query
@@ -471,7 +472,8 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
       tmem_st32(tS + 64, lo);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&pfull[b]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pfull[b]);
     }
     // the two halves' denominators
     float* den_x = reinterpret_cast<float*>(abort_word + 1);   // [2][128]
