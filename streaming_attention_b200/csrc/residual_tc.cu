@@ -12,8 +12,9 @@
 //   warp 0      TMA producer: K_hi, K_lo, V_hi, V_lo (+ rep weights) per stage
 //   warp 1      TMEM owner and MMA issuer: the converged warp runs the loop, an
 //               elected lane issues every tcgen05.mma and commit
-//   warps 2..9  query rows: two warps per TMEM lane quarter, one row per
-//               thread, each warp of a pair owning 32 of a tile's 64 columns;
+//   warps 2..17 query rows: four warps per TMEM lane quarter, one row per
+//               thread, each warp of a quarter owning 16 of a tile's 64 columns
+//               (more warps shorten the P step that each P V product waits for);
 //               they write the scaled query into TMEM, turn each S tile into
 //               P = f(S), then run the epilogue
 // Precision: 3xTF32.  Every fp32 operand x is carried as hi = rna_tf32(x) and
@@ -48,7 +49,11 @@ using namespace tc;
 
 constexpr int kRowsQ = 128;    // queries per CTA = UMMA M
 constexpr int kTile = 64;      // keys per tile = N of S = K of PV
-constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 query rows
+constexpr int kQW = 4;          // query-row warps per TMEM lane quarter (column groups)
+constexpr int kCW = kTile / kQW;        // columns of a key tile one query-row warp handles (16)
+constexpr int kQueryWarps = 4 * kQW;    // 16
+constexpr int kQueryThreads = 32 * kQueryWarps;
+constexpr int kThreads = 64 + kQueryThreads;   // warp 0 TMA, warp 1 MMA, warps 2.. query rows
 
 // status codes written to the launch's status word
 constexpr int kErrWaitQ = 101, kErrWaitFull = 102, kErrWaitSfree = 103, kErrWaitP = 104, kErrWaitS = 105,
@@ -88,7 +93,7 @@ struct Layout {
   static constexpr uint32_t kO = 2 * DP + 256;
   static constexpr bool kPVStack = kO + 2 * DVP <= 512;  // O' = P [V_hi | V_lo] fits
   static_assert(kO + DVP <= 512, "TMEM columns");
-  static constexpr uint32_t kSmemBytes = kStages * kStage + kW + (2 * kStages + 11) * 8 + 64 + 2 * 128 * 4 + 1024;
+  static constexpr uint32_t kSmemBytes = kStages * kStage + kW + (2 * kStages + 11) * 8 + 64 + kQW * 128 * 4 + 1024;
 };
 
 template <int DEG>
@@ -127,13 +132,13 @@ __device__ __forceinline__ float exp_score(float x) {
   return __expf(CLAMP ? fminf(x, 80.0f) : x);
 }
 
-// P = w (e^x - P_t(x)) over 32 rep scores, split hi / lo; MASK zeroes j > jhi;
+// P = w (e^x - P_t(x)) over NC rep scores, split hi / lo; MASK zeroes j > jhi;
 // w = nullptr for unit weights.
-template <bool MASK, int DEG, bool CLAMP>
-__device__ __forceinline__ void rep_to_p(const float (&sv)[32], const float* w, int jhi, float& den,
-                                         uint32_t (&hi)[32], uint32_t (&lo)[32]) {
+template <bool MASK, int DEG, bool CLAMP, int NC>
+__device__ __forceinline__ void rep_to_p(const float (&sv)[NC], const float* w, int jhi, float& den,
+                                         uint32_t (&hi)[NC], uint32_t (&lo)[NC]) {
 #pragma unroll
-  for (int j4 = 0; j4 < 8; ++j4) {
+  for (int j4 = 0; j4 < NC / 4; ++j4) {
     float ww[4] = {1.0f, 1.0f, 1.0f, 1.0f};
     if (w) {
       const float4 w4 = reinterpret_cast<const float4*>(w)[j4];
@@ -153,12 +158,12 @@ __device__ __forceinline__ void rep_to_p(const float (&sv)[32], const float* w, 
   }
 }
 
-// P = e^x over 32 current-block scores; MASK keeps jlo <= j <= jhi only.
-template <bool MASK, bool CLAMP>
-__device__ __forceinline__ void cur_to_p(const float (&sv)[32], int jlo, int jhi, float& den, uint32_t (&hi)[32],
-                                         uint32_t (&lo)[32]) {
+// P = e^x over NC current-block scores; MASK keeps jlo <= j <= jhi only.
+template <bool MASK, bool CLAMP, int NC>
+__device__ __forceinline__ void cur_to_p(const float (&sv)[NC], int jlo, int jhi, float& den, uint32_t (&hi)[NC],
+                                         uint32_t (&lo)[NC]) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
+  for (int j = 0; j < NC; ++j) {
     float e = exp_score<CLAMP>(sv[j]);
     if (MASK && (j < jlo || j > jhi)) e = 0.0f;
     den += e;
@@ -225,10 +230,10 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sfull[b], 1);
-      mbar_init(&pfull[b], 8);   // one arrival per query-row warp
+      mbar_init(&pfull[b], kQueryWarps);   // one arrival per query-row warp
       mbar_init(&sfree[b], 1);
     }
-    mbar_init(qready, 8);
+    mbar_init(qready, kQueryWarps);
     mbar_init(ofull, 1);
     mbar_init(drain, 1);
     mbar_init(lowfull, 1);
@@ -392,30 +397,31 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     }
   } else {
     // ------------------------------------------------------------ query rows
-    // two warps per TMEM lane quarter: `half` 0 (warps 2..5) and 1 (warps 6..9)
-    // each own 32 of the 64 columns of every tile
+    // four warps per TMEM lane quarter: column group `cgp` (warps 2 + 4 cgp ..
+    // 5 + 4 cgp) owns columns [16 cgp, 16 cgp + 16) of every tile
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int cgp = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const int64_t i = q0 + row;
     const bool valid = i < p.n;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
-    // scaled query, split hi/lo, into TMEM (each half writes its 32-column chunks)
+    // scaled query, split hi/lo, into TMEM (16-column pieces, piece u written by
+    // column group u % 4)
     {
       const float* qr = p.q + (h * p.n + (valid ? i : 0)) * p.d;
 #pragma unroll
-      for (int cchunk = 0; cchunk < DP / 32; ++cchunk) {
-        if ((cchunk & 1) != half) continue;
-        uint32_t hi[32], lo[32];
+      for (int u = 0; u < DP / 16; ++u) {
+        if (u % kQW != cgp) continue;
+        uint32_t hi[16], lo[16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int a = cchunk * 32 + j;
+        for (int j = 0; j < 16; ++j) {
+          const int a = u * 16 + j;
           const float x = (valid && a < p.d) ? __ldg(qr + a) * p.scale : 0.0f;
           hi[j] = to_tf32(x);
           lo[j] = __float_as_uint(x - __uint_as_float(hi[j]));
         }
-        tmem_st32(lane_addr + L::kQhi + cchunk * 32, hi);
-        tmem_st32(lane_addr + L::kQlo + cchunk * 32, lo);
+        tmem_st16(lane_addr + L::kQhi + u * 16, hi);
+        tmem_st16(lane_addr + L::kQlo + u * 16, lo);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -435,51 +441,53 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
       const bool with_w = rep && p.rep_w != nullptr;
       if (with_w && !mbar_wait_warp(&full[s], (t / kStages) & 1, ab, kErrWaitFull)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t tS = lane_addr + L::kS0 + 128 * b + half * 32;
+      const uint32_t tS = lane_addr + L::kS0 + 128 * b + cgp * kCW;
       const int64_t row0 = rep ? (int64_t)t * kTile : kb0 + (int64_t)(t - n_rep) * kTile;
-      const int64_t col0 = row0 + half * 32;
-      float sv[32];
+      const int64_t col0 = row0 + cgp * kCW;
+      float sv[kCW];
       {
         // S = Q K_hi^T + Q K_lo^T: the two halves of the N = 128 product
-        float s2[32];
-        tmem_ld32(tS, sv);
-        tmem_ld32(tS + 64, s2);
+        float s2[kCW];
+        tmem_ld16(tS, sv);
+        tmem_ld16(tS + 64, s2);
         tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) sv[j] += s2[j];
+        for (int j = 0; j < kCW; ++j) sv[j] += s2[j];
       }
-      uint32_t hi[32], lo[32];
+      uint32_t hi[kCW], lo[kCW];
       if (rep) {
         // reps col0 + j with j <= jhi are active (r < lim)
         const int64_t rel = lim - 1 - col0;
-        const int jhi = rel < 0 ? -1 : (rel > 31 ? 31 : (int)rel);
-        const float* w = with_w ? wbuf + s * kTile + half * 32 : nullptr;
-        if (jhi == 31)
-          rep_to_p<false, DEG, CLAMP>(sv, w, jhi, den, hi, lo);
+        const int jhi = rel < 0 ? -1 : (rel > kCW - 1 ? kCW - 1 : (int)rel);
+        const float* w = with_w ? wbuf + s * kTile + cgp * kCW : nullptr;
+        if (jhi == kCW - 1)
+          rep_to_p<false, DEG, CLAMP, kCW>(sv, w, jhi, den, hi, lo);
         else
-          rep_to_p<true, DEG, CLAMP>(sv, w, jhi, den, hi, lo);
+          rep_to_p<true, DEG, CLAMP, kCW>(sv, w, jhi, den, hi, lo);
       } else {
         // keys col0 + j of the query's own block up to the query: jlo <= j <= jhi
         const int64_t rlo = bst - col0, rhi = i - col0;
-        const int jlo = rlo < 0 ? 0 : (rlo > 32 ? 32 : (int)rlo);
-        const int jhi = !valid || rhi < 0 ? -1 : (rhi > 31 ? 31 : (int)rhi);
-        if (jlo == 0 && jhi == 31)
-          cur_to_p<false, CLAMP>(sv, jlo, jhi, den, hi, lo);
+        const int jlo = rlo < 0 ? 0 : (rlo > kCW ? kCW : (int)rlo);
+        const int jhi = !valid || rhi < 0 ? -1 : (rhi > kCW - 1 ? kCW - 1 : (int)rhi);
+        if (jlo == 0 && jhi == kCW - 1)
+          cur_to_p<false, CLAMP, kCW>(sv, jlo, jhi, den, hi, lo);
         else
-          cur_to_p<true, CLAMP>(sv, jlo, jhi, den, hi, lo);
+          cur_to_p<true, CLAMP, kCW>(sv, jlo, jhi, den, hi, lo);
       }
-      tmem_st32(tS, hi);
-      tmem_st32(tS + 64, lo);
+      tmem_st16(tS, hi);
+      tmem_st16(tS + 64, lo);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&pfull[b]);
     }
-    // the two halves' denominators
-    float* den_x = reinterpret_cast<float*>(abort_word + 1);   // [2][128]
-    den_x[half * 128 + row] = den;
-    asm volatile("bar.sync 1, 256;" ::: "memory");
-    const float den_all = den_x[row] + den_x[128 + row];
+    // the column groups' denominators, added in group order
+    float* den_x = reinterpret_cast<float*>(abort_word + 1);   // [kQW][128]
+    den_x[cgp * 128 + row] = den;
+    asm volatile("bar.sync 1, %0;" ::"n"(kQueryThreads) : "memory");
+    float den_all = den_x[row];
+#pragma unroll
+    for (int g2 = 1; g2 < kQW; ++g2) den_all += den_x[g2 * 128 + row];
     // Epilogue.  The output rows and the moment kernel's `groups` partial
     // slices of the low term are read and written coalesced: each thread first
     // puts its row's O columns (and the row's divisor) into shared memory, over
@@ -491,7 +499,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     float* dms = os + kRowsQ * OS;                               // [128] max(den, eps)
     if (o_ok) {
       tc_fence_after();
-      if (half == 0) {
+      if (cgp == 0) {
         const float* lrow = p.low + (h * p.n + (valid ? i : 0)) * (int64_t)(p.dv + 1);
         float ldsum = 0.0f;
         for (int gi = 0; gi < p.groups; ++gi) ldsum += valid ? __ldg(lrow + gi * p.group_stride + p.dv) : 0.0f;
@@ -499,27 +507,26 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
         dms[row] = fmaxf(dtot, p.eps);
       }
 #pragma unroll
-      for (int cchunk = 0; cchunk < DVP / 32; ++cchunk) {
-        if (DVP > 32 && (cchunk & 1) != half) continue;
-        if (DVP == 32 && half != 0) continue;
-        float ov[32];
-        tmem_ld32(lane_addr + L::kO + cchunk * 32, ov);
+      for (int u = 0; u < DVP / 16; ++u) {
+        if (u % kQW != cgp) continue;
+        float ov[16];
+        tmem_ld16(lane_addr + L::kO + u * 16, ov);
         if (L::kPVStack) {
-          float o2[32];
-          tmem_ld32(lane_addr + L::kO + DVP + cchunk * 32, o2);
+          float o2[16];
+          tmem_ld16(lane_addr + L::kO + DVP + u * 16, o2);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) ov[j] += o2[j];
+          for (int j = 0; j < 16; ++j) ov[j] += o2[j];
         }
         tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) os[row * OS + cchunk * 32 + j] = ov[j];
+        for (int j = 0; j < 16; ++j) os[row * OS + u * 16 + j] = ov[j];
       }
     }
-    asm volatile("bar.sync 1, 256;" ::: "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(kQueryThreads) : "memory");
     if (o_ok && bulk_low) {
       // The rows arrive by bulk copy: every read below is from shared memory.
-      // Four rows per pass (rows r, r+8, r+16, r+24 of this warp), the slices'
+      // Four rows per pass (rows r, r+16, r+32, r+48 of this warp), the slices'
       // loads of a pass independent of each other, so their latencies overlap
       // instead of forming one chain per element.
       if (mbar_wait_warp(lowfull, 0, ab, kErrWaitO)) {
@@ -527,7 +534,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
         const float* lb = reinterpret_cast<const float*>(smem);
         const int ls = p.dv + 1;
         const int nrows = (int)erows;
-        for (int r0 = warp - 2; r0 < nrows; r0 += 8 * kRP) {
+        for (int r0 = warp - 2; r0 < nrows; r0 += kQueryWarps * kRP) {
           float lv[kRP][kNC];
 #pragma unroll
           for (int a = 0; a < kRP; ++a)
@@ -536,7 +543,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
           for (int gi = 0; gi < p.groups; ++gi) {
 #pragma unroll
             for (int a = 0; a < kRP; ++a) {
-              const int r = r0 + 8 * a;
+              const int r = r0 + kQueryWarps * a;
               const float* lr = lb + gi * lblk + (r < nrows ? r : 0) * ls;
 #pragma unroll
               for (int c = 0; c < kNC; ++c) {
@@ -547,7 +554,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
           }
 #pragma unroll
           for (int a = 0; a < kRP; ++a) {
-            const int r = r0 + 8 * a;
+            const int r = r0 + kQueryWarps * a;
             if (r >= nrows) continue;
             float* orow = p.out + (h * p.n + q0 + r) * (int64_t)p.dv;
             const float dm = dms[r];
@@ -560,7 +567,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
         }
       }
     } else if (o_ok) {
-      // Four rows per pass (rows r, r+8, r+16, r+24 of this warp), every load of
+      // Four rows per pass (rows r, r+16, r+32, r+48 of this warp), every load of
       // the pass issued before any store: the loads of a row do not wait for the
       // stores of the row before (the output and the slices never overlap).
       constexpr int kRP = 4, kNC = DVP / 32;
@@ -568,7 +575,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
       float* __restrict__ outp = p.out;
       const int nrows = (int)min((int64_t)kRowsQ, p.n - q0);
       const int64_t ls = p.dv + 1;
-      for (int r0 = warp - 2; r0 < nrows; r0 += 8 * kRP) {
+      for (int r0 = warp - 2; r0 < nrows; r0 += kQueryWarps * kRP) {
         float lv[kRP][kNC];
 #pragma unroll
         for (int a = 0; a < kRP; ++a)
@@ -577,7 +584,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
         for (int gi = 0; gi < p.groups; ++gi) {
 #pragma unroll
           for (int a = 0; a < kRP; ++a) {
-            const int r = r0 + 8 * a;
+            const int r = r0 + kQueryWarps * a;
             const float* lr = lowp + (h * p.n + q0 + (r < nrows ? r : 0)) * ls + gi * p.group_stride;
 #pragma unroll
             for (int c = 0; c < kNC; ++c) {
@@ -588,7 +595,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
         }
 #pragma unroll
         for (int a = 0; a < kRP; ++a) {
-          const int r = r0 + 8 * a;
+          const int r = r0 + kQueryWarps * a;
           if (r >= nrows) continue;
           float* orow = outp + (h * p.n + q0 + r) * (int64_t)p.dv;
           const float dm = dms[r];
