@@ -26,16 +26,15 @@
 // row-major k split, V tiles from the transposed v split (an MN-major tf32
 // operand runs markedly slower on the tensor cores).
 //
-// Both products put the hi and remainder copies of their B operand side by
-// side and take two MMAs of twice the width per 8-wide K step instead of three
-// N-wide ones.  That also forms the unneeded lo*lo product (a tf32 MMA's time
-// grows with N), but measured on the same GPU the three-MMA form ran this
-// kernel 10 % slower, so the doubled width stays:
-//   S' = Q_hi [K_hi; K_lo]^T + Q_lo [K_hi; K_lo]^T   (N = 128: each 32-column
-//        K chunk holds the 64 hi rows, then the 64 lo rows), S = S'[:, :64] + S'[:, 64:]
-//   O' = P_hi [V_hi | V_lo] + P_lo [V_hi | V_lo]     (N = 2 dv: each 32-key chunk of
-//        the V^T tile holds the dv hi rows, then the dv lo rows), O = O'[:, :dv] + O'[:, dv:]
-// (when 2 dv more TMEM columns do not fit, O takes the three-product form).
+// Each 8-wide K step issues the three products as three MMAs into one
+// accumulator (a tf32 MMA's time grows with N, so this costs 3/4 of the two
+// doubled-width MMAs that would also form the unneeded lo*lo product; with 16
+// query-row warps the doubled form measured 4 % slower at config 3, 8 % at
+// config 4):
+//   S = Q_hi K_hi^T + Q_hi K_lo^T + Q_lo K_hi^T   (N = 64: each 32-column K chunk
+//       holds the 64 hi rows, then the 64 lo rows)
+//   O = P_hi V_hi + P_hi V_lo + P_lo V_hi          (N = dv: each 32-key chunk of the
+//       V^T tile holds the dv hi rows, then the dv lo rows)
 #include <math.h>
 
 #include "sa_common.cuh"
@@ -91,7 +90,6 @@ struct Layout {
   static constexpr uint32_t kQhi = 0, kQlo = DP;
   static constexpr uint32_t kS0 = 2 * DP;           // buffer b: S/P_hi at kS0 + 128 b, P_lo at kS0 + 128 b + 64
   static constexpr uint32_t kO = 2 * DP + 256;
-  static constexpr bool kPVStack = kO + 2 * DVP <= 512;  // O' = P [V_hi | V_lo] fits
   static_assert(kO + DVP <= 512, "TMEM columns");
   static constexpr uint32_t kSmemBytes = kStages * kStage + kW + (2 * kStages + 11) * 8 + 64 + kQW * 128 * 4 + 1024;
 };
@@ -189,8 +187,7 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
   uint64_t* empty = bars + kStages;      // [kStages]
   uint64_t* sfull = bars + 2 * kStages;  // [2]
   uint64_t* pfull = sfull + 2;           // [2]
-  uint64_t* sfree = pfull + 2;           // [2]
-  uint64_t* qready = sfree + 2;
+  uint64_t* qready = pfull + 2;
   uint64_t* ofull = qready + 1;
   uint64_t* drain = ofull + 1;
   uint64_t* lowfull = drain + 1;          // the epilogue's low-sum rows, bulk-copied into the stages
@@ -231,7 +228,6 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sfull[b], 1);
       mbar_init(&pfull[b], kQueryWarps);   // one arrival per query-row warp
-      mbar_init(&sfree[b], 1);
     }
     mbar_init(qready, kQueryWarps);
     mbar_init(ofull, 1);
@@ -325,8 +321,8 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     // ------------------------------------------------------------ MMA issuer
     // the whole warp runs the loop; the elected lane issues MMAs and commits
     {
-      constexpr uint32_t idesc_qk = idesc_tf32(128, 2 * kTile, false, false);
-      constexpr uint32_t idesc_pv = idesc_tf32(128, L::kPVStack ? 2 * DVP : DVP, false, false);
+      constexpr uint32_t idesc_qk = idesc_tf32(128, kTile, false, false);
+      constexpr uint32_t idesc_pv = idesc_tf32(128, DVP, false, false);
       bool ok = mbar_wait_warp(qready, 0, ab, kErrWaitQ);
       if (ok) tc_fence_after();
       auto issue_pv = [&](int tp) -> bool {
@@ -344,17 +340,12 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
           for (int kk = 0; kk < kTile / 8; ++kk) {
             // 8 keys of 32-key chunk kk / 4: rows = value columns (hi rows, then lo rows)
             const uint64_t bh_ = vd + (uint64_t)(((kk >> 2) * (2 * DVP * 128) + (kk & 3) * 32) >> 4);
+            const uint64_t bl_ = bh_ + (uint64_t)((DVP * 128) >> 4);
             mma_tf32_ts(tmem + L::kO, ph + kk * 8, bh_, idesc_pv, (tp > 0 || kk > 0) ? 1u : 0u);
-            if (L::kPVStack) {
-              mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
-            } else {
-              const uint64_t bl_ = bh_ + (uint64_t)((DVP * 128) >> 4);
-              mma_tf32_ts(tmem + L::kO, ph + kk * 8, bl_, idesc_pv, 1u);
-              mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
-            }
+            mma_tf32_ts(tmem + L::kO, ph + kk * 8, bl_, idesc_pv, 1u);
+            mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
           }
           mma_commit(&empty[sp]);
-          mma_commit(&sfree[bp]);
         }
         __syncwarp();
         return true;
@@ -374,7 +365,10 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
           for (int kk = 0; kk < DP / 8; ++kk) {
             // N = 128 rows: the chunk's 64 hi rows, then its 64 lo rows
             const uint64_t bk = kd + (uint64_t)(((kk >> 2) * (2 * kTile * 128) + (kk & 3) * 32) >> 4);
+            // K_hi rows, then the chunk's K_lo rows 64 rows (8 KB) further
+            const uint64_t bkl = bk + (uint64_t)((kTile * 128) >> 4);
             mma_tf32_ts(dS, tmem + L::kQhi + kk * 8, bk, idesc_qk, kk > 0 ? 1u : 0u);
+            mma_tf32_ts(dS, tmem + L::kQhi + kk * 8, bkl, idesc_qk, 1u);
             mma_tf32_ts(dS, tmem + L::kQlo + kk * 8, bk, idesc_qk, 1u);
           }
           mma_commit(&sfull[b]);
@@ -446,13 +440,8 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
       const int64_t col0 = row0 + cgp * kCW;
       float sv[kCW];
       {
-        // S = Q K_hi^T + Q K_lo^T: the two halves of the N = 128 product
-        float s2[kCW];
         tmem_ld16(tS, sv);
-        tmem_ld16(tS + 64, s2);
         tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < kCW; ++j) sv[j] += s2[j];
       }
       uint32_t hi[kCW], lo[kCW];
       if (rep) {
@@ -511,13 +500,6 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
         if (u % kQW != cgp) continue;
         float ov[16];
         tmem_ld16(lane_addr + L::kO + u * 16, ov);
-        if (L::kPVStack) {
-          float o2[16];
-          tmem_ld16(lane_addr + L::kO + DVP + u * 16, o2);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) ov[j] += o2[j];
-        }
         tmem_wait_ld();
 #pragma unroll
         for (int j = 0; j < 16; ++j) os[row * OS + u * 16 + j] = ov[j];
