@@ -234,6 +234,28 @@ _CHECK_STATUS = os.environ.get("SA_CHECK_STATUS", "0") == "1"
 _HOST_CHUNK_BYTES = int(os.environ.get("SA_HOST_CHUNK_BYTES", str(384 << 20)))
 
 
+# device slots (q, k, v and output buffers of one chunk) and compute streams of the host path
+_HOST_SLOTS = 4
+_HOST_COMPUTE_STREAMS = 3
+_HOST_STREAMS: dict = {}
+
+
+def _host_streams(dev: torch.device):
+    """The host path's streams on `dev` (host->device copies, device->host
+    copies, compute), made once per device.  Fresh streams on every call would
+    come from torch's rotating stream pool, and the caching allocator keeps the
+    blocks freed on one stream for that stream alone: every call would then
+    allocate its workspaces anew (and, once device memory fills, release the
+    cache with a device-wide synchronisation)."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    got = _HOST_STREAMS.get(idx)
+    if got is None:
+        got = (torch.cuda.Stream(dev), torch.cuda.Stream(dev),
+               [torch.cuda.Stream(dev) for _ in range(_HOST_COMPUTE_STREAMS)])
+        _HOST_STREAMS[idx] = got
+    return got
+
+
 def _chunk_plan(bh: int, base: int) -> list:
     """Sequences per chunk of the host path: full chunks of `base` while more
     than two are left, then chunks of half the rest (at least base / 8), so that
@@ -256,10 +278,13 @@ def _run_host(q3: Tensor, k3: Tensor, v3: Tensor, *, batch: int, heads: int, deg
     chunk i's host->device copy, its kernels and its device->host copy run on
     separate streams, so the copies of one chunk overlap the kernels of its
     neighbours and the two copy directions overlap each other; chunks take
-    turns over three device slots and alternate between two compute streams,
-    which lets one chunk's last wave of CTAs share the GPU with the next
-    chunk's first.  Pinned inputs give asynchronous copies; the output is a
-    pinned CPU tensor."""
+    turns over four device slots and three compute streams, which lets the
+    short tail chunks (whose moment scans are latency-bound: one CTA scans a
+    whole sequence) run side by side with the chunk before them.  The streams
+    are the device's own persistent set (_host_streams), so the caching
+    allocator reuses the kernels' workspaces from one call to the next.
+    Pinned inputs give asynchronous copies; the output is a pinned CPU
+    tensor."""
     bh, n, d = q3.shape
     dv = v3.shape[-1]
     dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -275,11 +300,10 @@ def _run_host(q3: Tensor, k3: Tensor, v3: Tensor, *, batch: int, heads: int, deg
         s0 += c
     with torch.cuda.device(dev):
         main = torch.cuda.current_stream(dev)
-        h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-        comp = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+        h2d, d2h, comp = _host_streams(dev)
         for s_ in (h2d, d2h, *comp):
             s_.wait_stream(main)
-        nslot = min(3, len(bounds))
+        nslot = min(_HOST_SLOTS, len(bounds))
         dq = [torch.empty(chunk, n, d, device=dev) for _ in range(nslot)]
         dk = [torch.empty(chunk, n, d, device=dev) for _ in range(nslot)]
         dvv = [torch.empty(chunk, n, dv, device=dev) for _ in range(nslot)]
@@ -296,7 +320,7 @@ def _run_host(q3: Tensor, k3: Tensor, v3: Tensor, *, batch: int, heads: int, deg
                 dk[slot][:cnt].copy_(k3[s0:s1], non_blocking=True)
                 dvv[slot][:cnt].copy_(v3[s0:s1], non_blocking=True)
                 in_ready[slot].record(h2d)
-            cs = comp[i % 2]
+            cs = comp[i % len(comp)]
             cs.wait_event(in_ready[slot])
             if i >= nslot:   # and its output once chunk i - nslot has been copied back
                 cs.wait_event(copied_out[slot])
