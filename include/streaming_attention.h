@@ -124,7 +124,12 @@ int sa_fast_attention_workspace_size(int64_t bh, int64_t n, int d, int dv, int d
 /* The whole forward of fast_article_causal_attention for bh sequences.
  * rep_idx (nullable) receives the coreset selection [bh, nc*m].  workspace is
  * caller-owned device memory of at least sa_fast_attention_workspace_size
- * bytes, 256-byte aligned. */
+ * bytes, 256-byte aligned.  The call is ordered on `stream` like one kernel:
+ * with a compressor and the tensor-core kernels, its moment scan runs on a
+ * second stream of the device's highest priority (made, with two events, at
+ * the first such call per host thread and caller stream) that forks from and
+ * joins back into `stream`; under graph capture, or while stage events are
+ * set, everything runs on `stream` itself. */
 int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d,
                       int dv, int degree, int block_size, float scale, int compressor,
                       const float* dirs, const float* coins, const int32_t* perms, float eps,
@@ -153,7 +158,8 @@ int sa_set_wait_limit_ns(uint64_t limit_ns);
  * sa_fast_attention records events[i] (cudaEvent_t handles, created by the
  * caller) on its stream at stage boundaries: 0 start, 1 after the k / v
  * operand splits, 2 after the compressor (and the split of its reps), 3 after
- * the moment scan, 4 after the residual (the end).  count = 0 turns it off. */
+ * the moment scan, 4 after the residual (the end); the stages then run one
+ * after another on that stream.  count = 0 turns it off. */
 int sa_set_stage_events(void* const* events, int count);
 
 /* ---- streaming (decode) state: ArticleStreamingAttention -------------------

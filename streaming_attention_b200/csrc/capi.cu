@@ -417,6 +417,198 @@ int reset_status(int* status, cudaStream_t s) {
 
 using namespace sa;
 
+namespace sa {
+namespace {
+
+// The moment scan's own stream for one caller stream (per host thread and
+// device), and the two events that fork the forward onto it and join it back.
+struct ForkStreams {
+  cudaStream_t caller;
+  int device;
+  cudaStream_t moments;
+  cudaEvent_t fork, join;
+};
+constexpr int kMaxForks = 16;
+thread_local ForkStreams g_forks[kMaxForks];
+thread_local int g_nforks = 0;
+
+// The fork record of caller stream s on the current device, made at its first
+// use (a stream of the device's highest priority and two events); nullptr when
+// the stream is being captured into a graph, when this thread already has
+// kMaxForks records, or when making one fails -- the forward then runs in
+// order on s.
+ForkStreams* fork_for(cudaStream_t s) {
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  for (int i = 0; i < g_nforks; ++i)
+    if (g_forks[i].caller == s && g_forks[i].device == dev) return &g_forks[i];
+  if (g_nforks == kMaxForks) return nullptr;
+  int least = 0, greatest = 0;
+  ForkStreams f{s, dev, nullptr, nullptr, nullptr};
+  bool ok = cudaDeviceGetStreamPriorityRange(&least, &greatest) == cudaSuccess &&
+            cudaStreamCreateWithPriority(&f.moments, cudaStreamNonBlocking, greatest) == cudaSuccess &&
+            cudaEventCreateWithFlags(&f.fork, cudaEventDisableTiming) == cudaSuccess &&
+            cudaEventCreateWithFlags(&f.join, cudaEventDisableTiming) == cudaSuccess;
+  if (!ok) {
+    cudaGetLastError();
+    if (f.join) cudaEventDestroy(f.join);
+    if (f.fork) cudaEventDestroy(f.fork);
+    if (f.moments) cudaStreamDestroy(f.moments);
+    return nullptr;
+  }
+  g_forks[g_nforks] = f;
+  return &g_forks[g_nforks++];
+}
+
+}  // namespace
+
+// One forward of the fast path (sa_fast_attention).  In order on the caller's
+// stream: the k and v splits, the compressor and the split of its rep values,
+// the moment scan, the residual.  With `allow_fork` (and the tensor-core
+// kernels, a compressor, no stage events and no graph capture) the v split and
+// the moment scan run on a stream of the device's highest priority while the
+// caller's stream runs the k split, the compressor and the rep split, and the
+// residual waits for both: the moment scan holds one CTA per SM, so when it
+// leaves SMs idle (fewer than 148 CTAs in its last round) the compressor's
+// small CTAs run there, and the priority keeps them from delaying it.
+int fast_attention_run(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d, int dv,
+                       int degree, int block_size, float scale, int compressor, const float* dirs, const float* coins,
+                       const int32_t* perms, float eps, float* out, int32_t* rep_idx, void* workspace,
+                       size_t workspace_bytes, void* stream, bool allow_fork) {
+  int rc = check_common(q, k, v, bh, n, d, dv, degree, block_size);
+  if (rc) return rc;
+  rc = check_compressor(compressor);
+  if (rc) return rc;
+  if (bh == 0 || n == 0) return SA_OK;
+  if (!out) return set_error(SA_ERR_INVALID_ARG, "null output pointer");
+  const Workspace w = plan(bh, n, d, dv, degree, block_size, compressor, Plan::kFull);
+  rc = check_workspace(w, workspace, workspace_bytes);
+  if (rc) return rc;
+  char* ws = static_cast<char*>(workspace);
+  float* low = reinterpret_cast<float*>(ws + w.low);
+  int* status = reinterpret_cast<int*>(ws + w.status);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t nc = (n - 1) / block_size;
+  const bool compress = compressor != SA_COMPRESSOR_NONE && nc > 0;
+  int32_t* ridx = rep_idx ? rep_idx : reinterpret_cast<int32_t*>(ws + w.rep_idx);
+  rc = reset_status(status, s);
+  if (rc) return rc;
+  stage_mark(0, s);
+
+  // operand splits shared by the tensor-core kernels
+  float* khi = reinterpret_cast<float*>(ws + w.khi);
+  float* klo = reinterpret_cast<float*>(ws + w.klo);
+  float* vthi = reinterpret_cast<float*>(ws + w.vthi);
+  float* vtlo = reinterpret_cast<float*>(ws + w.vtlo);
+  const int groups = w.groups > 0 ? w.groups : 1;
+
+  auto split_v = [&](cudaStream_t st) -> int {
+    if (w.tc || w.groups > 0) return launch_split_t(v, bh, n, dv, w.dvp, w.n_pad, vthi, vtlo, st);
+    return SA_OK;
+  };
+  auto moments = [&](cudaStream_t st) -> int {
+    if (w.groups > 0)
+      return moments_tc_from_split(w, ws, vthi, vtlo, q, k, low, status, bh, n, d, dv, degree, block_size, scale, st);
+    return launch_low_moments(q, k, v, bh, n, d, dv, degree, block_size, scale, low, st);
+  };
+
+  // C1: compressor (and the split of its rep values)
+  const float* rk = k;
+  const float* rv = v;
+  float* rw = nullptr;
+  const TCOperands cur_ops{khi, klo, n, vthi, vtlo, n, w.n_pad};
+  TCOperands rep_ops = cur_ops;
+  auto compress_reps = [&](cudaStream_t st) -> int {
+    if (!compress) return SA_OK;
+    if (w.tc) {
+      SplitOut sp;
+      sp.khi = reinterpret_cast<float*>(ws + w.rkhi);
+      sp.klo = reinterpret_cast<float*>(ws + w.rklo);
+      sp.dp = w.dp;
+      sp.w_stride = w.r_pad;
+      rw = reinterpret_cast<float*>(ws + w.rep_w);
+      float* rep_v = reinterpret_cast<float*>(ws + w.rep_v);
+      const cudaError_t ce = cudaMemsetAsync(rw, 0, (size_t)bh * w.r_pad * sizeof(float), st);
+      if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "rep weight reset: %s", cudaGetErrorString(ce));
+      int r = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, ridx, nullptr, rep_v,
+                              rw, sp, st);
+      if (r) return r;
+      float* rvthi = reinterpret_cast<float*>(ws + w.rvthi);
+      float* rvtlo = reinterpret_cast<float*>(ws + w.rvtlo);
+      r = launch_split_t(rep_v, bh, w.R, dv, w.dvp, w.r_pad, rvthi, rvtlo, st);
+      if (r) return r;
+      rep_ops = TCOperands{sp.khi, sp.klo, w.R, rvthi, rvtlo, w.R, w.r_pad};
+      return SA_OK;
+    }
+    float* rep_k = reinterpret_cast<float*>(ws + w.rep_k);
+    float* rep_v = reinterpret_cast<float*>(ws + w.rep_v);
+    rw = reinterpret_cast<float*>(ws + w.rep_w);
+    const int r = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, ridx, rep_k, rep_v,
+                                  rw, SplitOut{}, st);
+    if (r) return r;
+    rk = rep_k;
+    rv = rep_v;
+    return SA_OK;
+  };
+
+  ForkStreams* f = nullptr;
+  if (allow_fork && w.tc && w.groups > 0 && compress && g_stage_count == 0) f = fork_for(s);
+  if (f) {
+    cudaError_t ce = cudaEventRecord(f->fork, s);
+    if (ce == cudaSuccess) ce = cudaStreamWaitEvent(f->moments, f->fork, 0);
+    if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "fork of the moment scan: %s", cudaGetErrorString(ce));
+    // the moment scan's stream first, so that its CTAs are queued before the compressor's
+    rc = split_v(f->moments);
+    if (!rc) rc = moments(f->moments);
+    int rc2 = launch_split(k, bh * n, d, w.dp, khi, klo, s);
+    if (!rc2) rc2 = compress_reps(s);
+    // join even after a failed launch: nothing of this call may outlive it on the side stream
+    ce = cudaEventRecord(f->join, f->moments);
+    if (ce == cudaSuccess) ce = cudaStreamWaitEvent(s, f->join, 0);
+    if (rc) return rc;
+    if (rc2) return rc2;
+    if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "join of the moment scan: %s", cudaGetErrorString(ce));
+  } else {
+    if (w.tc) {
+      rc = launch_split(k, bh * n, d, w.dp, khi, klo, s);
+      if (rc) return rc;
+    }
+    rc = split_v(s);
+    if (rc) return rc;
+    stage_mark(1, s);
+    rc = compress_reps(s);
+    if (rc) return rc;
+    stage_mark(2, s);
+    rc = moments(s);
+    if (rc) return rc;
+    stage_mark(3, s);
+  }
+
+  // R: residual + combine
+  if (w.tc) {
+    rc = residual_tc_from_split(w, rep_ops, cur_ops, rw, q, low, groups, out, status, bh, n, d, dv, degree,
+                                block_size, reps_per_block(compressor, block_size), scale, eps, s);
+  } else {
+    if (groups > 1)  // the CUDA-core residual reads one summed slice
+      rc = launch_sum_groups(low, groups, bh * n * (dv + 1), low, s);
+    if (!rc)
+      rc = launch_residual(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, block_size, compressor, scale, eps, out,
+                           s);
+  }
+  if (!rc) stage_mark(4, s);
+  return rc;
+}
+
+}  // namespace sa
+
 extern "C" {
 
 int sa_version(void) { return 110; }
@@ -597,102 +789,8 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
                       int block_size, float scale, int compressor, const float* dirs, const float* coins,
                       const int32_t* perms, float eps, float* out, int32_t* rep_idx, void* workspace,
                       size_t workspace_bytes, void* stream) {
-  int rc = check_common(q, k, v, bh, n, d, dv, degree, block_size);
-  if (rc) return rc;
-  rc = check_compressor(compressor);
-  if (rc) return rc;
-  if (bh == 0 || n == 0) return SA_OK;
-  if (!out) return set_error(SA_ERR_INVALID_ARG, "null output pointer");
-  const Workspace w = plan(bh, n, d, dv, degree, block_size, compressor, Plan::kFull);
-  rc = check_workspace(w, workspace, workspace_bytes);
-  if (rc) return rc;
-  char* ws = static_cast<char*>(workspace);
-  float* low = reinterpret_cast<float*>(ws + w.low);
-  int* status = reinterpret_cast<int*>(ws + w.status);
-  cudaStream_t s = (cudaStream_t)stream;
-  const int64_t nc = (n - 1) / block_size;
-  const bool compress = compressor != SA_COMPRESSOR_NONE && nc > 0;
-  int32_t* ridx = rep_idx ? rep_idx : reinterpret_cast<int32_t*>(ws + w.rep_idx);
-  rc = reset_status(status, s);
-  if (rc) return rc;
-  stage_mark(0, s);
-
-  // operand splits shared by the tensor-core kernels
-  float* khi = reinterpret_cast<float*>(ws + w.khi);
-  float* klo = reinterpret_cast<float*>(ws + w.klo);
-  float* vthi = reinterpret_cast<float*>(ws + w.vthi);
-  float* vtlo = reinterpret_cast<float*>(ws + w.vtlo);
-  if (w.tc) {
-    rc = launch_split(k, bh * n, d, w.dp, khi, klo, s);
-    if (rc) return rc;
-  }
-  if (w.tc || w.groups > 0) {
-    rc = launch_split_t(v, bh, n, dv, w.dvp, w.n_pad, vthi, vtlo, s);
-    if (rc) return rc;
-  }
-  stage_mark(1, s);
-
-  // C1: compressor
-  const float* rk = k;
-  const float* rv = v;
-  float* rw = nullptr;
-  const TCOperands cur_ops{khi, klo, n, vthi, vtlo, n, w.n_pad};
-  TCOperands rep_ops = cur_ops;
-  if (compress) {
-    if (w.tc) {
-      SplitOut sp;
-      sp.khi = reinterpret_cast<float*>(ws + w.rkhi);
-      sp.klo = reinterpret_cast<float*>(ws + w.rklo);
-      sp.dp = w.dp;
-      sp.w_stride = w.r_pad;
-      rw = reinterpret_cast<float*>(ws + w.rep_w);
-      float* rep_v = reinterpret_cast<float*>(ws + w.rep_v);
-      const cudaError_t ce = cudaMemsetAsync(rw, 0, (size_t)bh * w.r_pad * sizeof(float), s);
-      if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "rep weight reset: %s", cudaGetErrorString(ce));
-      rc = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, ridx, nullptr, rep_v, rw,
-                           sp, s);
-      if (rc) return rc;
-      float* rvthi = reinterpret_cast<float*>(ws + w.rvthi);
-      float* rvtlo = reinterpret_cast<float*>(ws + w.rvtlo);
-      rc = launch_split_t(rep_v, bh, w.R, dv, w.dvp, w.r_pad, rvthi, rvtlo, s);
-      if (rc) return rc;
-      rep_ops = TCOperands{sp.khi, sp.klo, w.R, rvthi, rvtlo, w.R, w.r_pad};
-    } else {
-      float* rep_k = reinterpret_cast<float*>(ws + w.rep_k);
-      float* rep_v = reinterpret_cast<float*>(ws + w.rep_v);
-      rw = reinterpret_cast<float*>(ws + w.rep_w);
-      rc = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, ridx, rep_k, rep_v, rw,
-                           SplitOut{}, s);
-      if (rc) return rc;
-      rk = rep_k;
-      rv = rep_v;
-    }
-  }
-
-  stage_mark(2, s);
-
-  // M: low-degree moments
-  if (w.groups > 0)
-    rc = moments_tc_from_split(w, ws, vthi, vtlo, q, k, low, status, bh, n, d, dv, degree, block_size, scale, s);
-  else
-    rc = launch_low_moments(q, k, v, bh, n, d, dv, degree, block_size, scale, low, s);
-  if (rc) return rc;
-  const int groups = w.groups > 0 ? w.groups : 1;
-  stage_mark(3, s);
-
-  // R: residual + combine
-  if (w.tc) {
-    rc = residual_tc_from_split(w, rep_ops, cur_ops, rw, q, low, groups, out, status, bh, n, d, dv, degree,
-                                block_size, reps_per_block(compressor, block_size), scale, eps, s);
-  } else {
-    if (groups > 1)  // the CUDA-core residual reads one summed slice
-      rc = launch_sum_groups(low, groups, bh * n * (dv + 1), low, s);
-    if (!rc)
-      rc = launch_residual(q, k, v, rk, rv, rw, low, bh, n, d, dv, degree, block_size, compressor, scale, eps, out,
-                           s);
-  }
-  if (!rc) stage_mark(4, s);
-  return rc;
+  return sa::fast_attention_run(q, k, v, bh, n, d, dv, degree, block_size, scale, compressor, dirs, coins, perms, eps,
+                                out, rep_idx, workspace, workspace_bytes, stream, true);
 }
 
 

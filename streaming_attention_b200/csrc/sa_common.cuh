@@ -19,6 +19,13 @@ int check_launch(const char* what);
 // (sa_set_wait_limit_ns; 2 s unless set).
 uint64_t wait_limit_ns();
 
+// sa_fast_attention; `allow_fork` lets the moment scan run on a second stream
+// of its own (made at the first such call per host thread and caller stream).
+int fast_attention_run(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d, int dv,
+                       int degree, int block_size, float scale, int compressor, const float* dirs, const float* coins,
+                       const int32_t* perms, float eps, float* out, int32_t* rep_idx, void* workspace,
+                       size_t workspace_bytes, void* stream, bool allow_fork);
+
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // Feature count sum_{l<=t} C(d+l-1, l) for t <= 3.

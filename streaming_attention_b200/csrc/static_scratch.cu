@@ -60,11 +60,12 @@ extern "C" int sa_fast_attention_static_scratch(const float* q, const float* k, 
                          "use sa_fast_attention with a caller workspace",
                          need, (size_t)SA_STATIC_SCRATCH_BYTES);
   if (bh == 0 || n == 0)
-    return sa_fast_attention(q, k, v, bh, n, d, dv, degree, block_size, scale, compressor, dirs, coins, perms, eps,
-                             out, rep_idx, nullptr, 0, stream);
+    return sa::fast_attention_run(q, k, v, bh, n, d, dv, degree, block_size, scale, compressor, dirs, coins, perms,
+                                  eps, out, rep_idx, nullptr, 0, stream, false);
   void* ws = nullptr;
   rc = static_scratch_address(&ws);
   if (rc) return rc;
-  return sa_fast_attention(q, k, v, bh, n, d, dv, degree, block_size, scale, compressor, dirs, coins, perms, eps, out,
-                           rep_idx, ws, (size_t)SA_STATIC_SCRATCH_BYTES, stream);
+  // in order on the caller's stream: no second stream is made on this path
+  return sa::fast_attention_run(q, k, v, bh, n, d, dv, degree, block_size, scale, compressor, dirs, coins, perms, eps,
+                                out, rep_idx, ws, (size_t)SA_STATIC_SCRATCH_BYTES, stream, false);
 }
