@@ -53,6 +53,7 @@ extern "C" {
 #define SA_ERR_CUDA (-3)          /* CUDA launch or runtime error; RuntimeError */
 #define SA_ERR_TIMEOUT (-4)       /* a bounded device-side wait gave up */
 #define SA_ERR_WORKSPACE (-5)     /* workspace smaller than sa_*_workspace_size */
+#define SA_ERR_DEVICE_CHECK (-6)  /* a device-side index check failed (libsa_b200_checks.so only) */
 
 /* compressor kinds (fast_article_attention.py:326, :332, :383) */
 #define SA_COMPRESSOR_NONE 0
@@ -145,8 +146,14 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
  * the shard calls keep in the first 4 bytes of their workspace: synchronises
  * `stream`, then returns SA_OK when no bounded device-side wait of the last
  * call on that workspace gave up, else SA_ERR_TIMEOUT (sa_last_error() names
- * the kernel's wait code). */
+ * the kernel's wait code), or SA_ERR_DEVICE_CHECK in a checks build. */
 int sa_workspace_status(const void* workspace, void* stream);
+
+/* 1 in libsa_b200_checks.so, the build with device-side index checks
+ * (-DSA_DEVICE_CHECKS: a check that fails records its code, 900..999, in the
+ * status word and the offending index 8 bytes after it, and skips the access;
+ * sa_workspace_status then returns SA_ERR_DEVICE_CHECK), 0 in libsa_b200.so. */
+int sa_device_checks_enabled(void);
 
 /* How long one bounded device-side wait of the tensor-core kernels may take
  * before its CTA gives up, drains what it issued, records SA_ERR_TIMEOUT's

@@ -11,7 +11,9 @@ import os
 import threading
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_PKG, "libsa_b200.so")
+# SA_DEVICE_CHECKS=1 loads the build with device-side index checks instead
+CHECKS = os.environ.get("SA_DEVICE_CHECKS", "0") == "1"
+LIB_PATH = os.path.join(_PKG, "libsa_b200_checks.so" if CHECKS else "libsa_b200.so")
 
 SA_OK = 0
 SA_ERR_INVALID_ARG = -1
@@ -19,6 +21,7 @@ SA_ERR_UNSUPPORTED = -2
 SA_ERR_CUDA = -3
 SA_ERR_TIMEOUT = -4
 SA_ERR_WORKSPACE = -5
+SA_ERR_DEVICE_CHECK = -6
 
 COMPRESSORS = {"none": 0, "sorted_pair": 1, "random": 2}
 # storage dtype of the segment-mean reps (SA_REP_*)
@@ -35,6 +38,7 @@ _sz = ctypes.c_size_t
 SIGNATURES = {
     "sa_version": [],
     "sa_workspace_status": [_vp, _vp],
+    "sa_device_checks_enabled": [],
     "sa_set_wait_limit_ns": [ctypes.c_uint64],
     "sa_set_stage_events": [ctypes.POINTER(_vp), _i32],
     "sa_feature_count": [_i32, _i32, ctypes.POINTER(_i64)],

@@ -7,6 +7,11 @@ tree; objects go to ``_build/`` at the repository root.  Rebuilds only when the
 sources, headers or flags differ from those the library was built from (a
 content hash kept beside it, so that a copied tree with new file times does
 not rebuild).
+
+``build(checks=True)`` makes libsa_b200_checks.so, the same sources with
+``-DSA_DEVICE_CHECKS``: device-side index checks that record a failure in the
+launch status word and skip the access (the stand-in for a memory checker;
+``SA_DEVICE_CHECKS=1`` in the environment makes the package load it).
 """
 
 from __future__ import annotations
@@ -23,7 +28,9 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libsa_b200.so")
 STAMP = LIB + ".stamp"
+LIB_CHECKS = os.path.join(PKG, "libsa_b200_checks.so")
 BUILD_DIR = os.path.join(ROOT, "_build")
+CHECKS_FLAGS = ["-DSA_DEVICE_CHECKS"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -49,9 +56,9 @@ def headers():
     return sorted(glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(ROOT, "include", "*.h")))
 
 
-def source_hash() -> str:
+def source_hash(checks: bool = False) -> str:
     h = hashlib.sha256()
-    h.update(" ".join(NVCC_FLAGS).encode())
+    h.update(" ".join(NVCC_FLAGS + (CHECKS_FLAGS if checks else [])).encode())
     for p in sources() + headers() + [__file__]:
         h.update(os.path.relpath(p, ROOT).encode())
         with open(p, "rb") as f:
@@ -59,41 +66,48 @@ def source_hash() -> str:
     return h.hexdigest()
 
 
-def needs_build() -> bool:
-    if not os.path.exists(LIB) or not os.path.exists(STAMP):
+def needs_build(checks: bool = False) -> bool:
+    lib = LIB_CHECKS if checks else LIB
+    stamp = lib + ".stamp"
+    if not os.path.exists(lib) or not os.path.exists(stamp):
         return True
-    with open(STAMP) as f:
-        return f.read().strip() != source_hash()
+    with open(stamp) as f:
+        return f.read().strip() != source_hash(checks)
 
 
-def build(force: bool = False, verbose: bool = False, jobs: int = 8) -> str:
-    """Compile every csrc/*.cu for sm_100a and link libsa_b200.so."""
-    if not force and not needs_build():
-        return LIB
+def build(force: bool = False, verbose: bool = False, jobs: int = 8, checks: bool = False) -> str:
+    """Compile every csrc/*.cu for sm_100a and link libsa_b200.so (or, with
+    `checks`, libsa_b200_checks.so)."""
+    lib = LIB_CHECKS if checks else LIB
+    stamp = lib + ".stamp"
+    if not force and not needs_build(checks):
+        return lib
     nvcc = _nvcc()
-    os.makedirs(BUILD_DIR, exist_ok=True)
+    bdir = os.path.join(BUILD_DIR, "checks") if checks else BUILD_DIR
+    os.makedirs(bdir, exist_ok=True)
+    flags = NVCC_FLAGS + (CHECKS_FLAGS if checks else [])
     procs, objs = [], []
     for src in sources():
-        obj = os.path.join(BUILD_DIR, os.path.basename(src)[:-3] + ".o")
+        obj = os.path.join(bdir, os.path.basename(src)[:-3] + ".o")
         objs.append(obj)
-        cmd = [nvcc, *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-c", src, "-o", obj]
+        cmd = [nvcc, *flags, "-I", os.path.join(ROOT, "include"), "-c", src, "-o", obj]
         if verbose:
             print(" ".join(cmd), flush=True)
         procs.append((cmd, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)))
         if len(procs) >= jobs:
             _drain(procs)
     _drain(procs)
-    tmp = LIB + ".tmp"
+    tmp = lib + ".tmp"
     cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp, *objs]
     if verbose:
         print(" ".join(cmd), flush=True)
     out = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
     if out.returncode != 0:
         raise RuntimeError("link failed:\n" + out.stdout)
-    os.replace(tmp, LIB)
-    with open(STAMP, "w") as f:
-        f.write(source_hash() + "\n")
-    return LIB
+    os.replace(tmp, lib)
+    with open(stamp, "w") as f:
+        f.write(source_hash(checks) + "\n")
+    return lib
 
 
 def _drain(procs):
@@ -111,3 +125,4 @@ def _drain(procs):
 
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv, checks=True))

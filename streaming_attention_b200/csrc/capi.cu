@@ -27,7 +27,7 @@ namespace sa {
 int launch_compress(const float* k, const float* v, int64_t bh, int64_t n, int d, int dv, int bs, int compressor,
                     const float* dirs, const float* coins, const int32_t* perms, int32_t* rep_idx, float* rep_k,
                     float* rep_v, float* rep_w, SplitOut sp, cudaStream_t stream,
-                    int64_t nc_force = -1, int64_t idx_offset = 0);
+                    int64_t nc_force = -1, int64_t idx_offset = 0, int* status = nullptr);
 int launch_split(const float* src, int64_t rows, int cols, int cols_pad, float* hi, float* lo, cudaStream_t stream);
 int launch_split_t(const float* src, int64_t bh, int64_t rows, int cols, int cols_pad, int64_t rows_pad, float* hi,
                    float* lo, cudaStream_t stream);
@@ -179,7 +179,7 @@ Workspace plan(int64_t bh, int64_t n, int d, int dv, int degree, int bs, int com
     return at;
   };
   const size_t f = sizeof(float);
-  w.status = take(sizeof(int));
+  w.status = take(16);   // status word, then the index of a failed device check
   if (what != Plan::kResidualOnly) w.low = take((size_t)(w.groups > 0 ? w.groups : 1) * bh * n * (dv + 1) * f);
   if (w.groups > 0) w.master = take((size_t)moments_tc_master_floats(bh, d, dv, degree) * f);
   const bool need_v_split = w.groups > 0 || (w.tc && what != Plan::kMomentsOnly);
@@ -324,7 +324,7 @@ Workspace plan_shard(int64_t bh, int64_t n, int d, int dv, int degree, int bs, i
     return at;
   };
   const size_t f = sizeof(float);
-  w.status = take(sizeof(int));
+  w.status = take(16);   // status word, then the index of a failed device check
   w.low = take((size_t)2 * (w.groups > 0 ? w.groups : 1) * bh * n * (dv + 1) * f);   // local + prefix slices
   w.master = take((size_t)moments_tc_master_floats(bh, d, dv, degree) * f);
   w.den_io = take((size_t)moments_tc_den_floats(bh, d, dv, degree) * f);
@@ -378,7 +378,7 @@ Workspace plan_flash(int64_t bh, int64_t n, int d, int dv) {
     return at;
   };
   const size_t f = sizeof(float);
-  w.status = take(sizeof(int));
+  w.status = take(16);   // status word, then the index of a failed device check
   w.khi = take((size_t)bh * n * w.dp * f);
   w.klo = take((size_t)bh * n * w.dp * f);
   w.vthi = take((size_t)bh * w.dvp * w.n_pad * f);
@@ -406,8 +406,10 @@ int check_workspace(const Workspace& w, const void* workspace, size_t workspace_
   return SA_OK;
 }
 
+// The status word and, 8 bytes further, the index a failed device check
+// recorded (checks builds): both cleared at the start of every call.
 int reset_status(int* status, cudaStream_t s) {
-  const cudaError_t ce = cudaMemsetAsync(status, 0, sizeof(int), s);
+  const cudaError_t ce = cudaMemsetAsync(status, 0, 16, s);
   if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "status reset: %s", cudaGetErrorString(ce));
   return SA_OK;
 }
@@ -539,7 +541,7 @@ int fast_attention_run(const float* q, const float* k, const float* v, int64_t b
       const cudaError_t ce = cudaMemsetAsync(rw, 0, (size_t)bh * w.r_pad * sizeof(float), st);
       if (ce != cudaSuccess) return set_error(SA_ERR_CUDA, "rep weight reset: %s", cudaGetErrorString(ce));
       int r = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, ridx, nullptr, rep_v,
-                              rw, sp, st);
+                              rw, sp, st, -1, 0, status);
       if (r) return r;
       float* rvthi = reinterpret_cast<float*>(ws + w.rvthi);
       float* rvtlo = reinterpret_cast<float*>(ws + w.rvtlo);
@@ -552,7 +554,7 @@ int fast_attention_run(const float* q, const float* k, const float* v, int64_t b
     float* rep_v = reinterpret_cast<float*>(ws + w.rep_v);
     rw = reinterpret_cast<float*>(ws + w.rep_w);
     const int r = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, ridx, rep_k, rep_v,
-                                  rw, SplitOut{}, st);
+                                  rw, SplitOut{}, st, -1, 0, status);
     if (r) return r;
     rk = rep_k;
     rv = rep_v;
@@ -615,12 +617,24 @@ int sa_version(void) { return 110; }
 
 int sa_workspace_status(const void* workspace, void* stream) {
   if (!workspace) return set_error(SA_ERR_INVALID_ARG, "null workspace");
-  int code = 0;
-  cudaError_t e = cudaMemcpyAsync(&code, workspace, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+  int64_t word[2] = {0, 0};   // status word (low 4 bytes of word[0]), then a failed check's index
+  cudaError_t e = cudaMemcpyAsync(word, workspace, sizeof(word), cudaMemcpyDeviceToHost, (cudaStream_t)stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
   if (e != cudaSuccess) return set_error(SA_ERR_CUDA, "status read: %s", cudaGetErrorString(e));
+  int code = 0;
+  memcpy(&code, word, sizeof(int));
+  if (code >= kCheckFirst && code <= kCheckLast)
+    return set_error(SA_ERR_DEVICE_CHECK, "device check %d failed at index %lld", code, (long long)word[1]);
   if (code != 0) return set_error(SA_ERR_TIMEOUT, "a bounded device-side wait gave up (wait code %d)", code);
   return SA_OK;
+}
+
+int sa_device_checks_enabled(void) {
+#ifdef SA_DEVICE_CHECKS
+  return 1;
+#else
+  return 0;
+#endif
 }
 
 int sa_set_wait_limit_ns(uint64_t limit_ns) {
@@ -852,7 +866,7 @@ int sa_shard_begin(const float* q, const float* k, const float* v, int64_t bh, i
   if (!rc) rc = launch_split_t(v, bh, n, dv, w.dvp, w.n_pad, vthi, vtlo, s);
   if (!rc && compress)
     rc = launch_compress(k, v, bh, n, d, dv, block_size, compressor, dirs, coins, perms, rep_idx, rep_k, rep_v, rep_w,
-                         SplitOut{}, s, n_compress, c_off * (int64_t)block_size);
+                         SplitOut{}, s, n_compress, c_off * (int64_t)block_size, status);
   float* master = reinterpret_cast<float*>(ws + w.master);
   float* den_io = reinterpret_cast<float*>(ws + w.den_io);
   if (!rc)

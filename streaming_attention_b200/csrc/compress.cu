@@ -39,7 +39,7 @@ compress_blocks_kernel(const float* __restrict__ k, const float* __restrict__ v,
                        int bs, int nc, int m, int pow2, int use_perm, const float* __restrict__ dirs,
                        const float* __restrict__ coins, const int32_t* __restrict__ perms,
                        int32_t* __restrict__ rep_idx, float* __restrict__ rep_k, float* __restrict__ rep_v,
-                       float* __restrict__ rep_w, const SplitOut sp, int64_t idx_offset) {
+                       float* __restrict__ rep_w, const SplitOut sp, int64_t idx_offset, int* status) {
   extern __shared__ unsigned char smem_raw[];
   unsigned long long* skey = reinterpret_cast<unsigned long long*>(smem_raw);
   int* sidx = reinterpret_cast<int*>(skey + pow2);
@@ -113,15 +113,18 @@ compress_blocks_kernel(const float* __restrict__ k, const float* __restrict__ v,
   }
   __syncthreads();
 
-  // write the selection and gather the rep rows (one warp per rep)
+  // write the selection and gather the rep rows (one warp per rep); a
+  // selected key lies in the block (perms come from a host table)
   const int64_t rbase = h * (int64_t)nc * m + (int64_t)c * m;
   const int64_t wbase = h * sp.w_stride + (int64_t)c * m;
   for (int p = tid; p < m; p += blockDim.x) {
+    if (!SA_DEVICE_CHECK(sel[p] >= 0 && sel[p] < bs, status, 901, blk * m + p)) continue;
     if (rep_idx) rep_idx[rbase + p] = (int32_t)(idx_offset + start + sel[p]);
     if (rep_w) rep_w[wbase + p] = selw[p];
   }
   const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   for (int p = warp; p < m; p += nwarps) {
+    if (!SA_DEVICE_CHECK(sel[p] >= 0 && sel[p] < bs, status, 901, blk * m + p)) continue;
     const int64_t src = h * n + start + sel[p];
     if (rep_k)
       for (int a = lane; a < d; a += 32) rep_k[(rbase + p) * d + a] = __ldg(k + src * d + a);
@@ -203,7 +206,7 @@ __global__ void split_transpose_kernel(const float* __restrict__ src, int64_t ro
 int launch_compress(const float* k, const float* v, int64_t bh, int64_t n, int d, int dv, int bs, int compressor,
                     const float* dirs, const float* coins, const int32_t* perms, int32_t* rep_idx, float* rep_k,
                     float* rep_v, float* rep_w, SplitOut sp, cudaStream_t stream, int64_t nc_force,
-                    int64_t idx_offset) {
+                    int64_t idx_offset, int* status) {
   // blocks to compress: the completed ones ((n - 1) / bs), or nc_force >= 0 blocks
   // (a shard of a longer sequence whose last block is completed by later tokens)
   const int64_t nc = nc_force >= 0 ? nc_force : (n > 0 ? (n - 1) / bs : 0);
@@ -225,7 +228,7 @@ int launch_compress(const float* k, const float* v, int64_t bh, int64_t n, int d
   dim3 grid((unsigned)nc, (unsigned)bh);
   compress_blocks_kernel<<<grid, kCompressThreads, smem, stream>>>(k, v, n, d, dv, bs, (int)nc, m, pow2,
                                                                    use_perm ? 1 : 0, dirs, coins, perms, rep_idx,
-                                                                   rep_k, rep_v, rep_w, sp, idx_offset);
+                                                                   rep_k, rep_v, rep_w, sp, idx_offset, status);
   return check_launch("compress_blocks_kernel");
 }
 

@@ -45,7 +45,7 @@ constexpr int kThreads = 320;
 constexpr float kRescale = 12.0f;   // base-2 units: p <= 4096
 constexpr int kFold = 16;           // key tiles per TMEM accumulation chain
 
-constexpr int kErrWaitQ = 301, kErrWaitFull = 302, kErrWaitSfree = 303, kErrWaitP = 304, kErrWaitS = 305,
+constexpr int kErrWaitQ = 301, kErrWaitFull = 302, kErrWaitP = 304, kErrWaitS = 305,
               kErrWaitEmpty = 306, kErrWaitO = 307, kErrDrain = 308, kErrWaitPV = 309;
 
 // 2^x with the SFU's ex2 (relative error about 2^-22; 2^-inf = 0).

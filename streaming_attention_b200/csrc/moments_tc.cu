@@ -257,6 +257,11 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
   for (int s = threadIdx.x; s < FT * 16; s += kThreads) {
     int p1, p2, c0;
     seg_of(seg0 + s, p.d, p.degree, p1, p2, c0);
+    // every entry indexes the extended row x~ of DX floats (8 of them from c0)
+    if (!SA_DEVICE_CHECK(p1 >= 0 && p1 < DX && p2 >= 0 && p2 < DX && c0 >= 0 && c0 + 8 <= DX, p.status, 911,
+                         seg0 + s)) {
+      p1 = p2 = c0 = 0;
+    }
     segtab[s] = (uint32_t)p1 | ((uint32_t)p2 << 10) | ((uint32_t)c0 << 20);
   }
   __syncthreads();
@@ -451,6 +456,8 @@ moments_tc_kernel(const __grid_constant__ CUtensorMap tm_vh, const __grid_consta
     int64_t out_i0 = 0;
     int out_rows = 0;
     auto copy_out = [&]() {
+      if (out_rows > 0 && !SA_DEVICE_CHECK(out_i0 >= 0 && out_i0 + out_rows <= p.n, p.status, 912, out_i0))
+        out_rows = 0;
       if (out_rows > 0) {
         const int total = out_rows * (int)col_stride;
         float* dst = part_h + out_i0 * col_stride;

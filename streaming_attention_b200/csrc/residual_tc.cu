@@ -55,7 +55,7 @@ constexpr int kQueryThreads = 32 * kQueryWarps;
 constexpr int kThreads = 64 + kQueryThreads;   // warp 0 TMA, warp 1 MMA, warps 2.. query rows
 
 // status codes written to the launch's status word
-constexpr int kErrWaitQ = 101, kErrWaitFull = 102, kErrWaitSfree = 103, kErrWaitP = 104, kErrWaitS = 105,
+constexpr int kErrWaitQ = 101, kErrWaitFull = 102, kErrWaitP = 104, kErrWaitS = 105,
               kErrWaitEmpty = 106, kErrWaitO = 107, kErrDrain = 108;
 
 struct ResTCParams {
@@ -289,7 +289,9 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
           tma_load_3d(vd, mvh, &full[s], row0 + a * 32, 0, (int)h);
           tma_load_3d(vd + DVP * 128, mvl, &full[s], row0 + a * 32, 0, (int)h);
         }
-        if (with_w) bulk_load(wbuf + s * kTile, p.rep_w + h * p.r_pad + row0, kTile * 4, &full[s]);
+        // (a bulk copy has no bounds of its own: the weight rows must lie in the sequence's stride)
+        if (with_w && SA_DEVICE_CHECK(row0 >= 0 && row0 + kTile <= p.r_pad, p.status, 921, row0))
+          bulk_load(wbuf + s * kTile, p.rep_w + h * p.r_pad + row0, kTile * 4, &full[s]);
         ++issued;
       }
       // never leave with copies in flight: the last use of each stage must have landed
@@ -305,9 +307,11 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
       // once O is complete nothing reads the stages: bring in the epilogue's rows
       if (bulk_low && issued == T && mbar_wait(ofull, 0, ab, kErrWaitO)) {
         mbar_arrive_expect_tx(lowfull, (uint32_t)lbytes);
-        for (int gi = 0; gi < p.groups; ++gi)
-          bulk_load(reinterpret_cast<float*>(smem) + gi * lblk,
-                    p.low + (h * p.n + q0) * (int64_t)(p.dv + 1) + gi * p.group_stride, (uint32_t)(lblk * 4), lowfull);
+        for (int gi = 0; gi < p.groups; ++gi) {
+          const int64_t e0 = (h * p.n + q0) * (int64_t)(p.dv + 1) + gi * p.group_stride;
+          if (SA_DEVICE_CHECK(e0 >= 0 && e0 + lblk <= (gi + 1) * p.group_stride, p.status, 922, e0))
+            bulk_load(reinterpret_cast<float*>(smem) + gi * lblk, p.low + e0, (uint32_t)(lblk * 4), lowfull);
+        }
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(lowfull, 0)) {   // and never leave with them in flight
           if (globaltimer_ns() - t0 > 1000000000ull) {

@@ -28,6 +28,25 @@ int fast_attention_run(const float* q, const float* k, const float* v, int64_t b
 
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Device-side index checks, compiled in only with -DSA_DEVICE_CHECKS (the
+// libsa_b200_checks.so build).  SA_DEVICE_CHECK(cond, status, code, index) is
+// then false when `cond` fails, after recording `code` in the launch status
+// word (the first failure of a launch wins) and `index` in the 8 bytes at
+// status + 2; the caller skips the access it guards.  In the ordinary build it
+// is `true` and `cond` is not evaluated.  Codes 900..999 are checks; the
+// status word's other codes (101..309) are bounded waits that gave up.
+#ifdef SA_DEVICE_CHECKS
+__device__ __forceinline__ bool device_check_failed(int* status, int code, long long index) {
+  if (status && atomicCAS(status, 0, code) == 0) *reinterpret_cast<volatile long long*>(status + 2) = index;
+  return false;
+}
+#define SA_DEVICE_CHECK(cond, status, code, index) \
+  ((cond) ? true : ::sa::device_check_failed((status), (code), (long long)(index)))
+#else
+#define SA_DEVICE_CHECK(cond, status, code, index) true
+#endif
+constexpr int kCheckFirst = 900, kCheckLast = 999;
+
 // Feature count sum_{l<=t} C(d+l-1, l) for t <= 3.
 __host__ __device__ inline int64_t feature_count(int d, int t) {
   int64_t f = 1;
