@@ -149,6 +149,16 @@ int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh
  * the kernel's wait code), or SA_ERR_DEVICE_CHECK in a checks build. */
 int sa_workspace_status(const void* workspace, void* stream);
 
+/* Whether sa_fast_attention may fork its moment scan onto a second stream
+ * (see sa_fast_attention), for the calling host thread: 1 (the default) lets
+ * it, 0 runs every stage in order on the caller's stream.  Callers that
+ * already overlap several forwards on streams of their own (this library's
+ * host-tensor path does, for its chunks) gain nothing from the fork: a later
+ * forward's moment scan, at the higher priority, then delays the earlier
+ * forward's residual.  sa_moment_fork_enabled returns the current setting. */
+int sa_set_moment_fork(int enable);
+int sa_moment_fork_enabled(void);
+
 /* 1 in libsa_b200_checks.so, the build with device-side index checks
  * (-DSA_DEVICE_CHECKS: a check that fails records its code, 900..999, in the
  * status word and the offending index 8 bytes after it, and skips the access;

@@ -39,6 +39,8 @@ SIGNATURES = {
     "sa_version": [],
     "sa_workspace_status": [_vp, _vp],
     "sa_device_checks_enabled": [],
+    "sa_set_moment_fork": [_i32],
+    "sa_moment_fork_enabled": [],
     "sa_set_wait_limit_ns": [ctypes.c_uint64],
     "sa_set_stage_events": [ctypes.POINTER(_vp), _i32],
     "sa_feature_count": [_i32, _i32, ctypes.POINTER(_i64)],

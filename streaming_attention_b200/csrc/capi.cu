@@ -433,6 +433,8 @@ struct ForkStreams {
 constexpr int kMaxForks = 16;
 thread_local ForkStreams g_forks[kMaxForks];
 thread_local int g_nforks = 0;
+// sa_set_moment_fork, per host thread
+thread_local bool g_fork_enabled = true;
 
 // The fork record of caller stream s on the current device, made at its first
 // use (a stream of the device's highest priority and two events); nullptr when
@@ -562,7 +564,7 @@ int fast_attention_run(const float* q, const float* k, const float* v, int64_t b
   };
 
   ForkStreams* f = nullptr;
-  if (allow_fork && w.tc && w.groups > 0 && compress && g_stage_count == 0) f = fork_for(s);
+  if (allow_fork && g_fork_enabled && w.tc && w.groups > 0 && compress && g_stage_count == 0) f = fork_for(s);
   if (f) {
     cudaError_t ce = cudaEventRecord(f->fork, s);
     if (ce == cudaSuccess) ce = cudaStreamWaitEvent(f->moments, f->fork, 0);
@@ -628,6 +630,13 @@ int sa_workspace_status(const void* workspace, void* stream) {
   if (code != 0) return set_error(SA_ERR_TIMEOUT, "a bounded device-side wait gave up (wait code %d)", code);
   return SA_OK;
 }
+
+int sa_set_moment_fork(int enable) {
+  g_fork_enabled = enable != 0;
+  return SA_OK;
+}
+
+int sa_moment_fork_enabled(void) { return g_fork_enabled ? 1 : 0; }
 
 int sa_device_checks_enabled(void) {
 #ifdef SA_DEVICE_CHECKS

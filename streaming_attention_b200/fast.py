@@ -283,6 +283,10 @@ def _run_host(q3: Tensor, k3: Tensor, v3: Tensor, *, batch: int, heads: int, deg
     whole sequence) run side by side with the chunk before them.  The streams
     are the device's own persistent set (_host_streams), so the caching
     allocator reuses the kernels' workspaces from one call to the next.
+    The chunks' forwards run with the moment-scan fork off
+    (sa_set_moment_fork): overlapping chunks already fill the SMs a lone
+    moment scan leaves idle, and a later chunk's scan at the fork's higher
+    priority would delay the earlier chunk's residual and copy-back.
     Pinned inputs give asynchronous copies; the output is a pinned CPU
     tensor."""
     bh, n, d = q3.shape
@@ -298,6 +302,23 @@ def _run_host(q3: Tensor, k3: Tensor, v3: Tensor, *, batch: int, heads: int, deg
     for c in _chunk_plan(bh, chunk):
         bounds.append((s0, s0 + c))
         s0 += c
+    lib = _lib.load()
+    fork_was = lib.sa_moment_fork_enabled()
+    lib.sa_set_moment_fork(0)
+    try:
+        _stream_chunks(q3, k3, v3, out, bounds, chunk, batch=batch, heads=heads, degree=degree,
+                       block_size=block_size, scale=scale, compressor=compressor, seed=seed, eps=eps, g0=g0, dev=dev)
+    finally:
+        lib.sa_set_moment_fork(fork_was)
+    return out
+
+
+def _stream_chunks(q3: Tensor, k3: Tensor, v3: Tensor, out: Tensor, bounds: list, chunk: int, *, batch: int,
+                   heads: int, degree: int, block_size: int, scale: float, compressor: str, seed: int, eps: float,
+                   g0: int, dev: torch.device) -> None:
+    """The chunk loop of _run_host: copies in, kernels, copies out."""
+    bh, n, d = q3.shape
+    dv = v3.shape[-1]
     with torch.cuda.device(dev):
         main = torch.cuda.current_stream(dev)
         h2d, d2h, comp = _host_streams(dev)
@@ -336,7 +357,6 @@ def _run_host(q3: Tensor, k3: Tensor, v3: Tensor, *, batch: int, heads: int, deg
         d2h.synchronize()
         for s_ in (h2d, *comp):
             s_.synchronize()
-    return out
 
 
 def _host_inputs(*ts: Tensor) -> bool:

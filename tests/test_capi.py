@@ -107,3 +107,20 @@ def test_workspace_size_and_argument_errors_without_gpu():
         _lib.check(_lib.SA_ERR_UNSUPPORTED, "x")
     with pytest.raises(_lib.SAError):
         _lib.check(_lib.SA_ERR_TIMEOUT, "x")
+
+
+def test_moment_fork_switch_is_per_thread():
+    import threading
+    lib = _lib.load()
+    assert lib.sa_moment_fork_enabled() == 1
+    assert lib.sa_set_moment_fork(0) == _lib.SA_OK
+    try:
+        assert lib.sa_moment_fork_enabled() == 0
+        seen = []
+        t = threading.Thread(target=lambda: seen.append(lib.sa_moment_fork_enabled()))
+        t.start()
+        t.join()
+        assert seen == [1]   # another host thread keeps the default
+    finally:
+        lib.sa_set_moment_fork(1)
+    assert lib.sa_moment_fork_enabled() == 1
