@@ -26,15 +26,24 @@
 // row-major k split, V tiles from the transposed v split (an MN-major tf32
 // operand runs markedly slower on the tensor cores).
 //
-// Each 8-wide K step issues the three products as three MMAs into one
-// accumulator (a tf32 MMA's time grows with N, so this costs 3/4 of the two
-// doubled-width MMAs that would also form the unneeded lo*lo product; with 16
-// query-row warps the doubled form measured 4 % slower at config 3, 8 % at
-// config 4):
-//   S = Q_hi K_hi^T + Q_hi K_lo^T + Q_lo K_hi^T   (N = 64: each 32-column K chunk
-//       holds the 64 hi rows, then the 64 lo rows)
-//   O = P_hi V_hi + P_hi V_lo + P_lo V_hi          (N = dv: each 32-key chunk of the
-//       V^T tile holds the dv hi rows, then the dv lo rows)
+// Each 8-wide K step forms the three products hi*hi + hi*lo + lo*hi (not the
+// unneeded lo*lo: a tf32 MMA's time grows with N) in two MMAs, one of them
+// twice as wide:
+//   S' = Q_hi [K_hi ; K_lo]^T (N = 128: each 32-column K chunk holds the 64 hi
+//        rows, then the 64 lo rows) + Q_lo K_hi^T into its first 64 columns;
+//        S = S'[0, 64) + S'[64, 128), added by the query-row warps (for d <= 32,
+//        whose S is only four K steps, three MMAs of N = 64: there the extra
+//        TMEM load and adds of the query-row warps cost more than the issues
+//        saved -- config 4's residual measured 18.4 against 17.2 ms)
+//   O' = P_hi [V_hi | V_lo] (N = 2 dv: each 32-key chunk of the V^T tile holds
+//        the dv hi rows, then the dv lo rows) + P_lo V_hi into its first dv
+//        columns; O = O'[0, dv) + O'[dv, 2 dv), added in the epilogue
+//        (for dv > 64, where O' would not fit in TMEM, three MMAs of N = dv)
+// The tensor time is that of three MMAs of N = 64, but the MMA warp issues a
+// third fewer instructions: issuing was the limit of the three-MMA form
+// (~40 cycles per tcgen05.mma from a warp that shares its scheduler with four
+// query-row warps, ~1900 issue cycles per 64-key tile against 1536 of tensor
+// work, measured with clock64 stamps).
 #include <math.h>
 
 #include "sa_common.cuh"
@@ -88,9 +97,13 @@ struct Layout {
   static constexpr uint32_t kW = kStages * kTile * 4;
   // TMEM columns
   static constexpr uint32_t kQhi = 0, kQlo = DP;
-  static constexpr uint32_t kS0 = 2 * DP;           // buffer b: S/P_hi at kS0 + 128 b, P_lo at kS0 + 128 b + 64
+  static constexpr uint32_t kS0 = 2 * DP;           // buffer b: S (or S', 128 columns) at kS0 + 128 b, then
+                                                    // P_hi over its first 64 columns and P_lo over the other 64
   static constexpr uint32_t kO = 2 * DP + 256;
-  static_assert(kO + DVP <= 512, "TMEM columns");
+  static constexpr bool kStackK = DP == 64;                 // S' = [S_hh + S_lh | S_hl]
+  static constexpr bool kStackV = DVP <= 64;                // O' = [O_hh + O_lh | O_hl]
+  static constexpr uint32_t kOCols = kStackV ? 2 * DVP : DVP;
+  static_assert(kO + kOCols <= 512, "TMEM columns");
   static constexpr uint32_t kSmemBytes = kStages * kStage + kW + (2 * kStages + 11) * 8 + 64 + kQW * 128 * 4 + 1024;
 };
 
@@ -220,6 +233,29 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
                         ((reinterpret_cast<uintptr_t>(p.low) + (uintptr_t)((h * p.n + q0) * (int64_t)(p.dv + 1) * 4)) & 15) == 0 &&
                         lbytes16 + (uint64_t)kRowsQ * (DVP + 1) * 4 + (uint64_t)kRowsQ * 4 <= (uint64_t)kStages * L::kStage;
 
+  // Query-row threads start loading their piece of the query row now, so that
+  // the loads' latency overlaps the set-up below: 16-byte loads when the rows
+  // allow them (a warp's load then touches 32 rows once, not once per float).
+  float qv[16];
+  if (warp >= 2) {
+    const int u = (warp - 2) >> 2;                 // the column group's 16-column piece
+    const int64_t iq = q0 + (warp & 3) * 32 + lane;
+    const bool vq = iq < p.n && u < DP / 16;
+    const float* qr = p.q + (h * p.n + (vq ? iq : 0)) * p.d + u * 16;
+    if (vq && (p.d & 3) == 0 && u * 16 + 16 <= p.d && (reinterpret_cast<uintptr_t>(p.q) & 15) == 0) {
+#pragma unroll
+      for (int j4 = 0; j4 < 4; ++j4) {
+        const float4 x = __ldg(reinterpret_cast<const float4*>(qr) + j4);
+        qv[4 * j4 + 0] = x.x;
+        qv[4 * j4 + 1] = x.y;
+        qv[4 * j4 + 2] = x.z;
+        qv[4 * j4 + 3] = x.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) qv[j] = (vq && u * 16 + j < p.d) ? __ldg(qr + j) : 0.0f;
+    }
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -325,7 +361,9 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     // ------------------------------------------------------------ MMA issuer
     // the whole warp runs the loop; the elected lane issues MMAs and commits
     {
+      constexpr uint32_t idesc_qk2 = idesc_tf32(128, 2 * kTile, false, false);
       constexpr uint32_t idesc_qk = idesc_tf32(128, kTile, false, false);
+      constexpr uint32_t idesc_pv2 = idesc_tf32(128, 2 * DVP, false, false);
       constexpr uint32_t idesc_pv = idesc_tf32(128, DVP, false, false);
       bool ok = mbar_wait_warp(qready, 0, ab, kErrWaitQ);
       if (ok) tc_fence_after();
@@ -344,10 +382,16 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
           for (int kk = 0; kk < kTile / 8; ++kk) {
             // 8 keys of 32-key chunk kk / 4: rows = value columns (hi rows, then lo rows)
             const uint64_t bh_ = vd + (uint64_t)(((kk >> 2) * (2 * DVP * 128) + (kk & 3) * 32) >> 4);
-            const uint64_t bl_ = bh_ + (uint64_t)((DVP * 128) >> 4);
-            mma_tf32_ts(tmem + L::kO, ph + kk * 8, bh_, idesc_pv, (tp > 0 || kk > 0) ? 1u : 0u);
-            mma_tf32_ts(tmem + L::kO, ph + kk * 8, bl_, idesc_pv, 1u);
-            mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
+            if (L::kStackV) {
+              // [V_hi | V_lo] are the chunk's 2 dv rows from bh_ on
+              mma_tf32_ts(tmem + L::kO, ph + kk * 8, bh_, idesc_pv2, (tp > 0 || kk > 0) ? 1u : 0u);
+              mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
+            } else {
+              const uint64_t bl_ = bh_ + (uint64_t)((DVP * 128) >> 4);
+              mma_tf32_ts(tmem + L::kO, ph + kk * 8, bh_, idesc_pv, (tp > 0 || kk > 0) ? 1u : 0u);
+              mma_tf32_ts(tmem + L::kO, ph + kk * 8, bl_, idesc_pv, 1u);
+              mma_tf32_ts(tmem + L::kO, pl + kk * 8, bh_, idesc_pv, 1u);
+            }
           }
           mma_commit(&empty[sp]);
         }
@@ -369,11 +413,16 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
           for (int kk = 0; kk < DP / 8; ++kk) {
             // N = 128 rows: the chunk's 64 hi rows, then its 64 lo rows
             const uint64_t bk = kd + (uint64_t)(((kk >> 2) * (2 * kTile * 128) + (kk & 3) * 32) >> 4);
-            // K_hi rows, then the chunk's K_lo rows 64 rows (8 KB) further
-            const uint64_t bkl = bk + (uint64_t)((kTile * 128) >> 4);
-            mma_tf32_ts(dS, tmem + L::kQhi + kk * 8, bk, idesc_qk, kk > 0 ? 1u : 0u);
-            mma_tf32_ts(dS, tmem + L::kQhi + kk * 8, bkl, idesc_qk, 1u);
-            mma_tf32_ts(dS, tmem + L::kQlo + kk * 8, bk, idesc_qk, 1u);
+            if (L::kStackK) {
+              mma_tf32_ts(dS, tmem + L::kQhi + kk * 8, bk, idesc_qk2, kk > 0 ? 1u : 0u);
+              mma_tf32_ts(dS, tmem + L::kQlo + kk * 8, bk, idesc_qk, 1u);
+            } else {
+              // K_lo rows 64 rows (8 KB) after the chunk's K_hi rows
+              const uint64_t bkl = bk + (uint64_t)((kTile * 128) >> 4);
+              mma_tf32_ts(dS, tmem + L::kQhi + kk * 8, bk, idesc_qk, kk > 0 ? 1u : 0u);
+              mma_tf32_ts(dS, tmem + L::kQhi + kk * 8, bkl, idesc_qk, 1u);
+              mma_tf32_ts(dS, tmem + L::kQlo + kk * 8, bk, idesc_qk, 1u);
+            }
           }
           mma_commit(&sfull[b]);
         }
@@ -403,23 +452,20 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
     const int64_t i = q0 + row;
     const bool valid = i < p.n;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
-    // scaled query, split hi/lo, into TMEM (16-column pieces, piece u written by
-    // column group u % 4)
+    // scaled query, split hi/lo, into TMEM (16-column pieces: column group cgp
+    // writes piece cgp, loaded into qv at the start)
     {
-      const float* qr = p.q + (h * p.n + (valid ? i : 0)) * p.d;
-#pragma unroll
-      for (int u = 0; u < DP / 16; ++u) {
-        if (u % kQW != cgp) continue;
+      static_assert(DP / 16 <= kQW, "one query piece per column group");
+      if (cgp < DP / 16) {
         uint32_t hi[16], lo[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const int a = u * 16 + j;
-          const float x = (valid && a < p.d) ? __ldg(qr + a) * p.scale : 0.0f;
+          const float x = qv[j] * p.scale;
           hi[j] = to_tf32(x);
           lo[j] = __float_as_uint(x - __uint_as_float(hi[j]));
         }
-        tmem_st16(lane_addr + L::kQhi + u * 16, hi);
-        tmem_st16(lane_addr + L::kQlo + u * 16, lo);
+        tmem_st16(lane_addr + L::kQhi + cgp * 16, hi);
+        tmem_st16(lane_addr + L::kQlo + cgp * 16, lo);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -443,7 +489,14 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
       const int64_t row0 = rep ? (int64_t)t * kTile : kb0 + (int64_t)(t - n_rep) * kTile;
       const int64_t col0 = row0 + cgp * kCW;
       float sv[kCW];
-      {
+      if (L::kStackK) {
+        float sl[kCW];
+        tmem_ld16(tS, sv);
+        tmem_ld16(tS + kTile, sl);   // the Q_hi K_lo^T half
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < kCW; ++j) sv[j] += sl[j];
+      } else {
         tmem_ld16(tS, sv);
         tmem_wait_ld();
       }
@@ -504,7 +557,15 @@ residual_tc_kernel(const __grid_constant__ CUtensorMap tm_rkh, const __grid_cons
         if (u % kQW != cgp) continue;
         float ov[16];
         tmem_ld16(lane_addr + L::kO + u * 16, ov);
-        tmem_wait_ld();
+        if (L::kStackV) {
+          float o2[16];   // the P_hi V_lo half
+          tmem_ld16(lane_addr + L::kO + DVP + u * 16, o2);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) ov[j] += o2[j];
+        } else {
+          tmem_wait_ld();
+        }
 #pragma unroll
         for (int j = 0; j < 16; ++j) os[row * OS + u * 16 + j] = ov[j];
       }
