@@ -39,11 +39,14 @@
 //        the dv hi rows, then the dv lo rows) + P_lo V_hi into its first dv
 //        columns; O = O'[0, dv) + O'[dv, 2 dv), added in the epilogue
 //        (for dv > 64, where O' would not fit in TMEM, three MMAs of N = dv)
-// The tensor time is that of three MMAs of N = 64, but the MMA warp issues a
-// third fewer instructions: issuing was the limit of the three-MMA form
-// (~40 cycles per tcgen05.mma from a warp that shares its scheduler with four
-// query-row warps, ~1900 issue cycles per 64-key tile against 1536 of tensor
-// work, measured with clock64 stamps).
+// The tensor time is that of three MMAs of N = 64, and the MMA warp issues a
+// third fewer instructions (it shares its scheduler with four query-row
+// warps).  Measured with clock64 stamps in every CTA at config 3: the issuing
+// of a tile's products took ~1900 cycles in the three-MMA form and ~1800 in
+// this one, against 1536 of tensor work -- the issuing thread waits on a full
+// tensor pipe queue -- and the main loop per 64-key tile went from ~2620 to
+// ~2560 cycles; the rest is waiting for the K/V ring (~290 per tile) and for
+// P (~160-260).
 #include <math.h>
 
 #include "sa_common.cuh"
