@@ -115,6 +115,31 @@ flash_tc_kernel(const __grid_constant__ CUtensorMap tm_kh, const __grid_constant
   const int64_t q_last = min(q0 + kRowsQ, p.n) - 1;
   const int T = (int)((q_last + kTile) / kTile);  // key tiles 0 .. q_last
 
+  // Query-row threads start loading their 32-column chunk of the query row now,
+  // so that the loads' latency overlaps the set-up below: 16-byte loads when
+  // the rows allow them (a warp's load then touches 32 rows once, not once per
+  // float).
+  float qv[32];
+  if (warp >= 2) {
+    const int cq = (warp - 2) >> 2;                // this warp's 32-column chunk (its half)
+    const int64_t iq = q0 + (warp & 3) * 32 + lane;
+    const bool vq = iq < p.n && cq < DP / 32;
+    const float* qr = p.q + (h * p.n + (vq ? iq : 0)) * p.d + cq * 32;
+    if (vq && (p.d & 3) == 0 && cq * 32 + 32 <= p.d && (reinterpret_cast<uintptr_t>(p.q) & 15) == 0) {
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 x = __ldg(reinterpret_cast<const float4*>(qr) + j4);
+        qv[4 * j4 + 0] = x.x;
+        qv[4 * j4 + 1] = x.y;
+        qv[4 * j4 + 2] = x.z;
+        qv[4 * j4 + 3] = x.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) qv[j] = (vq && cq * 32 + j < p.d) ? __ldg(qr + j) : 0.0f;
+    }
+  }
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -256,20 +281,18 @@ flash_tc_kernel(const __grid_constant__ CUtensorMap tm_kh, const __grid_constant
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     const float qscale = p.scale * 1.4426950408889634f;   // log2(e): scores in base 2
     {
-      const float* qr = p.q + (h * p.n + (valid ? i : 0)) * p.d;
-#pragma unroll
-      for (int cchunk = 0; cchunk < DP / 32; ++cchunk) {
-        if ((cchunk & 1) != half) continue;
+      // this half's 32-column chunk of the scaled query (loaded into qv at the start)
+      static_assert(DP / 32 <= 2, "one query chunk per half");
+      if (half < DP / 32) {
         uint32_t hi[32], lo[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const int a = cchunk * 32 + j;
-          const float x = (valid && a < p.d) ? __ldg(qr + a) * qscale : 0.0f;
+          const float x = qv[j] * qscale;
           hi[j] = to_tf32(x);
           lo[j] = __float_as_uint(x - __uint_as_float(hi[j]));
         }
-        tmem_st32(lane_addr + L::kQhi + cchunk * 32, hi);
-        tmem_st32(lane_addr + L::kQlo + cchunk * 32, lo);
+        tmem_st32(lane_addr + L::kQhi + half * 32, hi);
+        tmem_st32(lane_addr + L::kQlo + half * 32, lo);
       }
       tmem_wait_st();
       tc_fence_before();
