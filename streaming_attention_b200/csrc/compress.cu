@@ -39,7 +39,8 @@ compress_blocks_kernel(const float* __restrict__ k, const float* __restrict__ v,
                        int bs, int nc, int m, int pow2, int use_perm, const float* __restrict__ dirs,
                        const float* __restrict__ coins, const int32_t* __restrict__ perms,
                        int32_t* __restrict__ rep_idx, float* __restrict__ rep_k, float* __restrict__ rep_v,
-                       float* __restrict__ rep_w, const SplitOut sp, int64_t idx_offset, int* status) {
+                       float* __restrict__ rep_w, const SplitOut sp, int64_t idx_offset, int* status,
+                       int stage) {
   extern __shared__ unsigned char smem_raw[];
   unsigned long long* skey = reinterpret_cast<unsigned long long*>(smem_raw);
   int* sidx = reinterpret_cast<int*>(skey + pow2);
@@ -47,6 +48,7 @@ compress_blocks_kernel(const float* __restrict__ k, const float* __restrict__ v,
   float* selw = reinterpret_cast<float*>(sel + m);
   double* sdir = reinterpret_cast<double*>(
       reinterpret_cast<unsigned char*>(smem_raw) + (((size_t)pow2 * 12 + (size_t)m * 8 + 15) & ~(size_t)15));
+  float* skb = reinterpret_cast<float*>(sdir + d);   // (stage) the block's keys, row stride d + 1
 
   const int c = blockIdx.x;
   const int64_t h = blockIdx.y;
@@ -62,14 +64,35 @@ compress_blocks_kernel(const float* __restrict__ k, const float* __restrict__ v,
     }
   } else {
     for (int a = tid; a < d; a += blockDim.x) sdir[a] = (double)dirs[blk * d + a];
-    __syncthreads();
     const float* kb = k + (h * n + start) * d;
+    if (stage) {
+      // the block's keys into shared memory with 16-byte loads (d % 4 == 0, 16-byte
+      // aligned rows), rows d + 1 floats apart so that the per-thread row reads
+      // below fall on distinct banks; the sum order is unchanged
+      const int d4 = d >> 2;
+      const float4* src = reinterpret_cast<const float4*>(kb);
+      for (int e = tid; e < bs * d4; e += blockDim.x) {
+        const float4 x = __ldg(src + e);
+        const int r = e / d4, c = (e - r * d4) * 4;
+        float* dst = skb + r * (d + 1) + c;
+        dst[0] = x.x;
+        dst[1] = x.y;
+        dst[2] = x.z;
+        dst[3] = x.w;
+      }
+    }
+    __syncthreads();
     for (int t = tid; t < pow2; t += blockDim.x) {
       unsigned long long key = 0xFFFFFFFFFFFFFFFFull;  // padding sorts last
       if (t < bs) {
-        const float* row = kb + (int64_t)t * d;
         double acc = 0.0;
-        for (int a = 0; a < d; ++a) acc = fma((double)__ldg(row + a), sdir[a], acc);
+        if (stage) {
+          const float* row = skb + t * (d + 1);
+          for (int a = 0; a < d; ++a) acc = fma((double)row[a], sdir[a], acc);
+        } else {
+          const float* row = kb + (int64_t)t * d;
+          for (int a = 0; a < d; ++a) acc = fma((double)__ldg(row + a), sdir[a], acc);
+        }
         key = orderable(acc);
       }
       skey[t] = key;
@@ -221,14 +244,21 @@ int launch_compress(const float* k, const float* v, int64_t bh, int64_t n, int d
   int pow2 = 1;
   while (pow2 < bs) pow2 <<= 1;
   if (pow2 > 4096) return set_error(SA_ERR_UNSUPPORTED, "block_size > 4096 is not supported by the compressor");
-  const size_t smem = (((size_t)pow2 * 12 + (size_t)m * 8 + 15) & ~(size_t)15) + (size_t)d * 8;
+  // sorted_pair stages the block's keys in shared memory when they fit in 96 KB
+  // and rows allow 16-byte loads
+  const size_t key_tile = (size_t)bs * (size_t)(d + 1) * 4;
+  const int stage = (!use_perm && (d & 3) == 0 && (reinterpret_cast<uintptr_t>(k) & 15) == 0 &&
+                     key_tile <= 96 * 1024) ? 1 : 0;
+  const size_t smem = (((size_t)pow2 * 12 + (size_t)m * 8 + 15) & ~(size_t)15) + (size_t)d * 8 +
+                      (stage ? key_tile : 0);
   if (smem > 48 * 1024) {
     cudaFuncSetAttribute(compress_blocks_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   }
   dim3 grid((unsigned)nc, (unsigned)bh);
   compress_blocks_kernel<<<grid, kCompressThreads, smem, stream>>>(k, v, n, d, dv, bs, (int)nc, m, pow2,
                                                                    use_perm ? 1 : 0, dirs, coins, perms, rep_idx,
-                                                                   rep_k, rep_v, rep_w, sp, idx_offset, status);
+                                                                   rep_k, rep_v, rep_w, sp, idx_offset, status,
+                                                                   stage);
   return check_launch("compress_blocks_kernel");
 }
 
