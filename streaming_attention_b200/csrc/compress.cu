@@ -224,6 +224,54 @@ __global__ void split_transpose_kernel(const float* __restrict__ src, int64_t ro
   }
 }
 
+// The same transposing split in 64-row x 64-column tiles with 16-byte loads and
+// stores (cols % 4 == 0, rows_pad % 4 == 0, 16-byte aligned buffers): a warp
+// moves 512 contiguous bytes per access instead of 128, and a CTA four times
+// the data of the 32 x 32 form.
+__global__ void __launch_bounds__(256)
+split_transpose4_kernel(const float* __restrict__ src, int64_t rows, int cols, int cols_pad, int64_t rows_pad,
+                        float* __restrict__ hi, float* __restrict__ lo) {
+  __shared__ float tile[64][65];
+  const int64_t h = blockIdx.z;
+  const int64_t r0 = (int64_t)blockIdx.x * 64;
+  const int c0 = blockIdx.y * 64;
+  const int tid = threadIdx.x;
+  const float* sh = src + h * rows * cols;
+  // 64 rows x 16 float4 columns in; a column group c of 4 lies wholly inside
+  // or outside the row (cols % 4 == 0)
+  for (int e = tid; e < 64 * 16; e += 256) {
+    const int r = e >> 4, q = e & 15;
+    const int64_t row = r0 + r;
+    const int col = c0 + 4 * q;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (row < rows && col < cols) x = __ldg(reinterpret_cast<const float4*>(sh + row * cols + col));
+    tile[r][4 * q + 0] = x.x;
+    tile[r][4 * q + 1] = x.y;
+    tile[r][4 * q + 2] = x.z;
+    tile[r][4 * q + 3] = x.w;
+  }
+  __syncthreads();
+  float* hh = hi + h * cols_pad * rows_pad;
+  float* lh = lo + h * cols_pad * rows_pad;
+  // 64 output rows (value columns) x 16 float4 of keys out
+  for (int e = tid; e < 64 * 16; e += 256) {
+    const int cc = e >> 4, q = e & 15;
+    const int c = c0 + cc;
+    const int64_t rr = r0 + 4 * q;
+    if (c < cols_pad && rr < rows_pad) {
+      float x[4], xh[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        x[j] = tile[4 * q + j][cc];
+        xh[j] = __uint_as_float(tc_split_hi(x[j]));
+      }
+      *reinterpret_cast<float4*>(hh + (int64_t)c * rows_pad + rr) = make_float4(xh[0], xh[1], xh[2], xh[3]);
+      *reinterpret_cast<float4*>(lh + (int64_t)c * rows_pad + rr) =
+          make_float4(x[0] - xh[0], x[1] - xh[1], x[2] - xh[2], x[3] - xh[3]);
+    }
+  }
+}
+
 }  // namespace
 
 int launch_compress(const float* k, const float* v, int64_t bh, int64_t n, int d, int dv, int bs, int compressor,
@@ -267,6 +315,13 @@ int launch_split_t(const float* src, int64_t bh, int64_t rows, int cols, int col
   if (bh == 0 || rows_pad == 0) return SA_OK;
   if (bh > 65535 || (rows_pad + 31) / 32 > 2147483647LL)
     return set_error(SA_ERR_UNSUPPORTED, "too many sequences for one launch");
+  if (cols % 4 == 0 && rows_pad % 4 == 0 &&
+      ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo)) & 15) ==
+          0) {
+    dim3 grid4((unsigned)((rows_pad + 63) / 64), (unsigned)((cols_pad + 63) / 64), (unsigned)bh);
+    split_transpose4_kernel<<<grid4, 256, 0, stream>>>(src, rows, cols, cols_pad, rows_pad, hi, lo);
+    return check_launch("split_transpose4_kernel");
+  }
   dim3 grid((unsigned)((rows_pad + 31) / 32), (unsigned)((cols_pad + 31) / 32), (unsigned)bh);
   split_transpose_kernel<<<grid, dim3(32, 8), 0, stream>>>(src, rows, cols, cols_pad, rows_pad, hi, lo);
   return check_launch("split_transpose_kernel");
