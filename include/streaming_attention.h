@@ -128,9 +128,10 @@ int sa_fast_attention_workspace_size(int64_t bh, int64_t n, int d, int dv, int d
  * bytes, 256-byte aligned.  The call is ordered on `stream` like one kernel:
  * with a compressor and the tensor-core kernels, its moment scan runs on a
  * second stream of the device's highest priority (made, with two events, at
- * the first such call per host thread and caller stream) that forks from and
- * joins back into `stream`; under graph capture, or while stage events are
- * set, everything runs on `stream` itself. */
+ * the first such call per host thread and caller stream -- at most 16 per
+ * thread -- and kept until the process ends) that forks from and joins back
+ * into `stream`; under graph capture, while stage events are set, or with
+ * sa_set_moment_fork(0), everything runs on `stream` itself. */
 int sa_fast_attention(const float* q, const float* k, const float* v, int64_t bh, int64_t n, int d,
                       int dv, int degree, int block_size, float scale, int compressor,
                       const float* dirs, const float* coins, const int32_t* perms, float eps,
