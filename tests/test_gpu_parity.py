@@ -111,16 +111,19 @@ def test_deterministic(dev):
 
 def test_host_tensors_stream_through_the_gpu(dev, monkeypatch):
     """CPU inputs (as the reference takes them) run on the GPU in chunks and come
-    back on the host; every sequence is computed exactly as in one device call."""
+    back on the host; every sequence is computed exactly as in one device call
+    (the device call forks its moment scan onto a second stream, the chunks run
+    theirs in order: the same arithmetic either way)."""
     c = workloads.config(3, B=2, H=3, N=700)
     q, k, v = workloads.make_inputs(c, seed=5)
     kw = dict(degree=2, block_size=128, compressor="sorted_pair", seed=7)
     ref = sa.fast_article_causal_attention(q.to(dev), k.to(dev), v.to(dev), **kw).cpu()
-    # small chunks: 6 sequences in chunks of 2, 2, 1, 1 over the three device slots
+    # small chunks: 6 sequences in chunks of 2, 2, 1, 1 over the four device slots
     monkeypatch.setattr(fast, "_HOST_CHUNK_BYTES", 700 * (2 * 64 + 64) * 4 * 2)
     out = sa.fast_article_causal_attention(q.pin_memory(), k.pin_memory(), v.pin_memory(), **kw)
     assert out.device.type == "cpu"
     assert torch.equal(out, ref)
+    assert _lib.load().sa_moment_fork_enabled() == 1   # the host path gives the thread's setting back
     out2 = sa.fast_article_causal_attention(q, k, v, **kw)   # pageable inputs
     assert torch.equal(out2, ref)
     one = sa.fast_article_causal_attention(q[1, 2], k[1, 2], v[1, 2], seed=12)
